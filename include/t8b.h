@@ -1,0 +1,297 @@
+/*
+ * t8b.h - C ABI of the B200-native self-play hot path (simulator, policy, rollout).
+ *
+ * Every entry point is plain C: opaque handles, plain pointers and sizes, int status
+ * codes. Host pointers are read during the call only; device pointers are borrowed for
+ * the call and must address memory on the handle's device. A pointer returned by a
+ * `*_view` function stays valid until the next mutating call on the same handle.
+ *
+ * The C++ classes of the reference (t8::v2::GpuFullMoveSimulator,
+ * t8::v2::GpuActorCritic, t8::v2::GpuRolloutBuffer) map one method to one entry
+ * point here; each declaration names the reference member it replaces.
+ *
+ * Status codes: 0 ok; T8B_EINVAL (std::invalid_argument in the reference),
+ * T8B_ERANGE (std::out_of_range), T8B_ECUDA (std::runtime_error from a CUDA call),
+ * T8B_ENONFINITE (std::runtime_error on non-finite data), T8B_ESTATE
+ * (std::logic_error). t8b_last_error() gives the message of the calling thread's
+ * last failure.
+ */
+#ifndef T8B_H
+#define T8B_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    T8B_OK = 0,
+    T8B_EINVAL = 1,
+    T8B_ERANGE = 2,
+    T8B_ECUDA = 3,
+    T8B_ENONFINITE = 4,
+    T8B_ESTATE = 5,
+};
+
+enum { T8B_UNIVERSAL_COUNT = 22, T8B_MAX_CANDIDATES = 368, T8B_FEATURE_SIZE = 32, T8B_ROSTER_SLOTS = 42 };
+enum { T8B_STATE_FEATURES = 64, T8B_NOISE_FEATURES = 3, T8B_MAX_WINDOW_SPANS = 8, T8B_MAX_CONTACTS = 8 };
+enum { T8B_SCRIPTED_PROFILES = 331, T8B_SCENARIOS = 9, T8B_AGGRESSION_BUCKETS = 5 };
+
+/* ------------------------------------------------------------------ tables
+ * One fighter's compiled move tables, field for field the values of the reference's
+ * full_core::Move / Hit / Stance / Rules (include/t8_v2/full_combat_core.hpp:37-171)
+ * and FullEngineConfig (include/t8_v2/full_combat_engine.hpp:236-289). Enumerations
+ * are their uint8 values. The library repacks them into its own device layout. */
+
+typedef struct t8b_window {
+    int32_t count;
+    int32_t first[T8B_MAX_WINDOW_SPANS];
+    int32_t last[T8B_MAX_WINDOW_SPANS];
+} t8b_window_t;
+
+typedef struct t8b_hit {
+    uint8_t level;       /* FullHitLevel: High Mid Low SpecialMid SpecialLow Throw */
+    uint8_t throw_break; /* FullThrowBreak: None One Two OneTwo OneOrTwo */
+    uint16_t flags;      /* homing, ground hit, wall splat, wall break, floor break, balcony break,
+                            tornado, spike, unparryable, reversal break, has heat chip */
+    int32_t first_active_frame;
+    int32_t active_frames;
+    double damage, reach, tracking_left, tracking_right, chip_damage, heat_chip_damage;
+} t8b_hit_t;
+
+typedef struct t8b_move {
+    uint64_t flags; /* the 35 move flags of full_core::MoveFlag, same bit positions */
+    int32_t hit_offset, hit_count, total_frames, recovery, block_advantage, hit_advantage;
+    int32_t counter_hit_advantage, launch_air_frames, back_turned_hit_advantage;
+    int32_t heat_dash_block_advantage, heat_dash_hit_advantage, heat_cost_frames;
+    int32_t required_stance, result_stance, result_stance_on_hit, result_stance_on_block;
+    int32_t parry_outcomes[4];
+    int32_t heat_parry_outcome;
+    uint8_t hit_effect, counter_hit_effect, back_turned_hit_effect, heat_dash_hit_effect;
+    uint8_t required_posture, attack_throw, parry_levels, heat_parry_levels;
+    double travel, pushback_hit, pushback_block, reversal_damage, attack_throw_damage;
+    double recoverable_damage, rage_art_max_damage, self_damage, self_recoverable;
+    double restore_health_hit, restore_recoverable_hit, restore_recoverable_block;
+    double resource_gain_start, resource_gain_hit, resource_gain_airborne_hit, resource_gain_block;
+    double resource_gain_heat_activation, install_damage_bonus, install_chip_damage, install_reach;
+    /* high crush, low crush, power crush, armor, parry, reversal, invincible, airborne, heat parry */
+    t8b_window_t windows[9];
+} t8b_move_t;
+
+typedef struct t8b_stance {
+    uint8_t can_guard, has_max_frames, auto_parry, pad;
+    int32_t max_frames;
+    int32_t parry_outcomes[4];
+    int32_t pulse_interval_frames;
+    double pulse_recoverable, pulse_resource;
+} t8b_stance_t;
+
+typedef struct t8b_rules {
+    double resource_max;
+    double install_threshold;
+    uint8_t has_install_threshold, resource_persists, install_consumes, pad[5];
+} t8b_rules_t;
+
+typedef struct t8b_engine_config {
+    double half_width, body_radius, walk_speed, dash_distance;
+    int32_t dash_frames;
+    int32_t backdash_frames;
+    double backdash_distance, sidestep_distance;
+    int32_t sidestep_frames;
+    int32_t launch_air_frames;
+    double axis_realign_per_frame;
+    int32_t juggle_window_frames, juggle_window_decay, tornado_extra_frames, knockdown_frames;
+    int32_t wakeup_stand_frames, wakeup_roll_frames;
+    double wakeup_roll_distance;
+    int32_t tech_window_frames, tech_roll_frames, wall_splat_frames, crumple_frames, stage_break_air_frames;
+    int32_t pad0;
+    double wall_break_extension, combo_scale_step, combo_scale_floor, counter_hit_damage_scale;
+    int32_t throw_break_window, throw_break_recovery, parry_outcome_frames;
+    int32_t pad1;
+    double side_exposure_ratio, back_to_wall_distance;
+    int32_t ki_charge_frames;
+    int32_t pad2;
+    double ki_charge_damage_scale;
+    int32_t parry_stun_frames, reversal_recovery, heat_duration_frames, heat_dash_frames;
+    double heat_dash_distance, rage_health_fraction, rage_damage_scale, wall_combo_scale;
+    double recoverable_regain_hit, recoverable_regain_block, max_health;
+} t8b_engine_config_t;
+
+/* One roster character: FullMoveCharacter (include/t8_v2/full_move_roster.hpp:56-67) with
+ * its side-0 tables. candidate_features is [candidate_count, 32]. */
+typedef struct t8b_character {
+    const t8b_move_t* moves;
+    const t8b_hit_t* hits;
+    const t8b_stance_t* stances;
+    const int32_t* candidate_moves;
+    const float* candidate_features;
+    int32_t move_count, hit_count, stance_count, candidate_count;
+    int32_t roster_id;
+    int32_t pad;
+    t8b_rules_t rules;
+} t8b_character_t;
+
+/* ------------------------------------------------------------------ state
+ * full_core::State (include/t8_v2/full_combat_core.hpp:179-228) in a packed form: the
+ * fighter's bools are bits of `flags`, in this order. */
+enum {
+    T8B_F_HEAT = 1u << 0, T8B_F_HEAT_AVAILABLE = 1u << 1, T8B_F_RAGE = 1u << 2, T8B_F_RAGE_AVAILABLE = 1u << 3,
+    T8B_F_THROW_BREAK_ATTEMPTED = 1u << 4, T8B_F_INSTALLED = 1u << 5, T8B_F_MOVE_HIT = 1u << 6,
+    T8B_F_MOVE_BLOCKED = 1u << 7, T8B_F_RESOURCE_GAINED = 1u << 8, T8B_F_BACK_TURNED = 1u << 9,
+    T8B_F_MOVE_IN_HEAT = 1u << 10, T8B_F_KI_CHARGE_BOOST = 1u << 11, T8B_F_MOVE_BOOSTED = 1u << 12,
+    T8B_F_IN_BLOCKSTUN = 1u << 13, T8B_F_TORNADO_USED = 1u << 14, T8B_F_WALL_SPLAT_USED = 1u << 15,
+    T8B_F_WALL_SCALED = 1u << 16, T8B_F_TECHABLE = 1u << 17, T8B_F_CRUMPLED = 1u << 18,
+};
+enum {
+    T8B_S_LEFT_WALL_BREAKABLE = 1u << 0, T8B_S_RIGHT_WALL_BREAKABLE = 1u << 1, T8B_S_LEFT_BALCONY = 1u << 2,
+    T8B_S_RIGHT_BALCONY = 1u << 3, T8B_S_FLOOR_BREAKABLE = 1u << 4,
+};
+
+typedef struct t8b_fighter {
+    double health, recoverable_health, x, axis, resource;
+    uint8_t posture, universal;
+    int8_t heat_dash_from;
+    uint8_t pad;
+    uint32_t flags;
+    int32_t stance, heat_frames, throw_break_frames, pending_throw_hit, pending_throw_elapsed;
+    int32_t move, action_frame;
+    uint32_t hits_landed;
+    int32_t stance_frames, ki_charge_frames, stun, posture_frames, grounded_elapsed, combo_hits;
+} t8b_fighter_t; /* 104 bytes */
+
+typedef struct t8b_state {
+    t8b_fighter_t fighters[2];
+    double left_wall, right_wall;
+    uint32_t stage_flags;
+    int32_t stage_level;
+    int32_t frame, winner;
+} t8b_state_t; /* 240 bytes */
+
+typedef struct t8b_input {
+    int32_t move;      /* -1: the universal action */
+    int32_t universal; /* FullUniversal */
+} t8b_input_t;
+
+typedef struct t8b_contact {
+    int32_t attacker, hit_index, contact, pad;
+    double damage;
+} t8b_contact_t;
+
+typedef struct t8b_events {
+    int32_t contact_count, transition_count;
+    t8b_contact_t contacts[T8B_MAX_CONTACTS];
+    uint8_t transitions[4];
+    uint8_t heat_activated[2], rage_activated[2];
+} t8b_events_t;
+
+/* full_core::EnvConfig (include/t8_v2/full_move_contract.hpp:737-773). */
+typedef struct t8b_env_config {
+    int32_t max_round_frames, hold_frames, max_frames_per_decision;
+    float damage_reward, win_reward, draw_penalty, throw_break_penalty, time_penalty_per_second;
+    float damage_dealt_weight, damage_taken_weight, distance_penalty_per_second;
+    int32_t perception_delay;
+    uint8_t memory, live_noise, screen_view, pad;
+    float noise_position_max, noise_flip_max;
+    int32_t latency_min, latency_max;
+    int32_t pad2;
+    double start_center_range, start_distance_min, start_distance_max;
+} t8b_env_config_t;
+
+/* full_core::NoiseLevels (include/t8_v2/full_move_contract.hpp:787-792). */
+typedef struct t8b_noise_levels {
+    float position_sigma, flip_rate;
+    int32_t latency;
+    uint32_t key;
+} t8b_noise_levels_t;
+
+/* Fills defaults equal to the reference's default member initialisers. */
+void t8b_engine_config_default(t8b_engine_config_t* out);
+void t8b_env_config_default(t8b_env_config_t* out);
+
+const char* t8b_last_error(void);
+int t8b_device_count(int* out);
+
+/* ------------------------------------------------------------------ simulator
+ * class GpuFullMoveSimulator (include/t8_v2/full_move_gpu.hpp:42-141). */
+typedef struct t8b_sim t8b_sim;
+
+/* GpuFullMoveSimulator(roster, environments, config)  full_move_gpu.hpp:44-45 */
+int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_engine_config_t* engine,
+                   size_t environments, const t8b_env_config_t* config, t8b_sim** out);
+int t8b_sim_destroy(t8b_sim* sim);
+/* Stream for every following call (the reference always uses the default stream). */
+int t8b_sim_set_stream(t8b_sim* sim, void* stream);
+size_t t8b_sim_environment_count(const t8b_sim* sim);            /* full_move_gpu.hpp:52 */
+int t8b_sim_observation_size(const t8b_sim* sim);                /* full_move_gpu.hpp:58 */
+/* set_matchups  full_move_gpu.hpp:61 (host arrays [environments]) */
+int t8b_sim_set_matchups(t8b_sim* sim, const int32_t* p1_characters, const int32_t* p2_characters);
+/* reset_engine / step_engine / download_states / download_events / upload_states /
+ * download_legal_mask  full_move_gpu.hpp:64-74 (host arrays) */
+int t8b_sim_reset_engine(t8b_sim* sim, const double* p1_x, const double* p2_x);
+int t8b_sim_step_engine(t8b_sim* sim, const t8b_input_t* inputs, const uint8_t* new_round, const double* p1_x,
+                        const double* p2_x);
+int t8b_sim_download_states(t8b_sim* sim, t8b_state_t* out);
+int t8b_sim_download_events(t8b_sim* sim, t8b_events_t* out);
+int t8b_sim_upload_states(t8b_sim* sim, const t8b_state_t* states);
+int t8b_sim_download_legal_mask(t8b_sim* sim, int player, uint8_t* out);
+/* set_learner_sides / set_pending_opponents / set_pending_learners  full_move_gpu.hpp:79-86.
+ * aggression and scenarios may be NULL (0.5 and neutral, as the reference). */
+int t8b_sim_set_learner_sides(t8b_sim* sim, const uint8_t* learner_is_p1);
+int t8b_sim_set_pending_opponents(t8b_sim* sim, const int32_t* characters, const float* aggression,
+                                  const int32_t* scenarios);
+int t8b_sim_set_pending_learners(t8b_sim* sim, const int32_t* characters);
+/* reset_all / reset_done / step  full_move_gpu.hpp:87-93. learner/opponent candidates are
+ * device int64 [environments]; opponent NULL = scripted opponent. */
+int t8b_sim_reset_all(t8b_sim* sim, uint64_t seed, uint64_t counter);
+int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter);
+int t8b_sim_step(t8b_sim* sim, const int64_t* learner_candidates, const int64_t* opponent_candidates, uint64_t seed,
+                 uint64_t counter);
+/* Device views  full_move_gpu.hpp:96-112. Masks are uint8 [env][368] as in the
+ * reference; t8b_sim_learner_mask_bits gives the packed form the library keeps
+ * (12 uint32 words per environment, bit c of word c/32 = candidate c). */
+const float* t8b_sim_learner_observations(const t8b_sim* sim);
+const float* t8b_sim_opponent_observations(const t8b_sim* sim);
+const uint8_t* t8b_sim_learner_masks(t8b_sim* sim);
+const uint8_t* t8b_sim_opponent_masks(t8b_sim* sim);
+const uint32_t* t8b_sim_learner_mask_bits(const t8b_sim* sim);
+const uint32_t* t8b_sim_opponent_mask_bits(const t8b_sim* sim);
+const float* t8b_sim_rewards(const t8b_sim* sim);
+const float* t8b_sim_sparse_rewards(const t8b_sim* sim);
+const uint8_t* t8b_sim_terminated(const t8b_sim* sim);
+const uint8_t* t8b_sim_truncated(const t8b_sim* sim);
+const int8_t* t8b_sim_outcomes(const t8b_sim* sim);
+const int32_t* t8b_sim_learner_feature_tables(const t8b_sim* sim);
+const int32_t* t8b_sim_opponent_feature_tables(const t8b_sim* sim);
+/* download_noise_levels  full_move_gpu.hpp:110 */
+int t8b_sim_download_noise_levels(t8b_sim* sim, t8b_noise_levels_t* out);
+/* frames_simulated  full_move_gpu.hpp:120 */
+int t8b_sim_frames_simulated(t8b_sim* sim, uint64_t* out);
+/* download_and_clear_tally and the three tallies cleared with it  full_move_gpu.hpp:124-131.
+ * tally: [roster][5][2][3]; scenario: [9][3]; learner: [roster][3]; bot: [331][3]. */
+int t8b_sim_download_and_clear_tally(t8b_sim* sim, uint32_t* tally, uint32_t* scenario_tally,
+                                     uint32_t* learner_tally, uint32_t* bot_tally);
+/* snapshot / restore  full_move_gpu.hpp:134-136 (host arrays [environments]). */
+int t8b_sim_snapshot(t8b_sim* sim, t8b_state_t* states, int32_t* p1, int32_t* p2, uint8_t* learner_is_p1,
+                     float* aggression, int32_t* pending_opponents, float* pending_aggression, uint8_t* terminated,
+                     int32_t* scenarios, int32_t* pending_scenarios, int32_t* pending_learners);
+int t8b_sim_restore(t8b_sim* sim, const t8b_state_t* states, const int32_t* p1, const int32_t* p2,
+                    const uint8_t* learner_is_p1, const float* aggression, const int32_t* pending_opponents,
+                    const float* pending_aggression, const uint8_t* terminated, const int32_t* scenarios,
+                    const int32_t* pending_scenarios, const int32_t* pending_learners);
+int t8b_sim_synchronize(t8b_sim* sim);
+
+/* Engine-parity workload (no reference counterpart: the reference's tests drive fights
+ * from the host one frame at a time, tests/full_combat_random_play.hpp:181-201). Every
+ * fight plays `frames` frames; whenever a fighter has a decision it picks a uniformly
+ * random legal candidate with a PCG32 stream (seed, stream = fight index); a finished
+ * round restarts with next_round at the fight's start positions. hashes[fight*frames+f]
+ * is the FNV-1a hash of the packed state after frame f. All pointers are device. */
+int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32_t* p2, const double* p1_x,
+                        const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* T8B_H */
