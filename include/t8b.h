@@ -288,6 +288,12 @@ int t8b_sim_synchronize(t8b_sim* sim);
  * random legal candidate with a PCG32 stream (seed, stream = fight index); a finished
  * round restarts with next_round at the fight's start positions. hashes[fight*frames+f]
  * is the FNV-1a hash of the packed state after frame f. All pointers are device. */
+/* Test hook for the tcgen05 GEMM (no reference counterpart): c[m][n] = sum_k a . b^T in fp32,
+ * a bf16 [m][k] (or [k][m] when a_mn_major), b bf16 [n][k] (or [k][n]); bn is the tile width
+ * (64, 192 or 256) and splits the split-K factor. All pointers are device. */
+int t8b_debug_gemm(const void* a, int a_mn_major, const void* b, int b_mn_major, float* c, int m, int n, int k,
+                   int bn, int splits, void* stream);
+
 int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32_t* p2, const double* p1_x,
                         const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done);
 
