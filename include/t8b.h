@@ -297,6 +297,149 @@ int t8b_debug_gemm(const void* a, int a_mn_major, const void* b, int b_mn_major,
 int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32_t* p2, const double* p1_x,
                         const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done);
 
+/* ------------------------------------------------------------------ policy and PPO
+ * class GpuActorCritic (include/t8_v2/ppo.hpp:112-193). Every matrix product runs bf16 x bf16
+ * with fp32 accumulation on the tensor cores whatever matmul_precision asks (the reference's
+ * fp32 | tf32 | bf16 choice; storage, accumulation and the optimizer stay fp32 as there). */
+typedef struct t8b_actor_config { /* ActorCriticConfig (include/t8_v2/ppo.hpp:15-46) */
+    int32_t observation_size, action_count, hidden_size, action_feature_size, universal_action_count;
+    int32_t shared_layers, head_layers;
+    uint8_t observation_normalization, orthogonal_initialization, pad[2];
+    float observation_clip, observation_epsilon;
+    int32_t matmul_precision; /* 0 fp32, 1 tf32, 2 bf16 (recorded; products run bf16) */
+} t8b_actor_config_t;
+
+typedef struct t8b_ppo_config { /* PpoUpdateConfig (include/t8_v2/ppo.hpp:60-73) */
+    int32_t epochs, pad;
+    uint64_t minibatch_size;
+    float learning_rate, clip_range, value_clip_range, target_kl, value_coefficient, entropy_coefficient;
+    float max_gradient_norm, adam_beta1, adam_beta2, adam_epsilon;
+} t8b_ppo_config_t;
+
+typedef struct t8b_ppo_metrics { /* PpoUpdateMetrics (include/t8_v2/ppo.hpp:75-95) */
+    float policy_loss, value_loss, entropy, approximate_kl, clip_fraction, gradient_norm;
+    float decision_fraction, decision_entropy, rollout_decision_entropy, pad;
+    uint64_t minibatches;
+    int32_t epochs_completed, early_stopped;
+} t8b_ppo_metrics_t;
+
+typedef struct t8b_policy_output { /* GpuPolicyOutputView (include/t8_v2/ppo.hpp:48-56) */
+    const float* logits; /* [n][368] candidate scores, when requested */
+    const int64_t* actions;
+    const float* log_probabilities;
+    const float* values;
+    const float* entropies;
+    size_t environment_count;
+} t8b_policy_output_t;
+
+typedef struct t8b_rollout_view { /* GpuRolloutView (include/t8_v2/ppo.hpp:195-212) */
+    const float* observations;       /* [step][env][observation] */
+    const uint8_t* action_masks;     /* [step][env][368] */
+    const int64_t* actions;
+    const float* old_log_probabilities;
+    const float* old_values;
+    const float* rewards;
+    const uint8_t* terminated;
+    const uint8_t* truncated;
+    const float* next_values;
+    const float* advantages;
+    const float* returns;
+    size_t environment_count, horizon, sample_count;
+    const int32_t* feature_tables;
+    const float* entropies;
+    const uint32_t* action_mask_bits; /* [step][env][12] packed masks; used instead of action_masks when set */
+} t8b_rollout_view_t;
+
+/* Collectives for data parallelism (no reference counterpart: the reference is single-GPU).
+ * The library calls allreduce_sum_* on device buffers, on `stream`, wherever the ranks must
+ * agree: the minibatch gradient (then divided by world_size), the per-epoch KL, and the
+ * rollout statistics (advantage moments, return moments, observation moments). */
+typedef struct t8b_comm {
+    void (*allreduce_sum_f32)(float* data, size_t count, void* stream, void* user);
+    void (*allreduce_sum_f64)(double* data, size_t count, void* stream, void* user);
+    void* user;
+    int32_t world_size, rank;
+} t8b_comm_t;
+
+void t8b_actor_config_default(t8b_actor_config_t* out); /* full-move defaults of the trainer */
+void t8b_ppo_config_default(t8b_ppo_config_t* out);
+
+typedef struct t8b_policy t8b_policy;
+/* GpuActorCritic(capacity, config, initialization_seed)  ppo.hpp:114-117 */
+int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_t initialization_seed, t8b_policy** out);
+int t8b_policy_destroy(t8b_policy* policy);
+size_t t8b_policy_capacity(const t8b_policy* policy);        /* ppo.hpp:125 */
+size_t t8b_policy_parameter_count(const t8b_policy* policy); /* ppo.hpp:126 */
+int t8b_policy_action_feature_tables(const t8b_policy* policy);
+/* set_action_feature_tables  ppo.hpp:137 (host features [tables][368][32]) */
+int t8b_policy_set_action_feature_tables(t8b_policy* policy, const float* features, int tables, void* stream);
+/* forward  ppo.hpp:146-154. Device inputs; masks uint8 [n][368] or mask_bits [n][12]. */
+int t8b_policy_forward(t8b_policy* policy, const float* observations, const uint8_t* masks, const uint32_t* mask_bits,
+                       size_t environment_count, uint64_t sampling_seed, uint64_t sampling_step, int deterministic,
+                       void* stream, const int32_t* feature_tables, int want_logits, t8b_policy_output_t* out);
+/* update_ppo  ppo.hpp:156-160 */
+int t8b_policy_update_ppo(t8b_policy* policy, const t8b_rollout_view_t* rollout, const t8b_ppo_config_t* config,
+                          uint64_t shuffle_seed, void* stream, t8b_ppo_metrics_t* metrics);
+/* Starts computing update_ppo's host permutations in the background (no reference counterpart;
+ * the same std::shuffle permutations, ready when the update starts). */
+int t8b_policy_prepare_shuffle(t8b_policy* policy, size_t sample_count, int epochs, uint64_t shuffle_seed);
+int t8b_policy_set_comm(t8b_policy* policy, const t8b_comm_t* comm);
+/* Parameters, gradients and Adam state in the canonical order w1, b1, ..., w_out, b_out
+ * (the checkpoint payload of src/ppo.cu:1780-1845). */
+int t8b_policy_get_parameters(t8b_policy* policy, float* host, size_t count);
+int t8b_policy_set_parameters(t8b_policy* policy, const float* host, size_t count);
+int t8b_policy_get_gradients(t8b_policy* policy, float* host, size_t count);
+int t8b_policy_get_optimizer_state(t8b_policy* policy, float* first_moment, float* second_moment, uint64_t* step);
+int t8b_policy_set_optimizer_state(t8b_policy* policy, const float* first_moment, const float* second_moment,
+                                   uint64_t step);
+/* observation_count / download_observation_statistics  ppo.hpp:174-177 */
+int t8b_policy_get_observation_statistics(t8b_policy* policy, float* mean, float* variance, uint64_t* count);
+int t8b_policy_set_observation_statistics(t8b_policy* policy, const float* mean, const float* variance, uint64_t count);
+/* Test aid: the last forward's network outputs [n][feature_size + 1] (query, value). */
+int t8b_policy_download_outputs(t8b_policy* policy, float* host, size_t n);
+/* Test aid: an intermediate of the last forward/backward as fp32 rows (which: 0 layer-1 input,
+ * 1 hidden activation, 2 its pre-activation gradient, 3 output-layer gradient). */
+int t8b_policy_download_activation(t8b_policy* policy, int which, int layer, float* host, size_t n);
+int t8b_policy_synchronize(t8b_policy* policy, void* stream);
+
+/* debug_ppo_objective_gradient (include/t8_v2/ppo.hpp:100-108), batched: d(objective)/d(logits,
+ * value) of the clipped PPO objective for raw [n][k + 1] outputs. Device pointers. metric_sums
+ * (8 doubles: policy loss, value loss, entropy, KL, clip fraction, -, decisions, decision
+ * entropy) may be NULL. */
+int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const int64_t* actions,
+                            const float* old_log_probabilities, const float* old_values, const float* advantages,
+                            const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
+                            float* gradients, double* metric_sums, void* stream);
+
+/* ------------------------------------------------------------------ rollout buffer
+ * class GpuRolloutBuffer (include/t8_v2/ppo.hpp:223-291). */
+typedef struct t8b_rollout t8b_rollout;
+int t8b_rollout_create(size_t environments, size_t horizon, const t8b_actor_config_t* config, t8b_rollout** out);
+int t8b_rollout_destroy(t8b_rollout* rollout);
+int t8b_rollout_device_view(const t8b_rollout* rollout, t8b_rollout_view_t* out); /* ppo.hpp:239 */
+/* record_policy_device  ppo.hpp:241-250 (uint8 masks), or packed masks with mask_bits. */
+int t8b_rollout_record_policy_device(t8b_rollout* rollout, size_t step, const float* observations, const uint8_t* masks,
+                                     const uint32_t* mask_bits, const int64_t* actions, const float* log_probabilities,
+                                     const float* values, void* stream, const int32_t* feature_tables,
+                                     const float* entropies);
+/* record_outcome_device  ppo.hpp:252-259 */
+int t8b_rollout_record_outcome_device(t8b_rollout* rollout, size_t step, const float* rewards, const uint8_t* terminated,
+                                      const uint8_t* truncated, const float* next_values, float reward_scale,
+                                      void* stream);
+/* compute_gae  ppo.hpp:261-265 */
+int t8b_rollout_compute_gae(t8b_rollout* rollout, float gamma, float gae_lambda, int normalize_advantages, void* stream);
+/* normalize_rewards  ppo.hpp:271 (returns the standard deviation used) */
+int t8b_rollout_normalize_rewards(t8b_rollout* rollout, float gamma, float clip, void* stream, float* std_out);
+/* mean_reward  ppo.hpp:274 */
+int t8b_rollout_mean_reward(t8b_rollout* rollout, void* stream, double* out);
+/* return_normalizer_state / restore  ppo.hpp:275-276; returns [environments] host floats */
+int t8b_rollout_return_normalizer_state(t8b_rollout* rollout, uint64_t* count, double* mean, double* variance,
+                                        float* discounted_returns);
+int t8b_rollout_restore_return_normalizer_state(t8b_rollout* rollout, uint64_t count, double mean, double variance,
+                                                const float* discounted_returns);
+int t8b_rollout_set_comm(t8b_rollout* rollout, const t8b_comm_t* comm);
+int t8b_rollout_synchronize(t8b_rollout* rollout, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

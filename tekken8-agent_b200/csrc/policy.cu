@@ -1,0 +1,940 @@
+// Actor-critic policy and PPO update: the GpuActorCritic contract (include/t8_v2/ppo.hpp:112-193,
+// src/ppo.cu) on tcgen05 GEMMs, with its C ABI (include/t8b.h, t8b_policy_*).
+//
+// Network: observation -> shared tanh layers (hidden_size) -> [query (feature_size), value];
+// candidate scores are query . F[table, candidate] / sqrt(feature_size) (the parametric head).
+// Master parameters, Adam moments and gradients are fp32 in the reference's canonical order
+// (w1, b1, ..., w_out, b_out). Every matrix product runs bf16 x bf16 -> fp32 on the tensor
+// cores; the Adam kernel refreshes the bf16 operand copies (row-major and transposed).
+//
+// Forward: k_prep (normalise, bf16) -> GEMM+tanh per hidden layer -> GEMM+bias (output) ->
+// k_sample (scores, masked softmax, sample). Update, per minibatch: k_prep gathers through the
+// shuffled permutation -> the same forward GEMMs -> k_loss (scores, clipped objective, entropy,
+// value loss, d/d(query, value)) -> backward GEMMs with the tanh derivative and bias column sums
+// in the epilogue -> weight-gradient GEMMs reading the row-major activations as MN-major
+// operands (samples as K, split-K) -> fixed-order reductions -> gradient norm -> Adam + casts.
+#include "gemm_host.cuh"
+#include "ppo_kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <numeric>
+#include <random>
+#include <thread>
+#include <vector>
+
+namespace t8b {
+
+using bf16 = __nv_bfloat16;
+constexpr int kOutPad = 64;  // output layer width on the tensor cores (query + value + zero padding)
+
+struct Comm {
+    t8b_comm_t hooks{};
+    bool active() const { return hooks.allreduce_sum_f32 != nullptr && hooks.world_size > 1; }
+};
+
+// The reference's weight initialisation (src/ppo.cu:1030-1061, 1083-1121): modified Gram-Schmidt
+// with one re-orthogonalisation pass on normal draws in double, or Xavier normal draws.
+std::vector<float> orthogonal(int rows, int cols, float gain, std::mt19937_64& random) {
+    const size_t tall = static_cast<size_t>(std::max(rows, cols));
+    const size_t narrow = static_cast<size_t>(std::min(rows, cols));
+    std::normal_distribution<double> normal(0.0, 1.0);
+    std::vector<double> basis(tall * narrow);
+    for (double& v : basis) v = normal(random);
+    for (size_t k = 0; k < narrow; ++k) {
+        double* cur = basis.data() + k * tall;
+        for (int pass = 0; pass < 2; ++pass) {
+            for (size_t j = 0; j < k; ++j) {
+                const double* prev = basis.data() + j * tall;
+                double dot = 0.0;
+                for (size_t i = 0; i < tall; ++i) dot += prev[i] * cur[i];
+                for (size_t i = 0; i < tall; ++i) cur[i] -= dot * prev[i];
+            }
+        }
+        double norm = 0.0;
+        for (size_t i = 0; i < tall; ++i) norm += cur[i] * cur[i];
+        norm = std::sqrt(norm);
+        for (size_t i = 0; i < tall; ++i) cur[i] /= norm;
+    }
+    std::vector<float> out(static_cast<size_t>(rows) * cols);
+    for (int r = 0; r < rows; ++r) {
+        for (int c = 0; c < cols; ++c) {
+            const double v = rows >= cols ? basis[static_cast<size_t>(c) * tall + r] : basis[static_cast<size_t>(r) * tall + c];
+            out[static_cast<size_t>(r) * cols + c] = gain * static_cast<float>(v);
+        }
+    }
+    return out;
+}
+
+std::vector<float> xavier(int rows, int cols, std::mt19937_64& random, float deviation_override) {
+    const float deviation = deviation_override > 0.0f ? deviation_override : std::sqrt(2.0f / static_cast<float>(rows + cols));
+    std::normal_distribution<float> normal(0.0f, deviation);
+    std::vector<float> out(static_cast<size_t>(rows) * cols);
+    for (float& v : out) v = normal(random);
+    return out;
+}
+
+}  // namespace t8b
+
+using namespace t8b;
+
+struct t8b_policy {
+    t8b_actor_config_t config{};
+    size_t capacity = 0;
+    int layers = 0;      // shared hidden layers
+    int hidden = 0;
+    int width = 0;       // observation floats
+    int padded = 0;      // layer-1 operand row (multiple of 64)
+    int outputs = 0;     // feature_size + 1
+    int feature_size = 0;
+    size_t param_count = 0;
+    std::vector<size_t> w_off, b_off;  // per layer, then the output layer last
+    Buffer<float> params, grads, m1, m2;
+    std::vector<Buffer<bf16>> w_bf, wt_bf;  // operand copies per layer (index layers = output)
+    // activations
+    Buffer<bf16> x;
+    std::vector<Buffer<bf16>> h, dz;
+    std::vector<Buffer<float>> colsum;
+    Buffer<float> out;   // [capacity][64]
+    Buffer<bf16> dout;   // [capacity][64]
+    Buffer<float> out_colsum;
+    Buffer<float> split_part;
+    // inference outputs
+    Buffer<float> logits, log_probs, values, entropies;
+    Buffer<int64_t> actions;
+    // minibatch side data
+    Buffer<uint32_t> mb_bits, perm;
+    Buffer<int32_t> mb_actions, mb_tables;
+    Buffer<float> mb_old_lp, mb_old_v, mb_adv, mb_ret;
+    Buffer<double> block_metrics, metrics, norm_partial, norm_sq, entropy_sums;
+    Buffer<float> sample_entropy;
+    Buffer<uint8_t> sample_decision;
+    Buffer<int> error, invalid;
+    Buffer<double> kl_pair;
+    // features
+    Buffer<float> features;
+    int tables = 0;
+    bool features_ready = false;
+    // observation normaliser
+    Buffer<float> obs_mean, obs_var, obs_istd;
+    Buffer<double> obs_chunks;
+    uint64_t obs_count = 0;
+    uint64_t optimizer_step = 0;
+    ppo::AdamSpec adam{};
+    Comm comm;
+    // prepared permutations
+    std::thread shuffler;
+    std::vector<std::vector<uint32_t>> prepared;
+    size_t prepared_samples = 0;
+    int prepared_epochs = 0;
+    uint64_t prepared_seed = 0;
+    bool prepared_valid = false;
+
+    ~t8b_policy() {
+        if (shuffler.joinable()) shuffler.join();
+    }
+    bool normalizing() const { return config.observation_normalization && obs_count > 0; }
+    int bn_hidden() const { return hidden % 256 == 0 ? 256 : 64; }
+
+    void refresh_operands(cudaStream_t stream) {
+        ppo::k_adam<<<blocks(param_count, 256), 256, 0, stream>>>(params.data(), grads.data(), m1.data(), m2.data(),
+                                                                  param_count, norm_sq.data(), 1.0f, 0.0f, 0.9f, 0.999f,
+                                                                  1e-5f, 1.0f, 1.0f, adam, 0);
+        check(cudaGetLastError(), "refresh operand copies");
+    }
+
+    template <int BN, class Epi>
+    void dense(const Operand& a, const Operand& b, Epi epi, cudaStream_t stream, int splits = 1) {
+        gemm<BN, false, false>(a, b, splits, error.data(), epi, stream);
+    }
+
+    // forward of the network on x[0..n) -> out [n][64]
+    void network(size_t n, cudaStream_t stream) {
+        const int m = static_cast<int>(n);
+        for (int l = 0; l < layers; ++l) {
+            const Operand a = l == 0 ? Operand{x.data(), m, padded, padded, false} : Operand{h[l - 1].data(), m, hidden, hidden, false};
+            const Operand b{w_bf[l].data(), hidden, a.k, a.k, false};
+            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data(), hidden, m};
+            if (bn_hidden() == 256) dense<256>(a, b, epi, stream); else dense<64>(a, b, epi, stream);
+        }
+        const Operand a{h[layers - 1].data(), m, hidden, hidden, false};
+        const Operand b{w_bf[layers].data(), kOutPad, hidden, hidden, false};
+        dense<64>(a, b, ppo::EpiBias{params.data() + b_off[layers], out.data(), kOutPad, m, outputs}, stream);
+    }
+
+    int splits_for(int tiles) const {
+        const int s = sm_count() / std::max(1, tiles);
+        return std::max(1, s);
+    }
+
+    // backward from dout [n][64] into grads (unclipped, averaged by the loss scaling)
+    void backward(size_t n, cudaStream_t stream) {
+        const int m = static_cast<int>(n);
+        const int tiles_rows = (m + tc::BM - 1) / tc::BM;
+        // output layer weight gradient: dW_out^T [hidden][64] = H_L^T . dO
+        {
+            const Operand a{h[layers - 1].data(), hidden, m, hidden, true};
+            const Operand b{dout.data(), kOutPad, m, kOutPad, true};
+            const int splits = splits_for(hidden / tc::BM);
+            gemm<64, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, kOutPad}, stream);
+            const int k_blocks = (m + tc::BK - 1) / tc::BK;
+            const int used = std::min(splits, k_blocks);
+            ppo::k_reduce_split<<<blocks(static_cast<size_t>(outputs) * hidden, 256), 256, 0, stream>>>(
+                split_part.data(), used, hidden, kOutPad, grads.data() + w_off[layers], outputs, hidden, 1);
+        }
+        // output layer input gradient through tanh of the top hidden layer
+        {
+            const Operand a{dout.data(), m, kOutPad, kOutPad, false};
+            const Operand b{wt_bf[layers].data(), hidden, kOutPad, kOutPad, false};
+            const ppo::EpiTanhGrad epi{h[layers - 1].data(), dz[layers - 1].data(), colsum[layers - 1].data(), hidden, m};
+            if (bn_hidden() == 256) dense<256>(a, b, epi, stream); else dense<64>(a, b, epi, stream);
+        }
+        for (int l = layers - 1; l >= 0; --l) {
+            column_sums(colsum[l].data(), tiles_rows * 4, hidden, hidden, grads.data() + b_off[l], stream);
+            // weight gradient dW_l [hidden][in] = dZ_l^T . A_{l-1}
+            const int in_rows = l == 0 ? padded : hidden;
+            const bf16* in = l == 0 ? x.data() : h[l - 1].data();
+            const Operand a{dz[l].data(), hidden, m, hidden, true};
+            const Operand b{in, in_rows, m, in_rows, true};
+            const int k_blocks = (m + tc::BK - 1) / tc::BK;
+            if (l == 0 && padded % 256 != 0) {
+                const int tiles = (hidden / tc::BM) * ((in_rows + 191) / 192);
+                const int splits = splits_for(tiles);
+                if (padded == 192) {
+                    gemm<192, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                } else {
+                    gemm<64, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                }
+                ppo::k_reduce_split<<<blocks(static_cast<size_t>(hidden) * width, 256), 256, 0, stream>>>(
+                    split_part.data(), std::min(splits, k_blocks), hidden, in_rows, grads.data() + w_off[0], hidden, width, 0);
+            } else {
+                const int tiles = (hidden / tc::BM) * (in_rows / 256);
+                const int splits = splits_for(tiles);
+                gemm<256, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                const int cols = l == 0 ? width : hidden;
+                ppo::k_reduce_split<<<blocks(static_cast<size_t>(hidden) * cols, 256), 256, 0, stream>>>(
+                    split_part.data(), std::min(splits, k_blocks), hidden, in_rows, grads.data() + w_off[l], hidden, cols, 0);
+            }
+            if (l > 0) {
+                // dZ_{l-1} = (dZ_l . W_l) * (1 - H_{l-1}^2)
+                const Operand da{dz[l].data(), m, hidden, hidden, false};
+                const Operand db{wt_bf[l].data(), hidden, hidden, hidden, false};
+                const ppo::EpiTanhGrad epi{h[l - 1].data(), dz[l - 1].data(), colsum[l - 1].data(), hidden, m};
+                if (bn_hidden() == 256) dense<256>(da, db, epi, stream); else dense<64>(da, db, epi, stream);
+            }
+        }
+        check(cudaGetLastError(), "backward");
+    }
+
+    Buffer<float> column_scratch;
+    // grad[c] = sum over rows of in[r][c], two fixed-order levels
+    void column_sums(const float* in, int rows, int ld, int cols, float* grad, cudaStream_t stream) {
+        const size_t need = static_cast<size_t>(ppo::kColumnChunks) * cols;
+        if (column_scratch.size() < need) column_scratch.allocate(std::max<size_t>(need, ppo::kColumnChunks * 1024));
+        dim3 grid((cols + 31) / 32, ppo::kColumnChunks);
+        ppo::k_column_partials<<<grid, dim3(32, 8), 0, stream>>>(in, rows, ld, cols, column_scratch.data());
+        ppo::k_reduce_columns<<<blocks(cols, 128), 128, 0, stream>>>(column_scratch.data(), ppo::kColumnChunks, cols, cols, grad);
+        check(cudaGetLastError(), "column sums");
+    }
+
+    void sync_error(cudaStream_t stream) {
+        int flag = 0;
+        error.download(&flag, 1, stream);
+        if (flag) raise(T8B_ECUDA, "a tensor-core GEMM stalled and was aborted");
+    }
+};
+
+namespace {
+
+template <typename Body>
+int with_policy(t8b_policy* p, Body&& body) {
+    return guarded([&] {
+        if (p == nullptr) raise(T8B_EINVAL, "null policy handle");
+        body(*p);
+    });
+}
+
+// The host permutations of update_ppo (src/ppo.cu:1570-1579): one std::shuffle per epoch with
+// a std::mt19937_64 seeded by the shuffle seed.
+std::vector<std::vector<uint32_t>> make_permutations(size_t count, int epochs, uint64_t seed) {
+    std::mt19937_64 random(seed);
+    std::vector<uint32_t> order(count);
+    std::iota(order.begin(), order.end(), 0u);
+    std::vector<std::vector<uint32_t>> out;
+    for (int e = 0; e < epochs; ++e) {
+        std::shuffle(order.begin(), order.end(), random);
+        out.push_back(order);
+    }
+    return out;
+}
+
+__global__ void k_validate(const float* obs, int width, const uint8_t* bytes, const uint32_t* bits,
+                           const int64_t* actions, const float* lp, const float* v, const float* adv, const float* ret,
+                           size_t n, int* invalid) {
+    const size_t s = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    bool finite = isfinite(lp[s]) && isfinite(v[s]) && isfinite(adv[s]) && isfinite(ret[s]);
+    for (int f = 0; f < width && finite; ++f) finite = isfinite(obs[s * width + f]);
+    bool any = false;
+    bool chosen = false;
+    const int64_t a = actions[s];
+    for (int w = 0; w < 12; ++w) {
+        uint32_t word;
+        if (bits) {
+            word = bits[s * 12 + w];
+        } else {
+            word = 0;
+            for (int b = 0; b < 32 && w * 32 + b < 368; ++b) word |= (bytes[s * 368 + w * 32 + b] != 0 ? 1u : 0u) << b;
+        }
+        any = any || word != 0;
+        if (a >= w * 32 && a < w * 32 + 32) chosen = (word >> (a - w * 32)) & 1u;
+    }
+    const bool valid = a >= 0 && a < 368 && ((any && chosen) || (!any && a == 0));
+    if (!finite || !valid) atomicExch(invalid, 1);
+}
+
+// decision_flags_kernel + deterministic_decision_entropy_kernel (src/ppo.cu:570-610), multi-block:
+// per-block fp64 (entropy sum, decision count) in index order, then a fixed-order total.
+__global__ void k_decision_partials(const float* entropy, const uint8_t* decision, const uint8_t* bytes,
+                                    const uint32_t* bits, size_t n, double* partial) {
+    __shared__ double se[256], sd[256];
+    double e = 0.0, d = 0.0;
+    for (size_t s = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; s < n;
+         s += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        bool choice;
+        if (decision) {
+            choice = decision[s] != 0;
+        } else {
+            int legal = 0;
+            for (int w = 0; w < 12 && legal < 2; ++w) {
+                if (bits) {
+                    legal += __popc(bits[s * 12 + w]);
+                } else {
+                    for (int b = 0; b < 32 && w * 32 + b < 368; ++b) legal += bytes[s * 368 + w * 32 + b] != 0;
+                }
+            }
+            choice = legal > 1;
+        }
+        if (choice) {
+            e += entropy[s];
+            d += 1.0;
+        }
+    }
+    se[threadIdx.x] = e;
+    sd[threadIdx.x] = d;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            se[threadIdx.x] += se[threadIdx.x + w];
+            sd[threadIdx.x] += sd[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        partial[2 * blockIdx.x] = se[0];
+        partial[2 * blockIdx.x + 1] = sd[0];
+    }
+}
+
+__global__ void k_decision_finish(const double* partial, int blocks, double* out) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double e = 0.0, d = 0.0;
+    for (int b = 0; b < blocks; ++b) {
+        e += partial[2 * b];
+        d += partial[2 * b + 1];
+    }
+    out[0] = e;
+    out[1] = d;
+}
+
+}  // namespace
+
+extern "C" {
+
+void t8b_actor_config_default(t8b_actor_config_t* c) {
+    std::memset(c, 0, sizeof *c);
+    c->observation_size = 151;
+    c->action_count = T8B_MAX_CANDIDATES;
+    c->hidden_size = 512;
+    c->action_feature_size = T8B_FEATURE_SIZE;
+    c->universal_action_count = T8B_UNIVERSAL_COUNT;
+    c->shared_layers = 2;
+    c->head_layers = 0;
+    c->observation_normalization = 1;
+    c->orthogonal_initialization = 1;
+    c->observation_clip = 10.0f;
+    c->observation_epsilon = 1e-8f;
+    c->matmul_precision = 2;
+}
+
+void t8b_ppo_config_default(t8b_ppo_config_t* c) {
+    std::memset(c, 0, sizeof *c);
+    c->epochs = 4;
+    c->minibatch_size = 4096;
+    c->learning_rate = 3e-4f;
+    c->clip_range = 0.2f;
+    c->value_clip_range = 0.2f;
+    c->target_kl = 0.02f;
+    c->value_coefficient = 0.5f;
+    c->entropy_coefficient = 0.01f;
+    c->max_gradient_norm = 0.5f;
+    c->adam_beta1 = 0.9f;
+    c->adam_beta2 = 0.999f;
+    c->adam_epsilon = 1e-5f;
+}
+
+int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_t seed, t8b_policy** out) {
+    return guarded([&] {
+        if (out == nullptr || config == nullptr) raise(T8B_EINVAL, "null argument");
+        *out = nullptr;
+        const t8b_actor_config_t& c = *config;
+        // validate_actor_config (src/ppo.cu:26-45), restricted to the parametric full-move head
+        if (capacity == 0 || capacity > (1ull << 31)) raise(T8B_EINVAL, "policy capacity must be positive and fit 32-bit rows");
+        if (c.observation_size <= 0 || c.action_count <= 1 || c.hidden_size <= 0) {
+            raise(T8B_EINVAL, "actor-critic dimensions must be positive and representable");
+        }
+        if (c.shared_layers < 1 || c.shared_layers > 8 || c.head_layers < 0 || c.head_layers > 6) {
+            raise(T8B_EINVAL, "actor-critic depth must be 1-8 shared layers and 0-6 head layers");
+        }
+        if (c.head_layers != 0) raise(T8B_EINVAL, "separate policy/value heads are not supported by this library");
+        if (c.action_feature_size != T8B_FEATURE_SIZE || c.action_count != T8B_MAX_CANDIDATES) {
+            raise(T8B_EINVAL, "this library implements the parametric full-move head (368 candidates x 32 features)");
+        }
+        if (c.hidden_size % 64 != 0 || c.hidden_size % tc::BM != 0) raise(T8B_EINVAL, "hidden_size must be a multiple of 128");
+        if (!std::isfinite(c.observation_clip) || c.observation_clip <= 0.0f || !std::isfinite(c.observation_epsilon) ||
+            c.observation_epsilon <= 0.0f) {
+            raise(T8B_EINVAL, "observation normalizer clip/epsilon must be finite and positive");
+        }
+        auto p = std::make_unique<t8b_policy>();
+        p->config = c;
+        p->capacity = capacity;
+        p->layers = c.shared_layers;
+        p->hidden = c.hidden_size;
+        p->width = c.observation_size;
+        p->padded = (c.observation_size + 63) / 64 * 64;
+        p->feature_size = c.action_feature_size;
+        p->outputs = c.action_feature_size + 1;
+        // canonical order: w1, b1, ..., w_out, b_out
+        size_t off = 0;
+        for (int l = 0; l < p->layers; ++l) {
+            const int in = l == 0 ? p->width : p->hidden;
+            p->w_off.push_back(off);
+            off += static_cast<size_t>(p->hidden) * in;
+            p->b_off.push_back(off);
+            off += p->hidden;
+        }
+        p->w_off.push_back(off);
+        off += static_cast<size_t>(p->outputs) * p->hidden;
+        p->b_off.push_back(off);
+        off += p->outputs;
+        p->param_count = off;
+        p->params.allocate(off);
+        p->grads.allocate(off);
+        p->m1.allocate(off);
+        p->m2.allocate(off);
+        // bf16 operand copies
+        for (int l = 0; l <= p->layers; ++l) {
+            Buffer<bf16> w, wt;
+            if (l < p->layers) {
+                const int in = l == 0 ? p->padded : p->hidden;
+                w.allocate(static_cast<size_t>(p->hidden) * in);
+                if (l > 0) wt.allocate(static_cast<size_t>(p->hidden) * p->hidden);
+            } else {
+                w.allocate(static_cast<size_t>(kOutPad) * p->hidden);
+                wt.allocate(static_cast<size_t>(p->hidden) * kOutPad);
+            }
+            p->w_bf.push_back(std::move(w));
+            p->wt_bf.push_back(std::move(wt));
+        }
+        int t = 0;
+        for (int l = 0; l <= p->layers; ++l) {
+            const bool top = l == p->layers;
+            const int rows = top ? p->outputs : p->hidden;
+            const int cols = l == 0 ? p->width : p->hidden;
+            ppo::TensorSpec w{p->w_off[l], rows, cols, p->w_bf[l].data(), l == 0 ? p->padded : p->hidden,
+                              p->wt_bf[l].size() ? p->wt_bf[l].data() : nullptr, top ? kOutPad : p->hidden};
+            ppo::TensorSpec b{p->b_off[l], 1, rows, nullptr, 0, nullptr, 0};
+            p->adam.t[t++] = w;
+            p->adam.t[t++] = b;
+        }
+        p->adam.count = t;
+        // activations
+        const size_t cap = capacity;
+        p->x.allocate(cap * p->padded);
+        const size_t row_tiles = (cap + tc::BM - 1) / tc::BM;
+        for (int l = 0; l < p->layers; ++l) {
+            p->h.emplace_back(cap * p->hidden);
+            p->dz.emplace_back(cap * p->hidden);
+            p->colsum.emplace_back(row_tiles * 4 * p->hidden);
+        }
+        p->out.allocate(cap * kOutPad);
+        p->dout.allocate(cap * kOutPad);
+        p->out_colsum.allocate(((cap + ppo::kWarps - 1) / ppo::kWarps) * kOutPad);
+        const size_t sms = static_cast<size_t>(sm_count());
+        const size_t part = std::max({sms * p->hidden * kOutPad, sms * static_cast<size_t>(p->hidden) * p->hidden,
+                                      sms * static_cast<size_t>(p->hidden) * p->padded});
+        p->split_part.allocate(part);
+        p->logits.allocate(cap * T8B_MAX_CANDIDATES);
+        p->log_probs.allocate(cap);
+        p->values.allocate(cap);
+        p->entropies.allocate(cap);
+        p->actions.allocate(cap);
+        p->mb_bits.allocate(cap * 12);
+        p->mb_actions.allocate(cap);
+        p->mb_tables.allocate(cap);
+        p->mb_old_lp.allocate(cap);
+        p->mb_old_v.allocate(cap);
+        p->mb_adv.allocate(cap);
+        p->mb_ret.allocate(cap);
+        p->block_metrics.allocate(((cap + ppo::kWarps - 1) / ppo::kWarps) * ppo::kMetrics);
+        p->metrics.allocate(ppo::kMetrics);
+        p->norm_partial.allocate(1024);
+        p->norm_sq.allocate(1);
+        p->entropy_sums.allocate(2 * 1024 + 2);
+        p->error.allocate(1);
+        p->invalid.allocate(1);
+        p->kl_pair.allocate(2);
+        p->obs_mean.allocate(p->width);
+        p->obs_var.allocate(p->width);
+        p->obs_istd.allocate(p->width);
+        const std::vector<float> zeros(p->width, 0.0f), ones(p->width, 1.0f);
+        p->obs_mean.upload(zeros.data(), p->width, nullptr);
+        p->obs_var.upload(ones.data(), p->width, nullptr);
+        ppo::k_refresh_istd<<<blocks(p->width, 128), 128>>>(p->obs_var.data(), p->obs_istd.data(), p->width,
+                                                           c.observation_epsilon);
+        // initial weights: hidden layers, then the output layer, from one mt19937_64(seed)
+        std::mt19937_64 random(seed);
+        std::vector<float> host(p->param_count, 0.0f);
+        for (int l = 0; l < p->layers; ++l) {
+            const int in = l == 0 ? p->width : p->hidden;
+            const auto w = c.orthogonal_initialization ? orthogonal(p->hidden, in, std::sqrt(2.0f), random)
+                                                       : xavier(p->hidden, in, random, 0.0f);
+            std::copy(w.begin(), w.end(), host.begin() + static_cast<std::ptrdiff_t>(p->w_off[l]));
+        }
+        if (c.orthogonal_initialization) {
+            auto w = orthogonal(p->outputs, p->hidden, 1.0f, random);
+            for (int r = 0; r + 1 < p->outputs; ++r) {
+                for (int col = 0; col < p->hidden; ++col) w[static_cast<size_t>(r) * p->hidden + col] *= 0.01f;
+            }
+            std::copy(w.begin(), w.end(), host.begin() + static_cast<std::ptrdiff_t>(p->w_off[p->layers]));
+        } else {
+            const auto w = xavier(p->outputs, p->hidden, random, 0.01f);
+            std::copy(w.begin(), w.end(), host.begin() + static_cast<std::ptrdiff_t>(p->w_off[p->layers]));
+        }
+        p->params.upload(host.data(), host.size(), nullptr);
+        p->refresh_operands(nullptr);
+        check(cudaStreamSynchronize(nullptr), "create policy");
+        *out = p.release();
+    });
+}
+
+int t8b_policy_destroy(t8b_policy* p) {
+    return guarded([&] {
+        if (p != nullptr) cudaDeviceSynchronize();
+        delete p;
+    });
+}
+
+size_t t8b_policy_capacity(const t8b_policy* p) { return p ? p->capacity : 0; }
+size_t t8b_policy_parameter_count(const t8b_policy* p) { return p ? p->param_count : 0; }
+int t8b_policy_action_feature_tables(const t8b_policy* p) { return p ? p->tables : 0; }
+
+int t8b_policy_set_action_feature_tables(t8b_policy* p, const float* features, int tables, void* stream) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (tables <= 0) raise(T8B_EINVAL, "at least one action feature table is required");
+        const size_t count = static_cast<size_t>(tables) * T8B_MAX_CANDIDATES * s.feature_size;
+        for (size_t i = 0; i < count; ++i) {
+            if (!std::isfinite(features[i])) raise(T8B_EINVAL, "parametric action feature tensor has non-finite values");
+        }
+        if (s.features.size() != count) s.features.allocate(count);
+        s.features.upload(features, count, static_cast<cudaStream_t>(stream));
+        check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "upload features");
+        s.tables = tables;
+        s.features_ready = true;
+    });
+}
+
+int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, const uint32_t* mask_bits, size_t n,
+                       uint64_t seed, uint64_t step, int deterministic, void* stream, const int32_t* tables,
+                       int want_logits, t8b_policy_output_t* out) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (obs == nullptr || (masks == nullptr && mask_bits == nullptr)) raise(T8B_EINVAL, "policy input pointers cannot be null");
+        if (n == 0 || n > s.capacity) raise(T8B_EINVAL, "environment_count exceeds policy capacity");
+        if (!s.features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        ppo::Prep prep{};
+        prep.obs = obs;
+        prep.width = s.width;
+        prep.padded = s.padded;
+        prep.mean = s.obs_mean.data();
+        prep.istd = s.obs_istd.data();
+        prep.clip = s.config.observation_clip;
+        prep.normalize = s.normalizing() ? 1 : 0;
+        prep.count = n;
+        prep.x = s.x.data();
+        ppo::k_prep<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(prep);
+        check(cudaGetLastError(), "prepare inputs");
+        s.network(n, st);
+        ppo::Sample smp{};
+        smp.out = s.out.data();
+        smp.ld = kOutPad;
+        smp.feature_size = s.feature_size;
+        smp.features = s.features.data();
+        smp.table_count = s.tables;
+        smp.tables = tables;
+        smp.bits = mask_bits;
+        smp.bytes = mask_bits ? nullptr : masks;
+        smp.count = n;
+        smp.seed = seed;
+        smp.step = step;
+        smp.deterministic = deterministic;
+        smp.logits = want_logits ? s.logits.data() : nullptr;
+        smp.actions = s.actions.data();
+        smp.log_probs = s.log_probs.data();
+        smp.values = s.values.data();
+        smp.entropies = s.entropies.data();
+        ppo::k_sample<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(smp);
+        check(cudaGetLastError(), "sample actions");
+        if (out) {
+            out->logits = want_logits ? s.logits.data() : nullptr;
+            out->actions = s.actions.data();
+            out->log_probabilities = s.log_probs.data();
+            out->values = s.values.data();
+            out->entropies = s.entropies.data();
+            out->environment_count = n;
+        }
+    });
+}
+
+int t8b_policy_prepare_shuffle(t8b_policy* p, size_t sample_count, int epochs, uint64_t shuffle_seed) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (s.shuffler.joinable()) s.shuffler.join();
+        s.prepared_valid = false;
+        s.prepared_samples = sample_count;
+        s.prepared_epochs = epochs;
+        s.prepared_seed = shuffle_seed;
+        s.shuffler = std::thread([&s, sample_count, epochs, shuffle_seed] {
+            s.prepared = make_permutations(sample_count, epochs, shuffle_seed);
+        });
+        s.prepared_valid = true;
+    });
+}
+
+int t8b_policy_set_comm(t8b_policy* p, const t8b_comm_t* comm) {
+    return with_policy(p, [&](t8b_policy& s) { s.comm.hooks = comm ? *comm : t8b_comm_t{}; });
+}
+
+int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t8b_ppo_config_t* cfg, uint64_t shuffle_seed,
+                          void* stream, t8b_ppo_metrics_t* metrics_out) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (view == nullptr || cfg == nullptr) raise(T8B_EINVAL, "null argument");
+        const t8b_rollout_view_t& r = *view;
+        if (r.sample_count == 0 || !r.observations || (!r.action_masks && !r.action_mask_bits) || !r.actions ||
+            !r.old_log_probabilities || !r.old_values || !r.advantages || !r.returns) {
+            raise(T8B_EINVAL, "rollout view is incomplete");
+        }
+        if (cfg->epochs <= 0 || cfg->minibatch_size == 0 || cfg->minibatch_size > s.capacity) {
+            raise(T8B_EINVAL, "PPO epochs/minibatch size are invalid for policy capacity");
+        }
+        const float coefficients[] = {cfg->learning_rate, cfg->clip_range, cfg->value_clip_range, cfg->target_kl,
+                                      cfg->value_coefficient, cfg->entropy_coefficient, cfg->max_gradient_norm,
+                                      cfg->adam_beta1, cfg->adam_beta2, cfg->adam_epsilon};
+        bool finite = true;
+        for (float v : coefficients) finite = finite && std::isfinite(v);
+        if (!finite || cfg->learning_rate <= 0.0f || cfg->clip_range < 0.0f || cfg->value_clip_range < 0.0f ||
+            cfg->target_kl < 0.0f || cfg->value_coefficient < 0.0f || cfg->entropy_coefficient < 0.0f ||
+            cfg->max_gradient_norm <= 0.0f || cfg->adam_beta1 < 0.0f || cfg->adam_beta1 >= 1.0f ||
+            cfg->adam_beta2 < 0.0f || cfg->adam_beta2 >= 1.0f || cfg->adam_epsilon <= 0.0f) {
+            raise(T8B_EINVAL, "PPO optimizer coefficients are invalid or non-finite");
+        }
+        if (!s.features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
+        if (r.sample_count > 0xffffffffull) raise(T8B_EINVAL, "rollout too large for 32-bit sample indices");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const size_t samples = r.sample_count;
+        // validate_rollout_kernel (src/ppo.cu:423-451, 1545-1559)
+        s.invalid.zero(st);
+        k_validate<<<blocks(samples, 256), 256, 0, st>>>(r.observations, s.width, r.action_masks, r.action_mask_bits,
+                                                         r.actions, r.old_log_probabilities, r.old_values, r.advantages,
+                                                         r.returns, samples, s.invalid.data());
+        check(cudaGetLastError(), "validate rollout");
+        int invalid = 0;
+        s.invalid.download(&invalid, 1, st);
+        if (invalid) raise(T8B_ENONFINITE, "PPO rollout contains a non-finite value or invalid action");
+        s.metrics.zero(st);
+        s.error.zero(st);
+        if (s.sample_entropy.size() < samples) {
+            s.sample_entropy.allocate(samples);
+            s.sample_decision.allocate(samples);
+        }
+        if (s.perm.size() < samples) s.perm.allocate(samples);
+        // permutations: prepared in the background when the caller announced them
+        std::vector<std::vector<uint32_t>> perms;
+        if (s.shuffler.joinable()) s.shuffler.join();
+        if (s.prepared_valid && s.prepared_samples == samples && s.prepared_seed == shuffle_seed &&
+            s.prepared_epochs >= cfg->epochs) {
+            perms = std::move(s.prepared);
+        } else {
+            perms = make_permutations(samples, cfg->epochs, shuffle_seed);
+        }
+        s.prepared_valid = false;
+        const size_t mb = cfg->minibatch_size;
+        size_t minibatches = 0;
+        int epochs_completed = 0;
+        bool early = false;
+        double previous_kl = 0.0;
+        const int norm_blocks = 256;
+        for (int epoch = 0; epoch < cfg->epochs; ++epoch) {
+            s.perm.upload(perms[static_cast<size_t>(epoch)].data(), samples, st);
+            for (size_t offset = 0; offset < samples; offset += mb) {
+                const size_t n = std::min(mb, samples - offset);
+                ++minibatches;
+                ppo::Prep prep{};
+                prep.obs = r.observations;
+                prep.width = s.width;
+                prep.padded = s.padded;
+                prep.mean = s.obs_mean.data();
+                prep.istd = s.obs_istd.data();
+                prep.clip = s.config.observation_clip;
+                prep.normalize = s.normalizing() ? 1 : 0;
+                prep.perm = s.perm.data();
+                prep.offset = offset;
+                prep.count = n;
+                prep.x = s.x.data();
+                prep.src_bits = r.action_mask_bits;
+                prep.src_bytes = r.action_mask_bits ? nullptr : r.action_masks;
+                prep.bits = s.mb_bits.data();
+                prep.src_actions = r.actions;
+                prep.actions = s.mb_actions.data();
+                prep.src_old_lp = r.old_log_probabilities;
+                prep.old_lp = s.mb_old_lp.data();
+                prep.src_old_v = r.old_values;
+                prep.old_v = s.mb_old_v.data();
+                prep.src_adv = r.advantages;
+                prep.adv = s.mb_adv.data();
+                prep.src_ret = r.returns;
+                prep.ret = s.mb_ret.data();
+                prep.src_tables = r.feature_tables;
+                prep.tables = s.mb_tables.data();
+                ppo::k_prep<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(prep);
+                check(cudaGetLastError(), "gather minibatch");
+                s.network(n, st);
+                ppo::Loss loss{};
+                loss.out = s.out.data();
+                loss.ld = kOutPad;
+                loss.feature_size = s.feature_size;
+                loss.features = s.features.data();
+                loss.table_count = s.tables;
+                loss.tables = s.mb_tables.data();
+                loss.bits = s.mb_bits.data();
+                loss.actions = s.mb_actions.data();
+                loss.old_lp = s.mb_old_lp.data();
+                loss.old_v = s.mb_old_v.data();
+                loss.adv = s.mb_adv.data();
+                loss.ret = s.mb_ret.data();
+                loss.count = n;
+                loss.inv_batch = 1.0f / static_cast<float>(n);
+                loss.clip = cfg->clip_range;
+                loss.value_clip = cfg->value_clip_range;
+                loss.value_coef = cfg->value_coefficient;
+                loss.entropy_coef = cfg->entropy_coefficient;
+                loss.dout = s.dout.data();
+                loss.ld_grad = kOutPad;
+                loss.block_metrics = s.block_metrics.data();
+                loss.out_colsum = s.out_colsum.data();
+                loss.sample_entropy = epoch == 0 ? s.sample_entropy.data() : nullptr;
+                loss.sample_decision = epoch == 0 ? s.sample_decision.data() : nullptr;
+                loss.perm = s.perm.data();
+                loss.offset = offset;
+                const unsigned loss_blocks = blocks(n, ppo::kWarps);
+                ppo::k_loss<<<loss_blocks, 32 * ppo::kWarps, 0, st>>>(loss);
+                check(cudaGetLastError(), "PPO objective");
+                ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(s.block_metrics.data(), static_cast<int>(loss_blocks),
+                                                                   ppo::kMetrics, s.metrics.data(), 1);
+                s.column_sums(s.out_colsum.data(), static_cast<int>(loss_blocks), kOutPad, s.outputs,
+                              s.grads.data() + s.b_off[s.layers], st);
+                s.backward(n, st);
+                if (s.comm.active()) {
+                    // data parallel: the mean of the ranks' minibatch gradients, before the norm clip
+                    s.comm.hooks.allreduce_sum_f32(s.grads.data(), s.param_count, stream, s.comm.hooks.user);
+                    ppo::k_scale<<<blocks(s.param_count, 256), 256, 0, st>>>(s.grads.data(), s.param_count,
+                                                                              1.0f / static_cast<float>(s.comm.hooks.world_size));
+                }
+                ppo::k_square_partials<<<norm_blocks, 256, 0, st>>>(s.grads.data(), s.param_count, s.norm_partial.data());
+                ppo::k_norm_finish<<<1, 32, 0, st>>>(s.norm_partial.data(), norm_blocks, s.norm_sq.data(), s.metrics.data());
+                ++s.optimizer_step;
+                const float bc1 = 1.0f - std::pow(cfg->adam_beta1, static_cast<float>(s.optimizer_step));
+                const float bc2 = 1.0f - std::pow(cfg->adam_beta2, static_cast<float>(s.optimizer_step));
+                ppo::k_adam<<<blocks(s.param_count, 256), 256, 0, st>>>(
+                    s.params.data(), s.grads.data(), s.m1.data(), s.m2.data(), s.param_count, s.norm_sq.data(),
+                    cfg->max_gradient_norm, cfg->learning_rate, cfg->adam_beta1, cfg->adam_beta2, cfg->adam_epsilon, bc1,
+                    bc2, s.adam, 1);
+                check(cudaGetLastError(), "Adam");
+            }
+            epochs_completed = epoch + 1;
+            if (cfg->target_kl > 0.0f) {
+                double sums[ppo::kMetrics];
+                s.metrics.download(sums, ppo::kMetrics, st);
+                double kl = sums[3] - previous_kl;
+                previous_kl = sums[3];
+                double global_samples = static_cast<double>(samples);
+                if (s.comm.active() && s.comm.hooks.allreduce_sum_f64) {
+                    // every rank early-stops together on the KL over all ranks' samples
+                    double pair[2] = {kl, global_samples};
+                    check(cudaMemcpyAsync(s.kl_pair.data(), pair, sizeof pair, cudaMemcpyHostToDevice, st), "KL");
+                    s.comm.hooks.allreduce_sum_f64(s.kl_pair.data(), 2, stream, s.comm.hooks.user);
+                    s.kl_pair.download(pair, 2, st);
+                    kl = pair[0];
+                    global_samples = pair[1];
+                }
+                const double mean_kl = kl / global_samples;
+                if (!std::isfinite(mean_kl)) raise(T8B_ENONFINITE, "PPO KL became non-finite; optimizer update aborted");
+                if (mean_kl > cfg->target_kl) {
+                    early = true;
+                    break;
+                }
+            }
+        }
+        // merge the observation normaliser after the update (src/ppo.cu:1663-1667)
+        if (s.config.observation_normalization) {
+            const size_t chunk = 8192;
+            const size_t chunks = (samples + chunk - 1) / chunk;
+            if (s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
+            dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((s.width + 31) / 32));
+            ppo::k_obs_moments<<<grid, 256, 0, st>>>(r.observations, samples, s.width, chunk, s.obs_chunks.data());
+            ppo::k_obs_merge<<<blocks(s.width, 128), 128, 0, st>>>(s.obs_chunks.data(), static_cast<int>(chunks), s.width,
+                                                                   static_cast<double>(s.obs_count), s.obs_mean.data(),
+                                                                   s.obs_var.data(), s.obs_istd.data(),
+                                                                   s.config.observation_epsilon, nullptr);
+            check(cudaGetLastError(), "merge observation statistics");
+            s.obs_count += samples;
+        }
+        // rollout decision entropy (src/ppo.cu:1671-1683)
+        const int dblocks = 256;
+        if (r.entropies) {
+            k_decision_partials<<<dblocks, 256, 0, st>>>(r.entropies, nullptr, r.action_mask_bits ? nullptr : r.action_masks,
+                                                        r.action_mask_bits, samples, s.entropy_sums.data());
+        } else {
+            k_decision_partials<<<dblocks, 256, 0, st>>>(s.sample_entropy.data(), s.sample_decision.data(), nullptr, nullptr,
+                                                        samples, s.entropy_sums.data());
+        }
+        k_decision_finish<<<1, 32, 0, st>>>(s.entropy_sums.data(), dblocks, s.entropy_sums.data() + 2 * 1024);
+        check(cudaGetLastError(), "decision entropy");
+        double m[ppo::kMetrics];
+        s.metrics.download(m, ppo::kMetrics, st);
+        double ent[2];
+        check(cudaMemcpyAsync(ent, s.entropy_sums.data() + 2 * 1024, sizeof ent, cudaMemcpyDeviceToHost, st), "entropy");
+        check(cudaStreamSynchronize(st), "update");
+        s.sync_error(st);
+        for (double v : m) {
+            if (!std::isfinite(v)) raise(T8B_ENONFINITE, "PPO metrics became non-finite; checkpoint was not written");
+        }
+        if (metrics_out) {
+            const double visits = static_cast<double>(samples) * epochs_completed;
+            t8b_ppo_metrics_t& o = *metrics_out;
+            std::memset(&o, 0, sizeof o);
+            o.policy_loss = static_cast<float>(m[0] / visits);
+            o.value_loss = static_cast<float>(m[1] / visits);
+            o.entropy = static_cast<float>(m[2] / visits);
+            o.approximate_kl = static_cast<float>(m[3] / visits);
+            o.clip_fraction = static_cast<float>(m[4] / visits);
+            o.gradient_norm = static_cast<float>(m[5] / static_cast<double>(minibatches));
+            o.decision_fraction = static_cast<float>(m[6] / visits);
+            o.decision_entropy = m[6] > 0.0 ? static_cast<float>(m[7] / m[6]) : 0.0f;
+            o.rollout_decision_entropy = ent[1] > 0.0 ? static_cast<float>(ent[0] / ent[1]) : 0.0f;
+            o.minibatches = minibatches;
+            o.epochs_completed = epochs_completed;
+            o.early_stopped = early ? 1 : 0;
+        }
+    });
+}
+
+int t8b_policy_get_parameters(t8b_policy* p, float* host, size_t count) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (count != s.param_count) raise(T8B_EINVAL, "parameter count mismatch");
+        s.params.download(host, count, nullptr);
+    });
+}
+
+int t8b_policy_set_parameters(t8b_policy* p, const float* host, size_t count) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (count != s.param_count) raise(T8B_EINVAL, "parameter count mismatch");
+        s.params.upload(host, count, nullptr);
+        s.refresh_operands(nullptr);
+        check(cudaStreamSynchronize(nullptr), "set parameters");
+    });
+}
+
+int t8b_policy_get_gradients(t8b_policy* p, float* host, size_t count) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (count != s.param_count) raise(T8B_EINVAL, "parameter count mismatch");
+        s.grads.download(host, count, nullptr);
+    });
+}
+
+int t8b_policy_get_optimizer_state(t8b_policy* p, float* first, float* second, uint64_t* step) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (first) s.m1.download(first, s.param_count, nullptr);
+        if (second) s.m2.download(second, s.param_count, nullptr);
+        if (step) *step = s.optimizer_step;
+    });
+}
+
+int t8b_policy_set_optimizer_state(t8b_policy* p, const float* first, const float* second, uint64_t step) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (first) s.m1.upload(first, s.param_count, nullptr);
+        if (second) s.m2.upload(second, s.param_count, nullptr);
+        s.optimizer_step = step;
+        check(cudaStreamSynchronize(nullptr), "set optimizer state");
+    });
+}
+
+int t8b_policy_get_observation_statistics(t8b_policy* p, float* mean, float* variance, uint64_t* count) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (mean) s.obs_mean.download(mean, s.width, nullptr);
+        if (variance) s.obs_var.download(variance, s.width, nullptr);
+        if (count) *count = s.obs_count;
+    });
+}
+
+int t8b_policy_set_observation_statistics(t8b_policy* p, const float* mean, const float* variance, uint64_t count) {
+    return with_policy(p, [&](t8b_policy& s) {
+        s.obs_mean.upload(mean, s.width, nullptr);
+        s.obs_var.upload(variance, s.width, nullptr);
+        ppo::k_refresh_istd<<<blocks(s.width, 128), 128>>>(s.obs_var.data(), s.obs_istd.data(), s.width,
+                                                           s.config.observation_epsilon);
+        check(cudaStreamSynchronize(nullptr), "set observation statistics");
+        s.obs_count = count;
+    });
+}
+
+// Test aid: the network outputs [n][query..., value] of the last forward (fp32).
+int t8b_policy_download_outputs(t8b_policy* p, float* host, size_t n) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (n > s.capacity) raise(T8B_EINVAL, "count exceeds capacity");
+        std::vector<float> rows(n * kOutPad);
+        s.out.download(rows.data(), rows.size(), nullptr);
+        for (size_t i = 0; i < n; ++i) std::copy(rows.begin() + i * kOutPad, rows.begin() + i * kOutPad + s.outputs, host + i * s.outputs);
+    });
+}
+
+// Test aid: an intermediate of the last forward/backward as fp32 rows: which = 0 the layer-1
+// input (padded width), 1 hidden activation `layer`, 2 its pre-activation gradient, 3 the output
+// gradient row (64 wide).
+int t8b_policy_download_activation(t8b_policy* p, int which, int layer, float* host, size_t n) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (n > s.capacity || layer < 0 || layer >= s.layers) raise(T8B_EINVAL, "activation request out of range");
+        const bf16* src = which == 0 ? s.x.data() : which == 1 ? s.h[layer].data() : which == 2 ? s.dz[layer].data() : s.dout.data();
+        const size_t width = which == 0 ? s.padded : which == 3 ? kOutPad : s.hidden;
+        std::vector<bf16> rows(n * width);
+        check(cudaMemcpy(rows.data(), src, rows.size() * sizeof(bf16), cudaMemcpyDeviceToHost), "download activation");
+        for (size_t i = 0; i < rows.size(); ++i) host[i] = __bfloat162float(rows[i]);
+    });
+}
+
+int t8b_policy_synchronize(t8b_policy* p, void* stream) {
+    return with_policy(p, [&](t8b_policy&) { check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "synchronize policy"); });
+}
+
+}  // extern "C"

@@ -1,0 +1,775 @@
+// SIMT kernels of the policy and PPO update around the tcgen05 GEMMs: input preparation
+// (normalisation, minibatch gather), the parametric scorer fused with masked sampling or with
+// the clipped PPO objective and its gradient, the tanh/bias epilogues of the GEMMs, split-K and
+// bias-gradient reductions, the global gradient norm and Adam. Every reduction that feeds
+// weights or control decisions runs in a fixed order, so an update is bit-reproducible.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "gemm.cuh"
+
+namespace t8b {
+namespace ppo {
+namespace {  // internal linkage: every translation unit gets its own kernels
+
+constexpr int kWarps = 8;  // warps per block of the warp-per-sample kernels
+constexpr int kMaskWords = 12;
+constexpr int kCandidates = 368;
+constexpr int kMetrics = 8;  // policy loss, value loss, entropy, KL, clip fraction, grad norm, decisions, decision entropy
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ uint64_t splitmix(uint64_t v) {
+    v += 0x9e3779b97f4a7c15ull;
+    v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+    v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+    return v ^ (v >> 31);
+}
+// uniform01 (src/ppo.cu:224-230)
+__device__ __forceinline__ float uniform01(uint64_t seed, uint64_t step, uint64_t lane) {
+    const uint64_t bits = splitmix(seed ^ splitmix(step) ^ splitmix(lane));
+    return static_cast<float>(static_cast<double>(bits >> 40) + 0.5) * (1.0f / 16777216.0f);
+}
+
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// ------------------------------------------------------------------ inputs
+// Normalised (src/ppo.cu:132-145), clipped, bf16, zero-padded rows of the layer-1 operand;
+// with `perm` the rows are gathered (src/ppo.cu:383-421) and the minibatch side data follows.
+struct Prep {
+    const float* obs;
+    int width, padded;  // observation floats, padded operand row
+    const float* mean;
+    const float* istd;
+    float clip;
+    int normalize;
+    const uint32_t* perm;  // null: identity
+    size_t offset, count;
+    __nv_bfloat16* x;
+    // minibatch side data (null when preparing an inference batch)
+    const uint32_t* src_bits;
+    const uint8_t* src_bytes;
+    uint32_t* bits;
+    const int64_t* src_actions;
+    int32_t* actions;
+    const float* src_old_lp;
+    float* old_lp;
+    const float* src_old_v;
+    float* old_v;
+    const float* src_adv;
+    float* adv;
+    const float* src_ret;
+    float* ret;
+    const int32_t* src_tables;
+    int32_t* tables;
+    const double* adv_stats;  // [mean, inverse std] applied to advantages when non-null
+};
+
+__global__ void k_prep(Prep p) {
+    const int lane = threadIdx.x & 31;
+    const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5);
+    if (i >= p.count) return;
+    const size_t src = p.perm ? p.perm[p.offset + i] : p.offset + i;
+    const float* row = p.obs + src * static_cast<size_t>(p.width);
+    __nv_bfloat16* out = p.x + i * static_cast<size_t>(p.padded);
+    for (int j = lane; j < p.padded; j += 32) {
+        float v = 0.0f;
+        if (j < p.width) {
+            v = row[j];
+            if (p.normalize) v = fminf(p.clip, fmaxf(-p.clip, (v - p.mean[j]) * p.istd[j]));
+        }
+        out[j] = __float2bfloat16_rn(v);
+    }
+    if (p.bits != nullptr) {
+        if (lane < kMaskWords) {
+            uint32_t w;
+            if (p.src_bits) {
+                w = p.src_bits[src * kMaskWords + lane];
+            } else {
+                w = 0;
+                const uint8_t* m = p.src_bytes + src * kCandidates + lane * 32;
+                for (int b = 0; b < 32 && lane * 32 + b < kCandidates; ++b) w |= (m[b] != 0 ? 1u : 0u) << b;
+            }
+            p.bits[i * kMaskWords + lane] = w;
+        }
+        if (lane == 0) {
+            p.actions[i] = static_cast<int32_t>(p.src_actions[src]);
+            p.old_lp[i] = p.src_old_lp[src];
+            p.old_v[i] = p.src_old_v[src];
+            float a = p.src_adv[src];
+            if (p.adv_stats) a = static_cast<float>((static_cast<double>(a) - p.adv_stats[0]) * p.adv_stats[1]);
+            p.adv[i] = a;
+            p.ret[i] = p.src_ret[src];
+            p.tables[i] = p.src_tables ? p.src_tables[src] : 0;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ GEMM epilogues
+// Hidden layer forward: h = tanh(acc + b) as bf16 [rows][ld].
+struct EpiTanh {
+    const float* bias;
+    __nv_bfloat16* out;
+    int ld, m;
+    __device__ void operator()(int row, int col0, const float* v, int, int, int, int) const {
+        if (row >= m) return;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            const float a = tanh_fast(v[2 * i] + bias[col0 + 2 * i]);
+            const float b = tanh_fast(v[2 * i + 1] + bias[col0 + 2 * i + 1]);
+            __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            packed[i] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ld + col0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+    }
+};
+
+// Output layer: o = acc + b for the valid columns, fp32 [rows][ld].
+struct EpiBias {
+    const float* bias;
+    float* out;
+    int ld, m, valid;
+    __device__ void operator()(int row, int col0, const float* v, int, int, int, int) const {
+        if (row >= m) return;
+        float* dst = out + static_cast<size_t>(row) * ld + col0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dst[i] = col0 + i < valid ? v[i] + bias[col0 + i] : 0.0f;
+    }
+};
+
+// Backward through tanh: g = acc * (1 - h^2) as bf16 [rows][ld], plus per-32-row column sums of g
+// (fp32 [tile_m * 4 + quarter][ld]) for the bias gradient.
+struct EpiTanhGrad {
+    const __nv_bfloat16* h;
+    __nv_bfloat16* out;
+    float* colsum;
+    int ld, m;
+    __device__ void operator()(int row, int col0, const float* v, int, int tm, int quarter, int lane) const {
+        float g[32];
+        const bool live = row < m;
+        if (live) {
+            const uint4* src = reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * ld + col0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint4 q = src[i];
+                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const __nv_bfloat162 pair = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
+                    const float2 f = __bfloat1622float2(pair);
+                    g[8 * i + 2 * k] = v[8 * i + 2 * k] * (1.0f - f.x * f.x);
+                    g[8 * i + 2 * k + 1] = v[8 * i + 2 * k + 1] * (1.0f - f.y * f.y);
+                }
+            }
+            uint32_t packed[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                __nv_bfloat162 pair = __floats2bfloat162_rn(g[2 * i], g[2 * i + 1]);
+                packed[i] = *reinterpret_cast<uint32_t*>(&pair);
+            }
+            uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ld + col0);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) g[i] = 0.0f;
+        }
+        // Transpose-reduce across the warp: after 5 halving steps lane c holds column c's sum.
+#pragma unroll
+        for (int width = 16; width >= 1; width >>= 1) {
+            const bool upper = (lane & width) != 0;
+#pragma unroll
+            for (int i = 0; i < width; ++i) {
+                const float send = upper ? g[i] : g[i + width];
+                const float keep = upper ? g[i + width] : g[i];
+                g[i] = keep + __shfl_xor_sync(0xffffffffu, send, width);
+            }
+        }
+        colsum[(static_cast<size_t>(tm) * 4 + quarter) * ld + col0 + lane] = g[0];
+    }
+};
+
+// Split-K partial of a weight gradient: part[split][row][col] (fp32).
+struct EpiSplit {
+    float* part;
+    int m, n;
+    __device__ void operator()(int row, int col0, const float* v, int split, int, int, int) const {
+        if (row >= m) return;
+        float* out = part + (static_cast<size_t>(split) * m + row) * n + col0;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+};
+
+// grad[r][c] (reference layout, rows x cols, cols <= part cols) = sum over splits in order;
+// transpose: the partial is [cols][rows] (the weight gradient came out transposed).
+__global__ void k_reduce_split(const float* part, int splits, int part_rows, int part_cols, float* grad, int rows,
+                               int cols, int transpose) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols) return;
+    const int r = i / cols, c = i % cols;
+    const size_t at = transpose ? static_cast<size_t>(c) * part_cols + r : static_cast<size_t>(r) * part_cols + c;
+    const size_t stride = static_cast<size_t>(part_rows) * part_cols;
+    float sum = 0.0f;
+    for (int s = 0; s < splits; ++s) sum += part[s * stride + at];
+    grad[i] = sum;
+}
+
+// Bias gradient = column sums of the per-32-row partials, in row order.
+__global__ void k_reduce_columns(const float* partial, int rows, int ld, int cols, float* grad) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= cols) return;
+    float sum = 0.0f;
+    for (int r = 0; r < rows; ++r) sum += partial[static_cast<size_t>(r) * ld + c];
+    grad[c] = sum;
+}
+
+// Column sums of a [rows][ld] fp32 matrix in two fixed-order levels: each block sums 32 columns
+// over one row chunk (8 interleaved sub-rows, combined in order), then one pass over the chunks.
+constexpr int kColumnChunks = 128;
+__global__ void k_column_partials(const float* in, int rows, int ld, int cols, float* partial) {
+    __shared__ float part[8][33];
+    const int c = blockIdx.x * 32 + threadIdx.x;
+    const int per = (rows + gridDim.y - 1) / gridDim.y;
+    const int begin = blockIdx.y * per;
+    const int end = min(rows, begin + per);
+    float s = 0.0f;
+    if (c < cols) {
+        for (int r = begin + threadIdx.y; r < end; r += 8) s += in[static_cast<size_t>(r) * ld + c];
+    }
+    part[threadIdx.y][threadIdx.x] = s;
+    __syncthreads();
+    if (threadIdx.y == 0 && c < cols) {
+        float t = 0.0f;
+        for (int k = 0; k < 8; ++k) t += part[k][threadIdx.x];
+        partial[static_cast<size_t>(blockIdx.y) * cols + c] = t;
+    }
+}
+
+__global__ void k_scale(float* v, size_t n, float factor) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) v[i] *= factor;
+}
+
+// ------------------------------------------------------------------ scorer + sampler
+// parametric_policy_output_kernel + masked_sample_kernel (src/ppo.cu:316-348, 232-306): one warp
+// per sample; scores q . F[table, a] / sqrt(F) only where needed, masked softmax, inverse-CDF
+// sample, log-probability, value and entropy.
+struct Sample {
+    const float* out;  // [n][ld]: q (feature_size), value
+    int ld, feature_size;
+    const float* features;  // [tables][368][feature_size]
+    int table_count;
+    const int32_t* tables;
+    const uint32_t* bits;   // [n][12] or null
+    const uint8_t* bytes;   // [n][368] or null
+    size_t count;
+    uint64_t seed, step, lane_offset;
+    int deterministic;
+    float* logits;  // [n][368] or null
+    int64_t* actions;
+    float* log_probs;
+    float* values;
+    float* entropies;
+};
+
+__device__ __forceinline__ uint32_t mask_word(const uint32_t* bits, const uint8_t* bytes, size_t i, int word, int lane) {
+    if (bits) return bits[i * kMaskWords + word];
+    const int c = word * 32 + lane;
+    const bool legal = c < kCandidates && bytes[i * kCandidates + c] != 0;
+    return __ballot_sync(0xffffffffu, legal);
+}
+
+constexpr int kFeatures = 32;  // kFullMoveFeatureSize (include/t8_v2/full_move_roster.hpp:21)
+
+// q . F[a] in feature order, then scaled (src/ppo.cu:340-346).
+__device__ __forceinline__ float score_of(const float* q, const float* frow, int, float scale) {
+    const float4* f4 = reinterpret_cast<const float4*>(frow);
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kFeatures / 4; ++k) {
+        const float4 f = __ldg(f4 + k);
+        s += q[4 * k] * f.x;
+        s += q[4 * k + 1] * f.y;
+        s += q[4 * k + 2] * f.z;
+        s += q[4 * k + 3] * f.w;
+    }
+    return s * scale;
+}
+
+// 32 per-lane vectors -> lane f holds the warp sum of element f.
+__device__ __forceinline__ float transpose_sum32(float* g, int lane) {
+#pragma unroll
+    for (int width = 16; width >= 1; width >>= 1) {
+        const bool upper = (lane & width) != 0;
+#pragma unroll
+        for (int i = 0; i < width; ++i) {
+            const float send = upper ? g[i] : g[i + width];
+            const float keep = upper ? g[i + width] : g[i];
+            g[i] = keep + __shfl_xor_sync(0xffffffffu, send, width);
+        }
+    }
+    return g[0];
+}
+
+__global__ void k_sample(Sample p) {
+    __shared__ float qs[kWarps][64];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
+    if (i >= p.count) return;
+    const float* o = p.out + i * p.ld;
+    for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
+    __syncwarp();
+    const float* q = qs[warp];
+    const float scale = rsqrtf(static_cast<float>(p.feature_size));
+    const int table = p.tables ? p.tables[i] : 0;
+    const bool bad_table = table < 0 || table >= p.table_count;
+    const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * kCandidates * p.feature_size;
+    uint32_t words[kMaskWords];
+    bool any = false;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) {
+        words[w] = mask_word(p.bits, p.bytes, i, w, lane);
+        any = any || words[w] != 0;
+    }
+    float s[kMaskWords];
+    float best = -3.402823466e38f;
+    int best_at = kCandidates;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) {
+        const int c = w * 32 + lane;
+        const bool legal = any ? ((words[w] >> lane) & 1u) != 0 : c == 0;
+        s[w] = 0.0f;
+        if (c < kCandidates && (legal || p.logits)) s[w] = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale);
+        if (p.logits && c < kCandidates) p.logits[i * kCandidates + c] = s[w];
+        if (legal && c < kCandidates && (s[w] > best || best_at == kCandidates)) {
+            best = s[w];
+            best_at = c;
+        }
+    }
+    // argmax: largest score, then the lowest candidate (the reference's first-seen maximum)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+        const int oa = __shfl_xor_sync(0xffffffffu, best_at, off);
+        if (ob > best || (ob == best && oa < best_at)) {
+            best = ob;
+            best_at = oa;
+        }
+    }
+    const float maximum = best;
+    float e[kMaskWords];
+    float local = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) {
+        const int c = w * 32 + lane;
+        const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+        e[w] = legal ? expf(s[w] - maximum) : 0.0f;
+        local += e[w];
+    }
+    const float sum = fmaxf(warp_sum(local), 1e-20f);
+    int selected = best_at;
+    if (!p.deterministic) {
+        const float target = uniform01(p.seed, p.step, i + p.lane_offset) * sum;
+        float running = 0.0f;
+        int found = -1;
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            float x = e[w];
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, x, off);
+                if (lane >= off) x += y;
+            }
+            const float cumulative = running + x;
+            const uint32_t hit = __ballot_sync(0xffffffffu, found < 0 && e[w] > 0.0f && target <= cumulative);
+            if (found < 0 && hit) found = w * 32 + __ffs(hit) - 1;
+            running += __shfl_sync(0xffffffffu, x, 31);
+        }
+        if (found >= 0) selected = found;
+    }
+    const float log_sum = logf(sum) + maximum;
+    float entropy = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) {
+        const int c = w * 32 + lane;
+        const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+        if (legal) {
+            const float lp = s[w] - log_sum;
+            entropy -= expf(lp) * lp;
+        }
+    }
+    entropy = warp_sum(entropy);
+    const float chosen = __shfl_sync(0xffffffffu, s[selected >> 5], selected & 31);
+    if (lane == 0) {
+        p.actions[i] = selected;
+        p.log_probs[i] = chosen - log_sum;
+        p.values[i] = bad_table ? __int_as_float(0x7fc00000) : q[p.feature_size];
+        p.entropies[i] = entropy;
+    }
+}
+
+// ------------------------------------------------------------------ PPO objective
+// ppo_output_gradient_kernel + parametric_policy_gradient_kernel (src/ppo.cu:453-565, 350-381):
+// one warp per sample; the clipped policy objective, the clipped value loss and the entropy
+// bonus; d(objective)/d(q, value) written as the bf16 gradient row of the output layer.
+struct Loss {
+    const float* out;  // [n][ld]
+    int ld, feature_size;
+    const float* features;
+    int table_count;
+    const int32_t* tables;
+    const uint32_t* bits;
+    const int32_t* actions;
+    const float* old_lp;
+    const float* old_v;
+    const float* adv;
+    const float* ret;
+    size_t count;
+    float inv_batch;  // 1 / minibatch size
+    float clip, value_clip, value_coef, entropy_coef;
+    __nv_bfloat16* dout;  // [n][ld_grad]
+    int ld_grad;
+    double* block_metrics;  // [blocks][kMetrics]
+    float* out_colsum;      // [blocks][ld_grad]: bias gradient partials of the output layer
+    float* sample_entropy;  // first epoch: entropy per rollout sample (or null)
+    uint8_t* sample_decision;
+    const uint32_t* perm;
+    size_t offset;
+};
+
+__global__ void k_loss(Loss p) {
+    __shared__ float qs[kWarps][64];
+    __shared__ float grads[kWarps][64];
+    __shared__ float metric[kWarps][kMetrics];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
+    const bool live = i < p.count;
+    for (int f = lane; f < 64; f += 32) grads[warp][f] = 0.0f;
+    if (lane < kMetrics) metric[warp][lane] = 0.0f;
+    if (live) {
+        const float* o = p.out + i * p.ld;
+        for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
+        __syncwarp();
+        const float* q = qs[warp];
+        const float scale = rsqrtf(static_cast<float>(p.feature_size));
+        const int table = p.tables[i];
+        const bool bad_table = table < 0 || table >= p.table_count;
+        const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * kCandidates * p.feature_size;
+        uint32_t words[kMaskWords];
+        bool any = false;
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            words[w] = p.bits[i * kMaskWords + w];
+            any = any || words[w] != 0;
+        }
+        float s[kMaskWords];
+        float local_max = -3.402823466e38f;
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const int c = w * 32 + lane;
+            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+            s[w] = legal ? (bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale)) : 0.0f;
+            if (legal) local_max = fmaxf(local_max, s[w]);
+        }
+        const float maximum = warp_max(local_max);
+        float local = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const int c = w * 32 + lane;
+            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+            if (legal) local += expf(s[w] - maximum);
+        }
+        const float sum = fmaxf(warp_sum(local), 1e-20f);
+        const float log_sum = logf(sum) + maximum;
+        const int selected = any ? p.actions[i] : 0;
+        const float chosen = __shfl_sync(0xffffffffu, s[(selected >> 5) % kMaskWords], selected & 31);
+        const float new_lp = chosen - log_sum;
+        const float log_ratio = new_lp - p.old_lp[i];
+        const float ratio = expf(log_ratio);
+        const float advantage = p.adv[i];
+        const float unclipped = ratio * advantage;
+        const float clipped = fminf(1.0f + p.clip, fmaxf(1.0f - p.clip, ratio)) * advantage;
+        const bool use_unclipped = unclipped <= clipped;
+        const float policy_loss = -fminf(unclipped, clipped);
+        const float lp_grad = use_unclipped ? -advantage * ratio : 0.0f;
+        float entropy = 0.0f;
+        int legal_count = 0;
+        float prob[kMaskWords], lps[kMaskWords];
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const int c = w * 32 + lane;
+            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+            lps[w] = s[w] - log_sum;
+            prob[w] = legal ? expf(lps[w]) : 0.0f;
+            if (legal) {
+                entropy -= prob[w] * lps[w];
+                ++legal_count;
+            }
+        }
+        entropy = warp_sum(entropy);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) legal_count += __shfl_xor_sync(0xffffffffu, legal_count, o);
+        // d(objective)/d(score) for legal candidates, folded straight into d/dq
+        float dq_local[kFeatures];
+#pragma unroll
+        for (int f = 0; f < kFeatures; ++f) dq_local[f] = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const int c = w * 32 + lane;
+            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
+            if (!legal) continue;
+            float g = (lp_grad * ((c == selected ? 1.0f : 0.0f) - prob[w])) * p.inv_batch;
+            g += p.entropy_coef * prob[w] * (lps[w] + entropy) * p.inv_batch;
+            if (!bad_table) {
+                const float4* f4 = reinterpret_cast<const float4*>(ftab + c * kFeatures);
+#pragma unroll
+                for (int k = 0; k < kFeatures / 4; ++k) {
+                    const float4 f = __ldg(f4 + k);
+                    dq_local[4 * k] += g * f.x;
+                    dq_local[4 * k + 1] += g * f.y;
+                    dq_local[4 * k + 2] += g * f.z;
+                    dq_local[4 * k + 3] += g * f.w;
+                }
+            }
+        }
+        const float total = transpose_sum32(dq_local, lane);
+        grads[warp][lane] = bad_table ? __int_as_float(0x7fc00000) : total * scale;
+        const float value = q[p.feature_size];
+        const float error = value - p.ret[i];
+        float vgrad = error;
+        float vloss = 0.5f * error * error;
+        if (p.value_clip > 0.0f) {
+            const float delta = value - p.old_v[i];
+            const float clipped_value = p.old_v[i] + fminf(p.value_clip, fmaxf(-p.value_clip, delta));
+            const float cerr = clipped_value - p.ret[i];
+            const float closs = 0.5f * cerr * cerr;
+            if (closs > vloss) {
+                vloss = closs;
+                vgrad = fabsf(delta) <= p.value_clip ? cerr : 0.0f;
+            }
+        }
+        if (lane == 0) {
+            grads[warp][p.feature_size] = p.value_coef * vgrad * p.inv_batch;
+            metric[warp][0] = policy_loss;
+            metric[warp][1] = vloss;
+            metric[warp][2] = entropy;
+            metric[warp][3] = (ratio - 1.0f) - log_ratio;
+            metric[warp][4] = fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f;
+            metric[warp][6] = legal_count > 1 ? 1.0f : 0.0f;
+            metric[warp][7] = legal_count > 1 ? entropy : 0.0f;
+            if (p.sample_entropy) {
+                const size_t sample = p.perm[p.offset + i];
+                p.sample_entropy[sample] = entropy;
+                p.sample_decision[sample] = legal_count > 1 ? 1 : 0;
+            }
+        }
+        __syncwarp();
+        for (int f = lane; f < p.ld_grad; f += 32) p.dout[i * p.ld_grad + f] = __float2bfloat16_rn(grads[warp][f]);
+    }
+    __syncthreads();
+    // block partials in warp order (deterministic)
+    if (threadIdx.x < p.ld_grad) {
+        float sum = 0.0f;
+        for (int w = 0; w < kWarps; ++w) sum += grads[w][threadIdx.x];
+        p.out_colsum[static_cast<size_t>(blockIdx.x) * p.ld_grad + threadIdx.x] = sum;
+    }
+    if (threadIdx.x < kMetrics) {
+        double sum = 0.0;
+        for (int w = 0; w < kWarps; ++w) sum += metric[w][threadIdx.x];
+        p.block_metrics[static_cast<size_t>(blockIdx.x) * kMetrics + threadIdx.x] = sum;
+    }
+}
+
+// Fixed-order sum of [rows][cols] doubles into out[cols] (+= when accumulate).
+__global__ void k_sum_rows_f64(const double* in, int rows, int cols, double* out, int accumulate) {
+    __shared__ double part[256];
+    const int c = blockIdx.x;
+    double s = 0.0;
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) s += in[static_cast<size_t>(r) * cols + c];
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) out[c] = (accumulate ? out[c] : 0.0) + part[0];
+}
+
+// ------------------------------------------------------------------ norm + Adam
+// Squared gradient norm: per-block partial sums over fixed chunks, then one fixed-order sum.
+__global__ void k_square_partials(const float* g, size_t n, double* partial) {
+    __shared__ double part[256];
+    double s = 0.0;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const double v = g[i];
+        s += v * v;
+    }
+    part[threadIdx.x] = s;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) partial[blockIdx.x] = part[0];
+}
+
+__global__ void k_norm_finish(const double* partial, int blocks, double* norm_sq, double* metrics) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double s = 0.0;
+    for (int b = 0; b < blocks; ++b) s += partial[b];
+    *norm_sq = s;
+    metrics[5] += sqrt(s);
+}
+
+// One tensor's view in the flat parameter vector, with the bf16 operand copies to refresh.
+struct TensorSpec {
+    size_t offset;
+    int rows, cols;            // reference layout [rows][cols] (a bias has rows = 1)
+    __nv_bfloat16* copy;       // [rows][copy_ld] operand copy or null
+    int copy_ld;
+    __nv_bfloat16* copy_t;     // [cols][copy_t_ld] transposed operand copy or null
+    int copy_t_ld;
+};
+
+constexpr int kMaxTensors = 20;
+struct AdamSpec {
+    TensorSpec t[kMaxTensors];
+    int count;
+};
+
+// adam_kernel (src/ppo.cu:710-736) over the whole flat vector, fused with the bf16 casts.
+__global__ void k_adam(float* params, const float* grads, float* m1, float* m2, size_t n, const double* norm_sq,
+                       float max_norm, float lr, float beta1, float beta2, float eps, float bc1, float bc2, AdamSpec spec,
+                       int update) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    float p = params[i];
+    if (update) {
+        const float norm = sqrtf(static_cast<float>(*norm_sq));
+        if (isfinite(norm)) {
+            const float scale = norm > max_norm ? max_norm / fmaxf(norm, 1e-12f) : 1.0f;
+            const float g = grads[i] * scale;
+            const float m = beta1 * m1[i] + (1.0f - beta1) * g;
+            const float v = beta2 * m2[i] + (1.0f - beta2) * g * g;
+            m1[i] = m;
+            m2[i] = v;
+            p -= lr * (m / bc1) / (sqrtf(v / bc2) + eps);
+            params[i] = p;
+        }
+    }
+    int t = 0;
+    while (t + 1 < spec.count && spec.t[t + 1].offset <= i) ++t;
+    const TensorSpec& ts = spec.t[t];
+    const size_t local = i - ts.offset;
+    const int r = static_cast<int>(local / ts.cols), c = static_cast<int>(local % ts.cols);
+    const __nv_bfloat16 b = __float2bfloat16_rn(p);
+    if (ts.copy) ts.copy[static_cast<size_t>(r) * ts.copy_ld + c] = b;
+    if (ts.copy_t) ts.copy_t[static_cast<size_t>(c) * ts.copy_t_ld + r] = b;
+}
+
+// ------------------------------------------------------------------ observation normaliser
+// Per-feature moments of a block of observations (fp64), merged by Chan's formula in a fixed
+// order (src/ppo.cu:150-215 computes them in two passes over the rollout; one pass of
+// per-chunk (count, mean, M2) merged in chunk order gives the same statistics).
+__global__ void k_obs_moments(const float* obs, size_t samples, int width, size_t chunk, double* out) {
+    // grid: (chunks, ceil(width / 32)); each thread owns one feature over one chunk
+    const int feature = blockIdx.y * 32 + (threadIdx.x & 31);
+    const int sub = threadIdx.x >> 5;  // 8 sub-chunks per block, merged in order
+    __shared__ double sm_mean[8][32], sm_m2[8][32];
+    __shared__ double sm_n[8];
+    const size_t begin = static_cast<size_t>(blockIdx.x) * chunk;
+    const size_t end = begin + chunk < samples ? begin + chunk : samples;
+    const size_t span = (end > begin ? end - begin : 0);
+    const size_t per = (span + 7) / 8;
+    const size_t b = begin + sub * per;
+    const size_t e = b + per < end ? b + per : end;
+    double mean = 0.0, m2 = 0.0, count = 0.0;
+    if (feature < width) {
+        for (size_t s = b; s < e; ++s) {
+            const double x = obs[s * width + feature];
+            count += 1.0;
+            const double d = x - mean;
+            mean += d / count;
+            m2 += d * (x - mean);
+        }
+    } else {
+        count = e > b ? static_cast<double>(e - b) : 0.0;
+    }
+    sm_mean[sub][threadIdx.x & 31] = mean;
+    sm_m2[sub][threadIdx.x & 31] = m2;
+    if ((threadIdx.x & 31) == 0) sm_n[sub] = e > b ? static_cast<double>(e - b) : 0.0;
+    __syncthreads();
+    if (sub == 0 && feature < width) {
+        double n = 0.0, mu = 0.0, q = 0.0;
+        for (int k = 0; k < 8; ++k) {
+            const double nk = sm_n[k];
+            if (nk == 0.0) continue;
+            const double total = n + nk;
+            const double delta = sm_mean[k][threadIdx.x & 31] - mu;
+            q += sm_m2[k][threadIdx.x & 31] + delta * delta * n * nk / total;
+            mu += delta * nk / total;
+            n = total;
+        }
+        double* slot = out + (static_cast<size_t>(blockIdx.x) * width + feature) * 3;
+        slot[0] = n;
+        slot[1] = mu;
+        slot[2] = q;
+    }
+}
+
+// merge_observation_moments_kernel + refresh_inverse_standard_deviation_kernel (src/ppo.cu:183-215).
+__global__ void k_obs_merge(const double* chunks, int chunk_count, int width, double running_count, float* mean,
+                            float* variance, float* istd, float epsilon, double* batch_out) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f >= width) return;
+    double n = 0.0, mu = 0.0, q = 0.0;
+    for (int k = 0; k < chunk_count; ++k) {
+        const double* slot = chunks + (static_cast<size_t>(k) * width + f) * 3;
+        if (slot[0] == 0.0) continue;
+        const double total = n + slot[0];
+        const double delta = slot[1] - mu;
+        q += slot[2] + delta * delta * n * slot[0] / total;
+        mu += delta * slot[0] / total;
+        n = total;
+    }
+    if (batch_out) {
+        batch_out[3 * f] = n;
+        batch_out[3 * f + 1] = mu;
+        batch_out[3 * f + 2] = q;
+    }
+    if (mean == nullptr) return;
+    const double total = running_count + n;
+    const double delta = mu - static_cast<double>(mean[f]);
+    const double m2 = static_cast<double>(variance[f]) * running_count + q + delta * delta * running_count * n / total;
+    mean[f] = static_cast<float>(static_cast<double>(mean[f]) + delta * n / total);
+    variance[f] = static_cast<float>(m2 / total);
+    istd[f] = 1.0f / sqrtf(variance[f] + epsilon);
+}
+
+__global__ void k_refresh_istd(const float* variance, float* istd, int width, float epsilon) {
+    const int f = blockIdx.x * blockDim.x + threadIdx.x;
+    if (f < width) istd[f] = 1.0f / sqrtf(variance[f] + epsilon);
+}
+
+}  // namespace
+}  // namespace ppo
+}  // namespace t8b

@@ -1,0 +1,573 @@
+// Rollout buffer: the GpuRolloutBuffer contract (include/t8_v2/ppo.hpp:223-291, src/ppo.cu:2001-2481)
+// with its C ABI (t8b_rollout_*), plus the raw-logits PPO objective (t8b_ppo_output_gradient).
+//
+// Storage is [step][environment] so a step's records are contiguous and GAE's reverse sweep
+// reads coalesced rows. Masks are kept packed (12 words per sample) next to the uint8 view of
+// the reference. GAE writes advantages and returns and, in the same pass, per-block fp64
+// moments of the advantages, so normalisation needs one more pass instead of two.
+#include "common.cuh"
+#include "ppo_kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <vector>
+
+namespace t8b {
+
+constexpr unsigned kGaeThreads = 128;
+
+// gae_kernel (src/ppo.cu:2003-2029) fused with advantage_stats_kernel (src/ppo.cu:2031-2063).
+__global__ void k_gae(const float* rewards, const float* values, const uint8_t* terminated, const uint8_t* truncated,
+                      const float* next_values, size_t envs, size_t horizon, float gamma, float lambda, float* adv,
+                      float* ret, double* partial) {
+    __shared__ double s1[kGaeThreads], s2[kGaeThreads];
+    const size_t env = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    double sum = 0.0, square = 0.0;
+    if (env < envs) {
+        float next = 0.0f;
+        for (size_t back = 0; back < horizon; ++back) {
+            const size_t at = (horizon - 1 - back) * envs + env;
+            const bool time_limit = truncated[at] != 0;
+            const bool ended = terminated[at] != 0;
+            const float bootstrap = ended && !time_limit ? 0.0f : 1.0f;
+            const float trace = ended || time_limit ? 0.0f : 1.0f;
+            const float value = values[at];
+            const float delta = rewards[at] + gamma * next_values[at] * bootstrap - value;
+            next = delta + gamma * lambda * trace * next;
+            adv[at] = next;
+            ret[at] = next + value;
+            sum += static_cast<double>(next);
+            square += static_cast<double>(next) * static_cast<double>(next);
+        }
+    }
+    s1[threadIdx.x] = sum;
+    s2[threadIdx.x] = square;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            s1[threadIdx.x] += s1[threadIdx.x + w];
+            s2[threadIdx.x] += s2[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        partial[2 * blockIdx.x] = s1[0];
+        partial[2 * blockIdx.x + 1] = s2[0];
+    }
+}
+
+// Fixed-order total of [blocks][2] partial sums -> out[0..1].
+__global__ void k_pair_total(const double* partial, int blocks, double* out) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double a = 0.0, b = 0.0;
+    for (int i = 0; i < blocks; ++i) {
+        a += partial[2 * i];
+        b += partial[2 * i + 1];
+    }
+    out[0] = a;
+    out[1] = b;
+}
+
+// Per-block fp64 (sum, sum of squares) of a float array, grid-stride in index order.
+__global__ void k_moments(const float* values, size_t n, double* partial) {
+    __shared__ double s1[256], s2[256];
+    double a = 0.0, b = 0.0;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const double v = values[i];
+        a += v;
+        b += v * v;
+    }
+    s1[threadIdx.x] = a;
+    s2[threadIdx.x] = b;
+    __syncthreads();
+    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+        if (threadIdx.x < w) {
+            s1[threadIdx.x] += s1[threadIdx.x + w];
+            s2[threadIdx.x] += s2[threadIdx.x + w];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        partial[2 * blockIdx.x] = s1[0];
+        partial[2 * blockIdx.x + 1] = s2[0];
+    }
+}
+
+// normalize_advantages_kernel (src/ppo.cu:2079-2091); stats = (sum, sum of squares, count).
+__global__ void k_normalize(float* adv, size_t n, const double* stats) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const double count = stats[2];
+    const double mean = stats[0] / count;
+    const double second = stats[1] / count;
+    const double inv = 1.0 / sqrt(fmax(second - mean * mean, 1e-12));
+    adv[i] = static_cast<float>((static_cast<double>(adv[i]) - mean) * inv);
+}
+
+__global__ void k_set_count(double* stats, double count) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) stats[2] = count;
+}
+
+// record_outcome_kernel (src/ppo.cu:2093-2112)
+__global__ void k_record_outcome(float* rewards, uint8_t* terminated, uint8_t* truncated, float* next_values,
+                                 const float* r, const uint8_t* term, const uint8_t* trunc, const float* nv, float scale,
+                                 size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    rewards[i] = r[i] * scale;
+    terminated[i] = term[i];
+    truncated[i] = trunc[i];
+    next_values[i] = nv[i];
+}
+
+__global__ void k_pack_masks(const uint8_t* bytes, uint32_t* bits, size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * 12) return;
+    const size_t sample = i / 12;
+    const int word = static_cast<int>(i % 12);
+    uint32_t w = 0;
+    for (int b = 0; b < 32 && word * 32 + b < 368; ++b) w |= (bytes[sample * 368 + word * 32 + b] != 0 ? 1u : 0u) << b;
+    bits[i] = w;
+}
+
+__global__ void k_expand(const uint32_t* bits, uint8_t* bytes, size_t n) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * 368) return;
+    const size_t sample = i / 368;
+    const int c = static_cast<int>(i % 368);
+    bytes[i] = (bits[sample * 12 + (c >> 5)] >> (c & 31)) & 1u;
+}
+
+// discounted_return_kernel (src/ppo.cu:2114-2131)
+__global__ void k_discounted(const float* rewards, const uint8_t* terminated, const uint8_t* truncated, size_t envs,
+                             size_t horizon, float gamma, float* running, float* samples) {
+    const size_t env = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (env >= envs) return;
+    float r = running[env];
+    for (size_t t = 0; t < horizon; ++t) {
+        const size_t at = t * envs + env;
+        r = r * gamma + rewards[at];
+        samples[at] = r;
+        if (terminated[at] || truncated[at]) r = 0.0f;
+    }
+    running[env] = r;
+}
+
+// scale_rewards_kernel (src/ppo.cu:2133-2137)
+__global__ void k_scale_rewards(float* rewards, size_t n, float scale, float clip) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) rewards[i] = fminf(clip, fmaxf(-clip, rewards[i] * scale));
+}
+
+// ppo_output_gradient_kernel (src/ppo.cu:453-565) on raw outputs [n][k + 1], one warp per sample.
+constexpr int kMaxLogitSlots = 16;  // per lane: k <= 512
+__global__ void k_logit_objective(const float* out, const uint8_t* masks, const int64_t* actions, const float* old_lp,
+                                  const float* old_v, const float* adv, const float* ret, size_t n, int k, float inv_batch,
+                                  float clip, float value_clip, float value_coef, float entropy_coef, float* grads,
+                                  double* block_metrics) {
+    __shared__ float metric[ppo::kWarps][ppo::kMetrics];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t i = static_cast<size_t>(blockIdx.x) * ppo::kWarps + warp;
+    if (lane < ppo::kMetrics) metric[warp][lane] = 0.0f;
+    const int slots = (k + 31) / 32;
+    if (i < n) {
+        const float* o = out + i * static_cast<size_t>(k + 1);
+        const uint8_t* m = masks + i * static_cast<size_t>(k);
+        float logit[kMaxLogitSlots];
+        bool legal[kMaxLogitSlots];
+        bool any_local = false;
+#pragma unroll
+        for (int j = 0; j < kMaxLogitSlots; ++j) {
+            const int a = j * 32 + lane;
+            const bool inside = j < slots && a < k;
+            logit[j] = inside ? o[a] : 0.0f;
+            legal[j] = inside && m[a] != 0;
+            any_local = any_local || legal[j];
+        }
+        const bool any = __any_sync(0xffffffffu, any_local);
+        float local_max = -3.402823466e38f;
+#pragma unroll
+        for (int j = 0; j < kMaxLogitSlots; ++j) {
+            const int a = j * 32 + lane;
+            if (!any) legal[j] = j < slots && a == 0;
+            if (legal[j]) local_max = fmaxf(local_max, logit[j]);
+        }
+        const float maximum = ppo::warp_max(local_max);
+        float local = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kMaxLogitSlots; ++j) {
+            if (legal[j]) local += expf(logit[j] - maximum);
+        }
+        const float sum = fmaxf(ppo::warp_sum(local), 1e-20f);
+        const float log_sum = logf(sum) + maximum;
+        const int selected = any ? static_cast<int>(actions[i]) : 0;
+        const float chosen = __shfl_sync(0xffffffffu, logit[(selected >> 5) % kMaxLogitSlots], selected & 31);
+        const float log_ratio = (chosen - log_sum) - old_lp[i];
+        const float ratio = expf(log_ratio);
+        const float a_i = adv[i];
+        const float unclipped = ratio * a_i;
+        const float clipped = fminf(1.0f + clip, fmaxf(1.0f - clip, ratio)) * a_i;
+        const float lp_grad = unclipped <= clipped ? -a_i * ratio : 0.0f;
+        float entropy = 0.0f;
+        int legal_count = 0;
+        float prob[kMaxLogitSlots];
+#pragma unroll
+        for (int j = 0; j < kMaxLogitSlots; ++j) {
+            prob[j] = legal[j] ? expf(logit[j] - log_sum) : 0.0f;
+            if (legal[j]) {
+                entropy -= prob[j] * (logit[j] - log_sum);
+                ++legal_count;
+            }
+        }
+        entropy = ppo::warp_sum(entropy);
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) legal_count += __shfl_xor_sync(0xffffffffu, legal_count, off);
+        float* g = grads + i * static_cast<size_t>(k + 1);
+#pragma unroll
+        for (int j = 0; j < kMaxLogitSlots; ++j) {
+            const int a = j * 32 + lane;
+            if (j >= slots || a >= k) continue;
+            float value = 0.0f;
+            if (legal[j]) {
+                value = (lp_grad * ((a == selected ? 1.0f : 0.0f) - prob[j])) * inv_batch;
+                value += entropy_coef * prob[j] * ((logit[j] - log_sum) + entropy) * inv_batch;
+            }
+            g[a] = value;
+        }
+        const float v = o[k];
+        const float error = v - ret[i];
+        float vgrad = error;
+        float vloss = 0.5f * error * error;
+        if (value_clip > 0.0f) {
+            const float delta = v - old_v[i];
+            const float cv = old_v[i] + fminf(value_clip, fmaxf(-value_clip, delta));
+            const float cerr = cv - ret[i];
+            const float closs = 0.5f * cerr * cerr;
+            if (closs > vloss) {
+                vloss = closs;
+                vgrad = fabsf(delta) <= value_clip ? cerr : 0.0f;
+            }
+        }
+        if (lane == 0) {
+            g[k] = value_coef * vgrad * inv_batch;
+            metric[warp][0] = -fminf(unclipped, clipped);
+            metric[warp][1] = vloss;
+            metric[warp][2] = entropy;
+            metric[warp][3] = (ratio - 1.0f) - log_ratio;
+            metric[warp][4] = fabsf(ratio - 1.0f) > clip ? 1.0f : 0.0f;
+            metric[warp][6] = legal_count > 1 ? 1.0f : 0.0f;
+            metric[warp][7] = legal_count > 1 ? entropy : 0.0f;
+        }
+    }
+    __syncthreads();
+    if (block_metrics != nullptr && threadIdx.x < ppo::kMetrics) {
+        double s = 0.0;
+        for (int w = 0; w < ppo::kWarps; ++w) s += metric[w][threadIdx.x];
+        block_metrics[static_cast<size_t>(blockIdx.x) * ppo::kMetrics + threadIdx.x] = s;
+    }
+}
+
+}  // namespace t8b
+
+using namespace t8b;
+
+struct t8b_rollout {
+    size_t envs = 0, horizon = 0, samples = 0;
+    int width = 0;
+    Buffer<float> observations, log_probs, values, rewards, next_values, advantages, returns, entropies;
+    Buffer<uint8_t> masks, terminated, truncated;
+    Buffer<uint32_t> mask_bits;
+    Buffer<int64_t> actions;
+    Buffer<int32_t> tables;
+    std::vector<uint8_t> entropy_recorded, bytes_current;
+    Buffer<double> partial, stats;
+    Buffer<float> discounted, return_samples;
+    uint64_t return_count = 0;
+    double return_mean = 0.0, return_variance = 1.0;
+    t8b_comm_t comm{};
+    bool comm_active() const { return comm.allreduce_sum_f64 != nullptr && comm.world_size > 1; }
+
+    // uint8 masks materialised from the packed ones for the reference view, when stale
+    void expand_masks(cudaStream_t stream) {
+        bool stale = false;
+        for (uint8_t b : bytes_current) stale = stale || b == 0;
+        if (!stale) return;
+        if (masks.size() == 0) masks.allocate(samples * 368);
+        k_expand<<<blocks(samples * 368, 256), 256, 0, stream>>>(mask_bits.data(), masks.data(), samples);
+        check(cudaGetLastError(), "expand masks");
+        std::fill(bytes_current.begin(), bytes_current.end(), 1);
+    }
+
+    // (sum, sum of squares) of values[0..n) in fixed order -> stats[0..1], then the global totals
+    void moments(const float* values, size_t n, cudaStream_t stream, void* raw_stream) {
+        const int grid = static_cast<int>(std::min<size_t>(1024, (n + 255) / 256));
+        k_moments<<<grid, 256, 0, stream>>>(values, n, partial.data());
+        k_pair_total<<<1, 32, 0, stream>>>(partial.data(), grid, stats.data());
+        k_set_count<<<1, 32, 0, stream>>>(stats.data(), static_cast<double>(n));
+        check(cudaGetLastError(), "moments");
+        if (comm_active()) comm.allreduce_sum_f64(stats.data(), 3, raw_stream, comm.user);
+    }
+};
+
+namespace {
+
+template <typename Body>
+int with_rollout(t8b_rollout* r, Body&& body) {
+    return guarded([&] {
+        if (r == nullptr) raise(T8B_EINVAL, "null rollout handle");
+        body(*r);
+    });
+}
+
+}  // namespace
+
+extern "C" {
+
+int t8b_rollout_create(size_t environments, size_t horizon, const t8b_actor_config_t* config, t8b_rollout** out) {
+    return guarded([&] {
+        if (out == nullptr || config == nullptr) raise(T8B_EINVAL, "null argument");
+        *out = nullptr;
+        if (environments == 0 || horizon == 0) raise(T8B_EINVAL, "rollout dimensions must be greater than zero");
+        auto r = std::make_unique<t8b_rollout>();
+        r->envs = environments;
+        r->horizon = horizon;
+        r->samples = environments * horizon;
+        r->width = config->observation_size;
+        const size_t n = r->samples;
+        r->observations.allocate(n * static_cast<size_t>(r->width));
+        r->mask_bits.allocate(n * 12);
+        r->actions.allocate(n);
+        r->log_probs.allocate(n);
+        r->values.allocate(n);
+        r->rewards.allocate(n);
+        r->terminated.allocate(n);
+        r->truncated.allocate(n);
+        r->next_values.allocate(n);
+        r->advantages.allocate(n);
+        r->returns.allocate(n);
+        r->tables.allocate(n);
+        r->entropies.allocate(n);
+        r->entropy_recorded.assign(horizon, 0);
+        r->bytes_current.assign(horizon, 0);
+        r->partial.allocate(2 * 1024);
+        r->stats.allocate(4);
+        r->discounted.allocate(environments);
+        r->return_samples.allocate(n);
+        *out = r.release();
+    });
+}
+
+int t8b_rollout_destroy(t8b_rollout* r) {
+    return guarded([&] {
+        if (r) cudaDeviceSynchronize();
+        delete r;
+    });
+}
+
+int t8b_rollout_device_view(const t8b_rollout* rc, t8b_rollout_view_t* out) {
+    t8b_rollout* r = const_cast<t8b_rollout*>(rc);
+    return with_rollout(r, [&](t8b_rollout& s) {
+        s.expand_masks(nullptr);
+        std::memset(out, 0, sizeof *out);
+        out->observations = s.observations.data();
+        out->action_masks = s.masks.data();
+        out->action_mask_bits = s.mask_bits.data();
+        out->actions = s.actions.data();
+        out->old_log_probabilities = s.log_probs.data();
+        out->old_values = s.values.data();
+        out->rewards = s.rewards.data();
+        out->terminated = s.terminated.data();
+        out->truncated = s.truncated.data();
+        out->next_values = s.next_values.data();
+        out->advantages = s.advantages.data();
+        out->returns = s.returns.data();
+        out->environment_count = s.envs;
+        out->horizon = s.horizon;
+        out->sample_count = s.samples;
+        out->feature_tables = s.tables.data();
+        bool all = true;
+        for (uint8_t v : s.entropy_recorded) all = all && v;
+        out->entropies = all ? s.entropies.data() : nullptr;
+    });
+}
+
+int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* observations, const uint8_t* masks,
+                                     const uint32_t* mask_bits, const int64_t* actions, const float* log_probabilities,
+                                     const float* values, void* stream, const int32_t* feature_tables,
+                                     const float* entropies) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (step >= s.horizon) raise(T8B_ERANGE, "rollout step exceeds horizon");
+        if (!observations || (!masks && !mask_bits) || !actions || !log_probabilities || !values) {
+            raise(T8B_EINVAL, "rollout device pointers cannot be null");
+        }
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const size_t at = step * s.envs;
+        const size_t n = s.envs;
+        check(cudaMemcpyAsync(s.observations.data() + at * s.width, observations, sizeof(float) * n * s.width,
+                              cudaMemcpyDeviceToDevice, st), "record observations");
+        if (mask_bits) {
+            check(cudaMemcpyAsync(s.mask_bits.data() + at * 12, mask_bits, sizeof(uint32_t) * n * 12,
+                                  cudaMemcpyDeviceToDevice, st), "record masks");
+        } else {
+            k_pack_masks<<<blocks(n * 12, 256), 256, 0, st>>>(masks, s.mask_bits.data() + at * 12, n);
+            check(cudaGetLastError(), "pack masks");
+        }
+        s.bytes_current[step] = 0;
+        check(cudaMemcpyAsync(s.actions.data() + at, actions, sizeof(int64_t) * n, cudaMemcpyDeviceToDevice, st), "actions");
+        check(cudaMemcpyAsync(s.log_probs.data() + at, log_probabilities, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "lp");
+        check(cudaMemcpyAsync(s.values.data() + at, values, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "values");
+        if (feature_tables) {
+            check(cudaMemcpyAsync(s.tables.data() + at, feature_tables, sizeof(int32_t) * n, cudaMemcpyDeviceToDevice, st), "tables");
+        } else {
+            check(cudaMemsetAsync(s.tables.data() + at, 0, sizeof(int32_t) * n, st), "tables");
+        }
+        s.entropy_recorded[step] = entropies != nullptr;
+        if (entropies) {
+            check(cudaMemcpyAsync(s.entropies.data() + at, entropies, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "entropies");
+        }
+    });
+}
+
+int t8b_rollout_record_outcome_device(t8b_rollout* r, size_t step, const float* rewards, const uint8_t* terminated,
+                                      const uint8_t* truncated, const float* next_values, float reward_scale,
+                                      void* stream) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (step >= s.horizon) raise(T8B_ERANGE, "rollout step exceeds horizon");
+        if (!rewards || !terminated || !truncated || !next_values) raise(T8B_EINVAL, "outcome device pointers cannot be null");
+        if (!std::isfinite(reward_scale) || reward_scale <= 0.0f) raise(T8B_EINVAL, "reward scale must be finite and positive");
+        const size_t at = step * s.envs;
+        k_record_outcome<<<blocks(s.envs, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+            s.rewards.data() + at, s.terminated.data() + at, s.truncated.data() + at, s.next_values.data() + at, rewards,
+            terminated, truncated, next_values, reward_scale, s.envs);
+        check(cudaGetLastError(), "record outcome");
+    });
+}
+
+int t8b_rollout_compute_gae(t8b_rollout* r, float gamma, float gae_lambda, int normalize, void* stream) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (!std::isfinite(gamma) || !std::isfinite(gae_lambda) ||
+            !(gamma >= 0.0f && gamma <= 1.0f && gae_lambda >= 0.0f && gae_lambda <= 1.0f)) {
+            raise(T8B_EINVAL, "gamma and gae_lambda must be in [0, 1]");
+        }
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const unsigned grid = blocks(s.envs, kGaeThreads);
+        if (s.partial.size() < 2 * static_cast<size_t>(grid)) s.partial.allocate(2 * static_cast<size_t>(grid));
+        k_gae<<<grid, kGaeThreads, 0, st>>>(s.rewards.data(), s.values.data(), s.terminated.data(), s.truncated.data(),
+                                            s.next_values.data(), s.envs, s.horizon, gamma, gae_lambda, s.advantages.data(),
+                                            s.returns.data(), s.partial.data());
+        check(cudaGetLastError(), "GAE");
+        if (normalize) {
+            k_pair_total<<<1, 32, 0, st>>>(s.partial.data(), static_cast<int>(grid), s.stats.data());
+            k_set_count<<<1, 32, 0, st>>>(s.stats.data(), static_cast<double>(s.samples));
+            if (s.comm_active()) s.comm.allreduce_sum_f64(s.stats.data(), 3, stream, s.comm.user);
+            k_normalize<<<blocks(s.samples, 256), 256, 0, st>>>(s.advantages.data(), s.samples, s.stats.data());
+            check(cudaGetLastError(), "normalize advantages");
+        }
+    });
+}
+
+// normalize_rewards (src/ppo.cu:2365-2406)
+int t8b_rollout_normalize_rewards(t8b_rollout* r, float gamma, float clip, void* stream, float* std_out) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (!std::isfinite(gamma) || gamma < 0.0f || gamma > 1.0f) raise(T8B_EINVAL, "return normalization gamma must be in [0, 1]");
+        if (!std::isfinite(clip) || clip <= 0.0f) raise(T8B_EINVAL, "return normalization clip must be finite and positive");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        k_discounted<<<blocks(s.envs, 256), 256, 0, st>>>(s.rewards.data(), s.terminated.data(), s.truncated.data(), s.envs,
+                                                          s.horizon, gamma, s.discounted.data(), s.return_samples.data());
+        s.moments(s.return_samples.data(), s.samples, st, stream);
+        double sums[3];
+        s.stats.download(sums, 3, st);
+        const double batch_count = sums[2];
+        const double batch_mean = sums[0] / batch_count;
+        const double batch_m2 = std::max(0.0, sums[1] - sums[0] * batch_mean);
+        if (!std::isfinite(batch_mean) || !std::isfinite(batch_m2)) {
+            raise(T8B_ENONFINITE, "discounted returns became non-finite during return normalization");
+        }
+        const double running = static_cast<double>(s.return_count);
+        const double total = running + batch_count;
+        const double delta = batch_mean - s.return_mean;
+        s.return_variance = (s.return_variance * running + batch_m2 + delta * delta * running * batch_count / total) / total;
+        s.return_mean += delta * batch_count / total;
+        s.return_count += static_cast<uint64_t>(batch_count);
+        const float deviation = static_cast<float>(std::sqrt(s.return_variance + 1e-8));
+        k_scale_rewards<<<blocks(s.samples, 256), 256, 0, st>>>(s.rewards.data(), s.samples, 1.0f / deviation, clip);
+        check(cudaGetLastError(), "scale rewards");
+        if (std_out) *std_out = deviation;
+    });
+}
+
+int t8b_rollout_mean_reward(t8b_rollout* r, void* stream, double* out) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        s.moments(s.rewards.data(), s.samples, st, stream);
+        double sums[3];
+        s.stats.download(sums, 3, st);
+        *out = sums[0] / sums[2];
+    });
+}
+
+int t8b_rollout_return_normalizer_state(t8b_rollout* r, uint64_t* count, double* mean, double* variance,
+                                        float* discounted_returns) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (count) *count = s.return_count;
+        if (mean) *mean = s.return_mean;
+        if (variance) *variance = s.return_variance;
+        if (discounted_returns) s.discounted.download(discounted_returns, s.envs, nullptr);
+    });
+}
+
+int t8b_rollout_restore_return_normalizer_state(t8b_rollout* r, uint64_t count, double mean, double variance,
+                                                const float* discounted_returns) {
+    return with_rollout(r, [&](t8b_rollout& s) {
+        if (!std::isfinite(mean) || !std::isfinite(variance) || variance < 0.0) {
+            raise(T8B_EINVAL, "return normalizer state is invalid for this rollout buffer");
+        }
+        for (size_t i = 0; i < s.envs; ++i) {
+            if (!std::isfinite(discounted_returns[i])) raise(T8B_EINVAL, "return normalizer state is invalid for this rollout buffer");
+        }
+        s.discounted.upload(discounted_returns, s.envs, nullptr);
+        check(cudaStreamSynchronize(nullptr), "restore return normalizer");
+        s.return_count = count;
+        s.return_mean = mean;
+        s.return_variance = variance;
+    });
+}
+
+int t8b_rollout_set_comm(t8b_rollout* r, const t8b_comm_t* comm) {
+    return with_rollout(r, [&](t8b_rollout& s) { s.comm = comm ? *comm : t8b_comm_t{}; });
+}
+
+int t8b_rollout_synchronize(t8b_rollout* r, void* stream) {
+    return with_rollout(r, [&](t8b_rollout&) { check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "synchronize rollout"); });
+}
+
+int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const int64_t* actions,
+                            const float* old_log_probabilities, const float* old_values, const float* advantages,
+                            const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
+                            float* gradients, double* metric_sums, void* stream) {
+    return guarded([&] {
+        if (!outputs || !masks || !actions || !old_log_probabilities || !old_values || !advantages || !returns ||
+            !gradients || !config || n == 0) {
+            raise(T8B_EINVAL, "invalid PPO objective input");
+        }
+        if (action_count < 2 || action_count > 32 * kMaxLogitSlots) raise(T8B_EINVAL, "action_count must be 2..512");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const unsigned grid = blocks(n, ppo::kWarps);
+        Buffer<double> partial;
+        if (metric_sums) partial.allocate(static_cast<size_t>(grid) * ppo::kMetrics);
+        k_logit_objective<<<grid, 32 * ppo::kWarps, 0, st>>>(
+            outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
+            1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
+            config->entropy_coefficient, gradients, metric_sums ? partial.data() : nullptr);
+        check(cudaGetLastError(), "PPO objective");
+        if (metric_sums) {
+            ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(partial.data(), static_cast<int>(grid), ppo::kMetrics,
+                                                               metric_sums, 0);
+            check(cudaStreamSynchronize(st), "PPO objective metrics");
+        }
+    });
+}
+
+}  // extern "C"

@@ -231,3 +231,103 @@ def call(name: str, *args):
     status = getattr(lib(), name)(*args)
     if status != T8B_OK:
         raise T8bError(status, lib().t8b_last_error().decode())
+
+
+# ------------------------------------------------------------------ policy / rollout
+class ActorConfig(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("observation_size", "action_count", "hidden_size", "action_feature_size",
+                                          "universal_action_count", "shared_layers", "head_layers")] + \
+               [("observation_normalization", C.c_uint8), ("orthogonal_initialization", C.c_uint8),
+                ("pad", C.c_uint8 * 2), ("observation_clip", C.c_float), ("observation_epsilon", C.c_float),
+                ("matmul_precision", C.c_int32)]
+
+
+class PpoConfig(C.Structure):
+    _fields_ = [("epochs", C.c_int32), ("pad", C.c_int32), ("minibatch_size", C.c_uint64)] + \
+               [(n, C.c_float) for n in ("learning_rate", "clip_range", "value_clip_range", "target_kl",
+                                          "value_coefficient", "entropy_coefficient", "max_gradient_norm",
+                                          "adam_beta1", "adam_beta2", "adam_epsilon")]
+
+
+class PpoMetrics(C.Structure):
+    _fields_ = [(n, C.c_float) for n in ("policy_loss", "value_loss", "entropy", "approximate_kl", "clip_fraction",
+                                          "gradient_norm", "decision_fraction", "decision_entropy",
+                                          "rollout_decision_entropy", "pad")] + \
+               [("minibatches", C.c_uint64), ("epochs_completed", C.c_int32), ("early_stopped", C.c_int32)]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_ if name != "pad"}
+
+
+class PolicyOutput(C.Structure):
+    _fields_ = [("logits", C.c_void_p), ("actions", C.c_void_p), ("log_probabilities", C.c_void_p),
+                ("values", C.c_void_p), ("entropies", C.c_void_p), ("environment_count", C.c_size_t)]
+
+
+class RolloutView(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("observations", "action_masks", "actions", "old_log_probabilities",
+                                           "old_values", "rewards", "terminated", "truncated", "next_values",
+                                           "advantages", "returns")] + \
+               [("environment_count", C.c_size_t), ("horizon", C.c_size_t), ("sample_count", C.c_size_t),
+                ("feature_tables", C.c_void_p), ("entropies", C.c_void_p), ("action_mask_bits", C.c_void_p)]
+
+
+ALLREDUCE_F32 = C.CFUNCTYPE(None, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+ALLREDUCE_F64 = C.CFUNCTYPE(None, C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p)
+
+
+class Comm(C.Structure):
+    _fields_ = [("allreduce_sum_f32", ALLREDUCE_F32), ("allreduce_sum_f64", ALLREDUCE_F64), ("user", C.c_void_p),
+                ("world_size", C.c_int32), ("rank", C.c_int32)]
+
+
+SIZES.update({"t8b_actor_config_t": 44, "t8b_ppo_config_t": 56, "t8b_ppo_metrics_t": 56, "t8b_policy_output_t": 48,
+              "t8b_rollout_view_t": 136, "t8b_comm_t": 32})
+for _name, _cls in (("t8b_actor_config_t", ActorConfig), ("t8b_ppo_config_t", PpoConfig),
+                    ("t8b_ppo_metrics_t", PpoMetrics), ("t8b_policy_output_t", PolicyOutput),
+                    ("t8b_rollout_view_t", RolloutView), ("t8b_comm_t", Comm)):
+    assert C.sizeof(_cls) == SIZES[_name], (_name, C.sizeof(_cls))
+
+fp = C.POINTER(C.c_float)
+PROTOTYPES.update({
+    "t8b_debug_gemm": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+    "t8b_actor_config_default": (None, [C.POINTER(ActorConfig)]),
+    "t8b_ppo_config_default": (None, [C.POINTER(PpoConfig)]),
+    "t8b_policy_create": (C.c_int, [C.c_size_t, C.POINTER(ActorConfig), u64, C.POINTER(vp)]),
+    "t8b_policy_destroy": (C.c_int, [vp]),
+    "t8b_policy_capacity": (C.c_size_t, [vp]),
+    "t8b_policy_parameter_count": (C.c_size_t, [vp]),
+    "t8b_policy_action_feature_tables": (C.c_int, [vp]),
+    "t8b_policy_set_action_feature_tables": (C.c_int, [vp, vp, C.c_int, vp]),
+    "t8b_policy_forward": (C.c_int, [vp, vp, vp, vp, C.c_size_t, u64, u64, C.c_int, vp, vp, C.c_int,
+                                     C.POINTER(PolicyOutput)]),
+    "t8b_policy_update_ppo": (C.c_int, [vp, C.POINTER(RolloutView), C.POINTER(PpoConfig), u64, vp,
+                                        C.POINTER(PpoMetrics)]),
+    "t8b_policy_prepare_shuffle": (C.c_int, [vp, C.c_size_t, C.c_int, u64]),
+    "t8b_policy_set_comm": (C.c_int, [vp, C.POINTER(Comm)]),
+    "t8b_policy_get_parameters": (C.c_int, [vp, vp, C.c_size_t]),
+    "t8b_policy_set_parameters": (C.c_int, [vp, vp, C.c_size_t]),
+    "t8b_policy_get_gradients": (C.c_int, [vp, vp, C.c_size_t]),
+    "t8b_policy_get_optimizer_state": (C.c_int, [vp, vp, vp, C.POINTER(u64)]),
+    "t8b_policy_set_optimizer_state": (C.c_int, [vp, vp, vp, u64]),
+    "t8b_policy_get_observation_statistics": (C.c_int, [vp, vp, vp, C.POINTER(u64)]),
+    "t8b_policy_set_observation_statistics": (C.c_int, [vp, vp, vp, u64]),
+    "t8b_policy_download_outputs": (C.c_int, [vp, vp, C.c_size_t]),
+    "t8b_policy_synchronize": (C.c_int, [vp, vp]),
+    "t8b_policy_download_activation": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_size_t]),
+    "t8b_ppo_output_gradient": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_size_t, C.c_int, C.POINTER(PpoConfig),
+                                          vp, vp, vp]),
+    "t8b_rollout_create": (C.c_int, [C.c_size_t, C.c_size_t, C.POINTER(ActorConfig), C.POINTER(vp)]),
+    "t8b_rollout_destroy": (C.c_int, [vp]),
+    "t8b_rollout_device_view": (C.c_int, [vp, C.POINTER(RolloutView)]),
+    "t8b_rollout_record_policy_device": (C.c_int, [vp, C.c_size_t, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "t8b_rollout_record_outcome_device": (C.c_int, [vp, C.c_size_t, vp, vp, vp, vp, C.c_float, vp]),
+    "t8b_rollout_compute_gae": (C.c_int, [vp, C.c_float, C.c_float, C.c_int, vp]),
+    "t8b_rollout_normalize_rewards": (C.c_int, [vp, C.c_float, C.c_float, vp, fp]),
+    "t8b_rollout_mean_reward": (C.c_int, [vp, vp, C.POINTER(C.c_double)]),
+    "t8b_rollout_return_normalizer_state": (C.c_int, [vp, C.POINTER(u64), C.POINTER(C.c_double),
+                                                      C.POINTER(C.c_double), vp]),
+    "t8b_rollout_restore_return_normalizer_state": (C.c_int, [vp, u64, C.c_double, C.c_double, vp]),
+    "t8b_rollout_set_comm": (C.c_int, [vp, C.POINTER(Comm)]),
+    "t8b_rollout_synchronize": (C.c_int, [vp, vp]),
+})

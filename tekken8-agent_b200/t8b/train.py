@@ -1,0 +1,122 @@
+"""One self-play training iteration, as the reference trainer's hot loop runs it
+(src/full_move_train.cpp:1374-1414): a rollout of `horizon` decisions over every fight
+(policy forward -> record -> simulator step -> reset of finished rounds), return
+normalisation, GAE, then the PPO update.
+
+Two changes of schedule, neither of which changes what is learned:
+  * the critic's bootstrap value of a decision's successor state is the value the next
+    decision's forward pass computes anyway (the reference runs a second, deterministic forward
+    per step for it). For a fight whose round ended the successor value is the reset state's,
+    which GAE multiplies by zero (terminated and not truncated; the simulator never truncates),
+    so advantages and returns are identical; one forward per decision remains, plus one at the
+    end of the rollout for the last bootstrap;
+  * masks stay packed (12 words per fight) from the simulator through the rollout to the
+    update, and the update's permutations are drawn on a host thread while the rollout runs.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from .policy import GpuActorCritic, GpuRolloutBuffer, actor_config, ppo_config
+from .sim import GpuFullMoveSimulator, env_config
+
+
+def config4_env(**overrides):
+    """BASELINE config 4 / training.ini: screen-only observation with live noise (sigma 0.28 m,
+    detection errors 10 %, latency 2-6 frames), perception delay 12, 8-frame holds, and the
+    trainer's anti-stalling terms (src/train_launcher.cpp:106-160)."""
+    base = dict(screen_view=1, live_noise=1, noise_position_max=0.28, noise_flip_max=0.10, latency_min=2,
+                latency_max=6, perception_delay=12, hold_frames=8, draw_penalty=0.5, throw_break_penalty=0.03,
+                time_penalty_per_second=0.01, max_round_frames=3600)
+    base.update(overrides)
+    return env_config(**base)
+
+
+class SelfPlayTrainer:
+    def __init__(self, roster, environments=32768, horizon=128, epochs=4, minibatches=8, seed=3, hidden=512,
+                 layers=2, env=None, comm=None, rank=0, target_kl=0.0, scenario_share=0.25):
+        self.roster = roster
+        self.n = environments
+        self.horizon = horizon
+        self.epochs = epochs
+        self.seed = seed + rank
+        self.rank = rank
+        self.samples = environments * horizon
+        self.minibatch = self.samples // minibatches
+        self.sim = GpuFullMoveSimulator(roster, environments, env if env is not None else config4_env())
+        self.actor = actor_config(observation_size=self.sim.observation_size(), hidden_size=hidden,
+                                  shared_layers=layers)
+        self.policy = GpuActorCritic(max(environments, self.minibatch), self.actor, seed)  # identical init on every rank
+        self.policy.set_action_feature_tables(roster.feature_tables())
+        self.rollout = GpuRolloutBuffer(environments, horizon, self.actor)
+        if comm is not None:
+            self.policy.set_comm(comm)
+            self.rollout.set_comm(comm)
+        self.ppo = ppo_config(epochs=epochs, minibatch_size=self.minibatch, learning_rate=5e-4, target_kl=target_kl,
+                              entropy_coefficient=0.01)
+        rng = np.random.default_rng(self.seed)
+        count = len(roster)
+        self.sides = (np.arange(environments) % 2 == 0).astype(np.uint8)
+        self.learners = rng.integers(0, count, environments).astype(np.int32)
+        self.scenario_share = scenario_share
+        self.rng = rng
+        opponents, aggression, scenarios = self.schedule()
+        p1 = np.where(self.sides == 1, self.learners, opponents).astype(np.int32)
+        p2 = np.where(self.sides == 1, opponents, self.learners).astype(np.int32)
+        self.sim.set_matchups(p1, p2)
+        self.sim.set_learner_sides(self.sides)
+        self.sim.set_pending_opponents(opponents, aggression, scenarios)
+        self.sim.set_pending_learners(self.learners)
+        self.sim.reset_all(self.seed, 0)
+        self.update_index = 0
+        self.stream = None
+
+    def schedule(self):
+        """Uniform opponents over the roster, scripted aggression in [0, 1], a share of scenario
+        starts (src/full_move_train.cpp schedule_opponents)."""
+        rng = self.rng
+        opponents = rng.integers(0, len(self.roster), self.n).astype(np.int32)
+        aggression = rng.random(self.n).astype(np.float32)
+        scenarios = np.where(rng.random(self.n) < self.scenario_share, rng.integers(1, 9, self.n), 0).astype(np.int32)
+        return opponents, aggression, scenarios
+
+    def upload_schedule(self):
+        """Host -> device: the next rounds' opponents, aggression, scenarios and learners."""
+        opponents, aggression, scenarios = self.schedule()
+        self.sim.set_pending_opponents(opponents, aggression, scenarios)
+        self.sim.set_pending_learners(self.learners)
+        return 4 * 4 * self.n
+
+    def iterate(self):
+        """One update: rollout + return normalisation + GAE + PPO. Returns the PPO metrics."""
+        update = self.update_index = self.update_index + 1
+        t, n = self.horizon, self.n
+        self.policy.prepare_shuffle(self.samples, self.epochs, self.seed + update)
+        sim, policy, rollout = self.sim, self.policy, self.rollout
+        tables = sim.learner_feature_tables()
+        for step in range(t):
+            counter = update * t + step
+            obs, bits = sim.learner_observations(), sim.learner_mask_bits()
+            out = policy.forward(obs, None, n, self.seed + 1, counter, False, None, tables, mask_bits=bits)
+            if step > 0:
+                rollout.record_outcome_device(step - 1, sim.rewards(), sim.terminated(), sim.truncated(), out["values"])
+            rollout.record_policy_device(step, obs, None, out["actions"], out["log_probabilities"], out["values"],
+                                         None, tables, out["entropies"], mask_bits=bits)
+            sim.step(out["actions"], None, self.seed, counter + 1)
+            if step == t - 1:
+                last = policy.forward(sim.learner_observations(), None, n, self.seed + 3, counter, True, None, tables,
+                                      mask_bits=sim.learner_mask_bits())
+                rollout.record_outcome_device(step, sim.rewards(), sim.terminated(), sim.truncated(), last["values"])
+            sim.reset_done(self.seed, counter + 1)
+        rollout.normalize_rewards(0.99)
+        rollout.compute_gae(0.99, 0.95, True)
+        return policy.update_ppo(rollout.device_view(), self.ppo, self.seed + update)
+
+    def host_boundary(self):
+        """The per-update host traffic of the reference trainer (schedule upload, tally and
+        metric download): returns (bytes to device, bytes to host)."""
+        up = self.upload_schedule()
+        tally, scenario, learner, bot = self.sim.download_and_clear_tally()
+        down = tally.nbytes + scenario.nbytes + learner.nbytes + bot.nbytes
+        return up, down

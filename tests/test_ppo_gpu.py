@@ -1,0 +1,353 @@
+"""Policy, PPO update and rollout buffer against the numpy oracle (oracle/ppo_ref.py).
+
+Tolerances: network outputs and gradients go through bf16 tensor-core products with fp32
+accumulation, compared to float64 with a relative (norm) tolerance of 2e-2; the scorer,
+sampler, objective, GAE, normalisers and Adam are fp32 arithmetic compared at 1e-4 or tighter;
+GAE keeps the reference's own 2e-5 absolute bound (tests/rollout_tests.cpp:75-93)."""
+import numpy as np
+import pytest
+
+from oracle import ppo_ref as R
+
+pytestmark = pytest.mark.gpu
+
+
+def make_batch(n, features_tables, rng, width=151):
+    obs = rng.random((n, width)).astype(np.float32)
+    obs[:, 64:148] = 0.0
+    obs[np.arange(n), 64 + rng.integers(0, 41, n)] = 1.0
+    obs[np.arange(n), 106 + rng.integers(0, 41, n)] = 1.0
+    tables = rng.integers(0, features_tables, n).astype(np.int32)
+    masks = (rng.random((n, 368)) < 0.3).astype(np.uint8)
+    masks[:, 0] = 1
+    return obs, tables, masks
+
+
+def relative(a, b):
+    return float(np.linalg.norm(np.asarray(a, np.float64) - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def features(roster):
+    return roster.feature_tables()
+
+
+def oracle_params(policy):
+    cfg = policy.config
+    shapes = R.layout(cfg.observation_size, cfg.hidden_size, cfg.shared_layers, cfg.action_feature_size + 1)
+    return shapes, R.unflatten(policy.parameters().astype(np.float64), shapes)
+
+
+def test_initial_weights_are_orthogonal(cuda):
+    from t8b.policy import GpuActorCritic
+    policy = GpuActorCritic(256, seed=2027)
+    shapes, p = oracle_params(policy)
+    w1, w2, wo = p["w1"], p["w2"], p["w_out"]
+    assert np.allclose(w1.T @ w1, 2.0 * np.eye(151), atol=1e-4)  # tall: orthonormal columns, gain sqrt(2)
+    assert np.allclose(w2 @ w2.T, 2.0 * np.eye(512), atol=1e-4)
+    assert np.allclose(wo[32] @ wo[32], 1.0, atol=1e-5)  # value row keeps unit gain
+    assert np.allclose(np.abs(wo[:32]).max(), np.abs(wo[:32]).max(), atol=0) and np.abs(wo[:32]).max() < 0.01
+    assert all(np.all(p[f"b{i}"] == 0) for i in (1, 2)) and np.all(p["b_out"] == 0)
+
+
+def test_forward_matches_oracle(cuda, features):
+    import torch
+    from t8b.policy import GpuActorCritic
+    rng = np.random.default_rng(4)
+    n = 6000
+    policy = GpuActorCritic(8192, seed=7)
+    policy.set_action_feature_tables(features)
+    # non-trivial weights: scale the output layer up so scores spread
+    flat = policy.parameters()
+    shapes, p = oracle_params(policy)
+    p["w_out"] *= 30.0
+    p["b1"] = rng.normal(scale=0.1, size=p["b1"].shape)
+    policy.set_parameters(R.flatten(p, shapes).astype(np.float32))
+    obs, tables, masks = make_batch(n, features.shape[0], rng)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    out = policy.forward(d(obs), d(masks), n, seed=11, step=3, deterministic=True, tables=d(tables), want_logits=True)
+    got = policy.outputs(n)
+    _, want = R.forward(obs.astype(np.float64), p, 2)
+    assert relative(got, want) < 2e-2
+    # scorer + sampler against the GPU's own network outputs (fp32 path only)
+    q, v = got[:, :32].astype(np.float64), got[:, 32]
+    logits = R.parametric_scores(q, features.astype(np.float64), tables)
+    assert np.allclose(out["logits"].cpu().numpy(), logits, atol=1e-5, rtol=1e-4)
+    lp, prob, legal = R.log_softmax_masked(logits, masks)
+    best = np.argmax(np.where(legal, logits, -np.inf), axis=1)
+    assert np.array_equal(out["actions"].cpu().numpy(), best)
+    assert np.allclose(out["log_probabilities"].cpu().numpy(), lp[np.arange(n), best], atol=1e-4)
+    assert np.allclose(out["entropies"].cpu().numpy(), R.entropy(lp, prob), atol=1e-4)
+    assert np.array_equal(out["values"].cpu().numpy(), v)
+    # stochastic: inverse-CDF with the reference uniform; flips only at a CDF boundary
+    out = policy.forward(d(obs), d(masks), n, seed=11, step=3, deterministic=False, tables=d(tables))
+    actions = out["actions"].cpu().numpy()
+    agree = 0
+    for i in range(n):
+        u = float(R.uniform01(11, 3, i))
+        cdf = np.cumsum(prob[i])
+        want_i = int(np.searchsorted(cdf, u * cdf[-1]))
+        agree += int(actions[i] == want_i)
+    assert agree >= n - 3
+    assert np.all(masks[np.arange(n), actions] == 1)
+
+
+def test_bad_table_gives_nan_and_is_rejected(cuda, features):
+    import torch
+    from t8b.policy import GpuActorCritic
+    rng = np.random.default_rng(5)
+    policy = GpuActorCritic(256, seed=3)
+    policy.set_action_feature_tables(features)
+    obs, tables, masks = make_batch(64, features.shape[0], rng)
+    tables[5] = features.shape[0]
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    out = policy.forward(d(obs), d(masks), 64, tables=d(tables), deterministic=True)
+    vals = out["values"].cpu().numpy()
+    assert np.isnan(vals[5]) and np.all(np.isfinite(np.delete(vals, 5)))
+
+
+def test_multi_table_forward_equals_single_table(cuda, features):
+    """tests/feature_tables_tests.cpp: a sample scored against its table in a many-table policy
+    equals the same sample in a policy holding only that table."""
+    import torch
+    from t8b.policy import GpuActorCritic
+    rng = np.random.default_rng(6)
+    obs, tables, masks = make_batch(512, features.shape[0], rng)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    many = GpuActorCritic(512, seed=9)
+    many.set_action_feature_tables(features)
+    a = many.forward(d(obs), d(masks), 512, tables=d(tables), deterministic=True, want_logits=True)
+    logits_many = a["logits"].cpu().numpy().copy()
+    one = GpuActorCritic(512, seed=9)
+    one.set_action_feature_tables(features[7:8])
+    b = one.forward(d(obs), d(masks), 512, tables=d(np.zeros(512, np.int32)), deterministic=True, want_logits=True)
+    rows = tables == 7
+    assert np.array_equal(logits_many[rows], b["logits"].cpu().numpy()[rows])
+
+
+def rollout_inputs(policy, features, n, rng):
+    import torch
+    obs, tables, masks = make_batch(n, features.shape[0], rng)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    out = policy.forward(d(obs), d(masks), n, seed=1, step=0, tables=d(tables))
+    actions = out["actions"].cpu().numpy()
+    old_lp = out["log_probabilities"].cpu().numpy() - rng.normal(scale=0.05, size=n).astype(np.float32)
+    old_v = out["values"].cpu().numpy()
+    adv = rng.normal(size=n).astype(np.float32)
+    ret = (old_v + rng.normal(scale=0.5, size=n)).astype(np.float32)
+    return obs, tables, masks, actions, old_lp, old_v, adv, ret
+
+
+def view_of(arrays):
+    import torch
+    from t8b._lib import RolloutView
+    obs, tables, masks, actions, old_lp, old_v, adv, ret = arrays
+    keep = [torch.as_tensor(a, device="cuda") for a in (obs, masks, actions.astype(np.int64), old_lp, old_v, adv, ret,
+                                                         tables)]
+    v = RolloutView()
+    v.observations, v.action_masks, v.actions, v.old_log_probabilities, v.old_values, v.advantages, v.returns, \
+        v.feature_tables = [t.data_ptr() for t in keep]
+    v.sample_count = obs.shape[0]
+    v.environment_count = obs.shape[0]
+    v.horizon = 1
+    return v, keep
+
+
+def run_update(features, arrays, n, seed=12, scale_out=30.0, lr=1e-3):
+    from t8b.policy import GpuActorCritic, ppo_config
+    policy = GpuActorCritic(n, seed=seed)
+    policy.set_action_feature_tables(features)
+    shapes, p = oracle_params(policy)
+    p["w_out"] *= scale_out
+    policy.set_parameters(R.flatten(p, shapes).astype(np.float32))
+    before = policy.parameters()
+    if arrays is None:
+        arrays = rollout_inputs(policy, features, n, np.random.default_rng(8))
+    view, keep = view_of(arrays)
+    cfg = ppo_config(epochs=1, minibatch_size=n, learning_rate=lr, target_kl=0.0, entropy_coefficient=0.01)
+    metrics = policy.update_ppo(view, cfg, shuffle_seed=5)
+    return policy, shapes, before, arrays, metrics
+
+
+def gathered_order(policy, obs, n):
+    """The update's sample order, recovered by matching its bf16 layer-1 rows to the inputs."""
+    import torch
+    xg = policy.activation(0, 0, n)[:, :obs.shape[1]]
+    keyed = {torch.tensor(obs[i]).to(torch.bfloat16).float().numpy().tobytes(): i for i in range(n)}
+    return np.array([keyed[xg[j].astype(np.float32).tobytes()] for j in range(n)]), xg.astype(np.float64)
+
+
+def test_update_stages_match_oracle(cuda, features):
+    """Every stage of a minibatch update against float64 recomputed from that stage's own inputs:
+    forward activations and backward pre-activation gradients within bf16 rounding (1e-2), the
+    fused objective within 1e-2 of float64 on the GPU's network outputs, the weight-gradient GEMMs
+    within 1e-5 of their operands (bias gradients, summed from fp32 values before the bf16 rows
+    are stored, within 1e-2 of the stored rows' sums), and the metrics equal to the oracle's."""
+    n = 8192
+    policy, shapes, before, arrays, metrics = run_update(features, None, n)
+    obs, tables, masks, actions, old_lp, old_v, adv, ret = arrays
+    params = R.unflatten(before.astype(np.float64), shapes)
+    got = R.unflatten(policy.gradients().astype(np.float64), shapes)
+    order, xg = gathered_order(policy, obs, n)
+    a = {key: policy.activation(*key, n).astype(np.float64) for key in ((1, 0), (1, 1), (2, 0), (2, 1))}
+    dg = policy.activation(3, 0, n)[:, :33].astype(np.float64)
+    o = policy.outputs(n).astype(np.float64)
+    assert relative(a[(1, 0)], np.tanh(xg @ params["w1"].T + params["b1"])) < 1e-2
+    assert relative(a[(1, 1)], np.tanh(a[(1, 0)] @ params["w2"].T + params["b2"])) < 1e-2
+    assert relative(o, np.concatenate([a[(1, 1)] @ params["w_out"].T + params["b_out"]], 1)) < 1e-2
+    lg = R.parametric_scores(o[:, :32], features.astype(np.float64), tables[order])
+    g, dv, m = R.objective_gradient(lg, masks[order], actions[order], old_lp[order], old_v[order], adv[order],
+                                    ret[order], o[:, 32], 0.2, 0.2, 0.5, 0.01, n)
+    want_dout = np.concatenate([R.query_gradient(g, features.astype(np.float64), tables[order]), dv[:, None]], 1)
+    assert relative(dg, want_dout) < 1e-2
+    assert relative(a[(2, 1)], (dg @ params["w_out"]) * (1 - a[(1, 1)] ** 2)) < 1e-2
+    assert relative(a[(2, 0)], (a[(2, 1)] @ params["w2"]) * (1 - a[(1, 0)] ** 2)) < 1e-2
+    assert relative(got["w_out"], dg.T @ a[(1, 1)]) < 1e-5
+    assert relative(got["b_out"], dg.sum(0)) < 1e-2  # fp32 sums before bf16 storage
+    assert relative(got["w2"], a[(2, 1)].T @ a[(1, 0)]) < 1e-5
+    assert relative(got["b2"], a[(2, 1)].sum(0)) < 1e-2  # fp32 sums before bf16 storage
+    assert relative(got["w1"], a[(2, 0)].T @ xg) < 1e-5
+    assert relative(got["b1"], a[(2, 0)].sum(0)) < 1e-2  # fp32 sums before bf16 storage
+    for key, name in (("policy_loss", "policy_loss"), ("value_loss", "value_loss"), ("entropy", "entropy"),
+                      ("approximate_kl", "kl"), ("clip_fraction", "clip"), ("decision_fraction", "decision")):
+        assert abs(metrics[key] - m[name].mean()) <= 1e-4 * max(1.0, abs(m[name].mean())), key
+
+
+def test_update_gradient_and_adam_end_to_end(cuda, features):
+    """A well-conditioned minibatch (eight distinct samples, each repeated) so the batch gradient
+    does not cancel: the whole update's gradient within 3e-2 of float64, and Adam exact in fp32."""
+    import torch
+    from t8b.policy import GpuActorCritic
+    rng = np.random.default_rng(13)
+    n, distinct = 8192, 8
+    probe = GpuActorCritic(n, seed=12)
+    probe.set_action_feature_tables(features)
+    base = rollout_inputs(probe, features, distinct, rng)
+    reps = n // distinct
+    arrays = [np.repeat(a, reps, axis=0) for a in base]
+    arrays[0] = arrays[0] + (np.arange(n) % reps)[:, None].astype(np.float32) * 1e-3 * (np.arange(151) == 7)
+    arrays[6] = arrays[6] + 0.3  # returns above the values: a coherent value gradient
+    arrays[5] = np.abs(arrays[5]) + 0.5
+    policy, shapes, before, arrays, metrics = run_update(features, arrays, n)
+    obs, tables, masks, actions, old_lp, old_v, adv, ret = arrays
+    params = R.unflatten(before.astype(np.float64), shapes)
+    x = obs.astype(np.float64)
+    hs, out = R.forward(x, params, 2)
+    logits = R.parametric_scores(out[:, :32], features.astype(np.float64), tables)
+    g, dv, m = R.objective_gradient(logits, masks, actions, old_lp, old_v, adv, ret, out[:, 32], 0.2, 0.2, 0.5, 0.01, n)
+    dout = np.concatenate([R.query_gradient(g, features.astype(np.float64), tables), dv[:, None]], axis=1)
+    want = R.backward(x, hs, params, dout, 2)
+    grads = policy.gradients()
+    got = R.unflatten(grads.astype(np.float64), shapes)
+    errors = {name: relative(got[name], want[name]) for name, _ in shapes}
+    assert all(e < 3e-2 for e in errors.values()), errors
+    after = policy.parameters()
+    m1, m2, step = policy.optimizer_state()
+    want_p, want_m, want_v, norm = R.adam(before, grads, np.zeros_like(before), np.zeros_like(before), 1, 1e-3, 0.9,
+                                          0.999, 1e-5, 0.5)
+    assert step == 1
+    assert abs(metrics["gradient_norm"] - norm) <= 1e-5 * norm
+    assert np.allclose(after, want_p, rtol=1e-5, atol=1e-7)
+    assert np.allclose(m1, want_m, rtol=1e-5, atol=1e-9)
+    assert np.allclose(m2, want_v, rtol=1e-5, atol=1e-12)
+
+
+def test_update_is_bit_reproducible(cuda, features):
+    from t8b.policy import GpuActorCritic, ppo_config
+    rng = np.random.default_rng(9)
+    n = 4096
+    results = []
+    for _ in range(2):
+        policy = GpuActorCritic(n, seed=21)
+        policy.set_action_feature_tables(features)
+        arrays = rollout_inputs(policy, features, n, np.random.default_rng(9))
+        view, keep = view_of(arrays)
+        cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0)
+        policy.update_ppo(view, cfg, shuffle_seed=77)
+        results.append(policy.parameters())
+    assert np.array_equal(results[0], results[1])
+
+
+def test_observation_normalizer_merges_like_the_reference(cuda, features):
+    from t8b.policy import GpuActorCritic, ppo_config
+    rng = np.random.default_rng(10)
+    n = 4096
+    policy = GpuActorCritic(n, seed=22)
+    policy.set_action_feature_tables(features)
+    arrays = rollout_inputs(policy, features, n, rng)
+    view, keep = view_of(arrays)
+    policy.update_ppo(view, ppo_config(epochs=1, minibatch_size=n, target_kl=0.0), shuffle_seed=1)
+    mean, var, count = policy.observation_statistics()
+    c, mu, v = R.merge_moments(0, np.zeros(151), np.ones(151), arrays[0])
+    assert count == n
+    assert np.allclose(mean, mu, atol=1e-6) and np.allclose(var, v, rtol=1e-4, atol=1e-7)
+
+
+def test_gae_and_advantage_normalization_config2(cuda):
+    """BASELINE config 2 shapes: T = 128, N = 32,768."""
+    import torch
+    from t8b.policy import GpuRolloutBuffer
+    rng = np.random.default_rng(1)
+    t, n = 128, 32768
+    buf = GpuRolloutBuffer(n, t)
+    rewards = np.where(rng.random((t, n)) < 0.1, rng.normal(scale=0.1, size=(t, n)), 0.0).astype(np.float32)
+    done = rng.random((t, n)) < 1.0 / 600
+    rewards[done] = np.sign(rng.normal(size=done.sum()))
+    term = done.astype(np.uint8)
+    trunc = (done & (rng.random((t, n)) < 0.1)).astype(np.uint8)
+    values = rng.normal(size=(t, n)).astype(np.float32)
+    nv = rng.normal(size=(t, n)).astype(np.float32)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    obs = torch.zeros((n, 151), device="cuda")
+    masks = torch.ones((n, 368), dtype=torch.uint8, device="cuda")
+    acts = torch.zeros(n, dtype=torch.int64, device="cuda")
+    for s in range(t):
+        vals = d(values[s])
+        buf.record_policy_device(s, obs, masks, acts, vals, vals)
+        buf.record_outcome_device(s, d(rewards[s]), d(term[s]), d(trunc[s]), d(nv[s]))
+    buf.compute_gae(0.99, 0.95, normalize=False)
+    adv = buf.tensor("advantages").cpu().numpy()
+    ret = buf.tensor("returns").cpu().numpy()
+    want_adv, want_ret = R.gae(rewards, values, term, trunc, nv, 0.99, 0.95)
+    assert np.abs(adv - want_adv).max() < 2e-5
+    assert np.abs(ret - want_ret).max() < 2e-5
+    buf.compute_gae(0.99, 0.95, normalize=True)
+    norm = buf.tensor("advantages").cpu().numpy().astype(np.float64)
+    assert abs(norm.mean()) < 2e-4 and abs(norm.var() - 1.0) < 2e-3
+    assert np.allclose(norm, R.normalize_advantages(want_adv), atol=1e-4)
+    # return normaliser against the oracle
+    scale = buf.normalize_rewards(0.99)
+    samples, running = R.discounted_returns(rewards, term, trunc, np.zeros(n), 0.99)
+    _, _, var = R.merge_moments(0, 0.0, 1.0, samples.reshape(-1))
+    assert abs(scale - np.sqrt(var + 1e-8)) <= 1e-4 * scale
+    count, mean, variance, disc = buf.return_normalizer_state()
+    assert count == t * n and np.allclose(disc, running, atol=1e-4)
+
+
+def test_ppo_output_gradient_config2(cuda):
+    """The fused objective on raw logits (K = 256 slots, ~30 % legal) against float64."""
+    import torch
+    from t8b.policy import ppo_output_gradient, ppo_config
+    rng = np.random.default_rng(3)
+    n, k = 65536, 256
+    logits = rng.normal(size=(n, k + 1)).astype(np.float32)
+    masks = (rng.random((n, k)) < 0.3).astype(np.uint8)
+    masks[:100] = 0  # the all-masked fallback
+    legal = np.where(masks.any(1, keepdims=True), masks, np.eye(1, k, dtype=np.uint8))
+    actions = np.array([rng.choice(np.nonzero(m)[0]) for m in legal], np.int64)
+    old_lp = rng.normal(scale=0.1, size=n).astype(np.float32) - 3.0
+    old_v = rng.normal(size=n).astype(np.float32)
+    adv = rng.normal(size=n).astype(np.float32)
+    ret = rng.normal(size=n).astype(np.float32)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    cfg = ppo_config(entropy_coefficient=0.017)
+    grads, sums = ppo_output_gradient(d(logits), d(masks), d(actions), d(old_lp), d(old_v), d(adv), d(ret), cfg)
+    g, dv, m = R.objective_gradient(logits[:, :k].astype(np.float64), masks, actions, old_lp, old_v, adv, ret,
+                                    logits[:, k].astype(np.float64), 0.2, 0.2, 0.5, 0.017, n)
+    got = grads.cpu().numpy()
+    assert np.allclose(got[:, :k], g, rtol=1e-4, atol=1e-10)
+    assert np.allclose(got[:, k], dv, rtol=1e-5, atol=1e-12)
+    s = sums.cpu().numpy()
+    assert abs(s[0] - m["policy_loss"].sum()) <= 1e-4 * np.abs(m["policy_loss"]).sum()
+    assert abs(s[2] - m["entropy"].sum()) <= 1e-4 * m["entropy"].sum()
+    assert s[6] == m["decision"].sum()
