@@ -1,0 +1,257 @@
+#!/usr/bin/env python
+"""Benchmark of the self-play training hot path (scaled out as config 5).
+
+One step = one training iteration per GPU: a 128-decision rollout over 32,768 fights (policy
+forward, simulator decision, resets), return normalisation, GAE and the PPO update (4 epochs x 8
+minibatches of 524,288 samples). Metric: env-steps/s = fights x horizon x GPUs / iteration time
+(a step of an environment is one policy decision, src/full_move_train.cpp:1499).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+Under torchrun each rank drives one GPU with its own fights (seed offset by rank) and the
+gradient, KL and rollout statistics are summed over NCCL; rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import lzma
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "tekken8-agent_b200"))
+
+METRIC = "env-steps/s (sim+PPO, whole box) at 32,768 fights/GPU, 1/2/4/8 B200"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--envs", type=int, default=32768)
+    ap.add_argument("--horizon", type=int, default=128)
+    ap.add_argument("--epochs", type=int, default=4)
+    ap.add_argument("--minibatches", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def roster_raw():
+    return lzma.decompress((ROOT / "tests" / "golden" / "roster41.bin.xz").read_bytes())
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 8:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower() == "active"})
+        loaded = [s for s in sm if s > 0]
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def distributed():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data.get("hbm_gbs", 6650.0), data.get("bf16_tflops", 1590.0), data.get("bf16_tflops_sustained", 1400.0), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def cpu_baseline(args, features, env, sample_envs=2048, sample_horizon=16):
+    """The CPU leg on the host cores, on a bounded sample of the same workload."""
+    from oracle.cpu_iteration import CpuIteration
+    threads = os.cpu_count() or 1
+    it = CpuIteration(roster_raw(), features, env, sample_envs, sample_horizon, args.epochs, args.minibatches,
+                      threads=threads)
+    seconds = it.iterate()
+    value = sample_envs * sample_horizon / seconds
+    return {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": f"{sample_envs} fights x {sample_horizon} decisions, one iteration: the reference's CPU "
+                      f"environment contract (oracle/_ref, {threads} threads) + a float32 numpy port of the policy, "
+                      f"PPO objective, backward and Adam ({args.epochs} epochs x {args.minibatches} minibatches)"}
+
+
+def run_reference(args):
+    world, rank, local = distributed()
+    if rank != 0:
+        return
+    import numpy as np
+    from t8b import roster as roster_module
+    from t8b.train import config4_env
+    roster = roster_module.parse(roster_raw())
+    features = roster.feature_tables()
+    env = config4_env()
+    from oracle.cpu_iteration import CpuIteration
+    threads = os.cpu_count() or 1
+    sample_envs, sample_horizon = 2048, 16
+    it = CpuIteration(roster_raw(), features, env, sample_envs, sample_horizon, args.epochs, args.minibatches,
+                      threads=threads)
+    for _ in range(max(0, min(args.warmup, 1))):
+        it.iterate()
+    times = [it.iterate() for _ in range(args.steps)]
+    seconds = sum(times)
+    value = sample_envs * sample_horizon * args.steps / seconds
+    line = {"metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * seconds / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64 engine, f32 policy", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"self-play iteration, bounded CPU sample of config 4 ({sample_envs} fights x "
+                                   f"{sample_horizon} decisions per step)", "envs": sample_envs,
+                       "horizon": sample_horizon, "epochs": args.epochs, "minibatches": args.minibatches},
+            "cpu_baseline": {"value": value, "unit": "env-steps/s", "cores": threads, "kind": "port",
+                             "sample": f"{sample_envs} fights x {sample_horizon} decisions per step; the reference's "
+                                       f"CPU environment contract (oracle/_ref) + numpy port of the PPO math"},
+            "e2e": {"value": value, "unit": "env-steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    world, rank, local = distributed()
+    torch.cuda.set_device(local)
+    comm = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
+        from t8b.policy import TorchComm
+        comm = TorchComm()
+    from t8b import roster as roster_module
+    from t8b.train import SelfPlayTrainer
+    from t8b.sim import GpuFullMoveSimulator  # noqa: F401  (loads the library)
+    roster = roster_module.parse(roster_raw())
+    trainer = SelfPlayTrainer(roster, environments=args.envs, horizon=args.horizon, epochs=args.epochs,
+                              minibatches=args.minibatches, seed=3, comm=comm, rank=rank)
+    for _ in range(args.warmup):
+        trainer.host_boundary()
+        trainer.iterate()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    device_ms = []
+    rollout_ms = []
+    bytes_up = bytes_down = 0
+    frames_before = trainer.sim.frames_simulated()
+    with ClockSampler(local) as clocks:
+        wall0 = time.perf_counter()
+        for _ in range(args.steps):
+            up, down = trainer.host_boundary()
+            bytes_up += up
+            bytes_down += down
+            start, mid, end = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            start.record()
+            trainer.rollout_event = mid
+            metrics = trainer.iterate()
+            end.record()
+            end.synchronize()
+            device_ms.append(start.elapsed_time(end))
+            rollout_ms.append(start.elapsed_time(mid))
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        wall = time.perf_counter() - wall0
+    frames = trainer.sim.frames_simulated() - frames_before
+    total_device = sum(device_ms)
+    vals = torch.tensor([total_device, wall, sum(rollout_ms)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    total_device, wall, rollout_total = vals.tolist()
+    units = args.envs * args.horizon * world * args.steps
+    value = units / (total_device / 1000.0)
+    e2e = units / wall
+    peak_hbm, peak_bf16, peak_bf16_sustained, peak_kind = measured_peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_device / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64 engine, bf16 tensor-core policy (fp32 accumulate, fp32 master weights)",
+        "data": "synthetic (41-fighter roster tables from the reference loader; random-init policy)",
+        "config": {"workload": "config 4: self-play iteration, 32,768 fights/GPU, T=128, 4 epochs x 8 minibatches, "
+                               "screen view + live noise, scripted opponents",
+                   "envs_per_gpu": args.envs, "horizon": args.horizon, "epochs": args.epochs,
+                   "minibatch": args.envs * args.horizon // args.minibatches, "parallelism": f"dp{world}",
+                   "l2": "inputs larger than L2 (rollout buffers > 4 GB per GPU)", "target_kl": "off (full 4 epochs)"},
+        "phases_ms_per_step": {"rollout": rollout_total / args.steps,
+                               "gae_and_update": (total_device - rollout_total) / args.steps},
+        "engine_frames_per_s": frames / (total_device / 1000.0) * world,
+        "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": bytes_up // args.steps,
+                "d2h_bytes_per_step": bytes_down // args.steps},
+        "gpu_launches": None,
+        "clocks": clocks.summary(),
+        "last_metrics": {k: float(v) for k, v in metrics.items()},
+    }
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, roster.feature_tables(), trainer.sim.config)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

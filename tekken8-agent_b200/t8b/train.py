@@ -109,6 +109,9 @@ class SelfPlayTrainer:
                                       mask_bits=sim.learner_mask_bits())
                 rollout.record_outcome_device(step, sim.rewards(), sim.terminated(), sim.truncated(), last["values"])
             sim.reset_done(self.seed, counter + 1)
+        marker = getattr(self, "rollout_event", None)
+        if marker is not None:
+            marker.record()
         rollout.normalize_rewards(0.99)
         rollout.compute_gae(0.99, 0.95, True)
         return policy.update_ppo(rollout.device_view(), self.ppo, self.seed + update)
