@@ -411,6 +411,17 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
                             const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
                             float* gradients, double* metric_sums, void* stream);
 
+/* No counterpart in the reference. t8b_ppo_output_gradient without allocating device memory,
+ * for callers that cannot call cudaMalloc (a host whose memory manager owns the whole GPU, a
+ * loop that must not pay cudaMalloc/cudaFree's implicit device synchronisation mid-step). The
+ * metric partials use a static 4 MiB device array instead of a per-call buffer: at most 524,288
+ * samples per call (T8B_EINVAL beyond); the first call on a device looks the array up and should
+ * come before any stream capture; calls overlapping on the GPU race on the shared array. */
+int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, const int64_t* actions,
+                                   const float* old_log_probabilities, const float* old_values, const float* advantages,
+                                   const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
+                                   float* gradients, double* metric_sums, void* stream);
+
 /* ------------------------------------------------------------------ rollout buffer
  * class GpuRolloutBuffer (include/t8_v2/ppo.hpp:223-291). */
 typedef struct t8b_rollout t8b_rollout;

@@ -12,6 +12,7 @@
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <mutex>
 #include <vector>
 
 namespace t8b {
@@ -267,6 +268,30 @@ __global__ void k_logit_objective(const float* out, const uint8_t* masks, const 
         for (int w = 0; w < ppo::kWarps; ++w) s += metric[w][threadIdx.x];
         block_metrics[static_cast<size_t>(blockIdx.x) * ppo::kMetrics + threadIdx.x] = s;
     }
+}
+
+// Scratch of t8b_ppo_output_gradient_static: the per-block metric partials (8 doubles for each
+// block of 8 samples). One copy per device that loads the library, held until the process exits.
+constexpr size_t kStaticObjectiveSamples = 524288;
+constexpr size_t kStaticObjectiveBlocks = kStaticObjectiveSamples / ppo::kWarps;
+static __device__ __align__(256) double g_objective_scratch[kStaticObjectiveBlocks * ppo::kMetrics];  // 4 MiB
+
+// Device address of the scratch on the current device. The array's name is only a host-side
+// stand-in in host code, so the address is asked for once per device (with that device
+// current) and kept.
+double* objective_scratch() {
+    int device = 0;
+    check(cudaGetDevice(&device), "cudaGetDevice");
+    static std::mutex lock;
+    static double* addresses[128] = {};
+    if (device < 0 || device >= 128) raise(T8B_ECUDA, "device index out of range");
+    std::lock_guard<std::mutex> guard(lock);
+    if (addresses[device] == nullptr) {
+        void* pointer = nullptr;
+        check(cudaGetSymbolAddress(&pointer, g_objective_scratch), "cudaGetSymbolAddress of the objective scratch");
+        addresses[device] = static_cast<double*>(pointer);
+    }
+    return addresses[device];
 }
 
 }  // namespace t8b
@@ -566,6 +591,44 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
             ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(partial.data(), static_cast<int>(grid), ppo::kMetrics,
                                                                metric_sums, 0);
             check(cudaStreamSynchronize(st), "PPO objective metrics");
+        }
+    });
+}
+
+// The raw-logits PPO objective without allocating device memory, for callers that cannot call
+// cudaMalloc: a host whose memory manager owns all of the GPU's memory and forbids allocations
+// outside it, or a training loop that must not pay the device-wide synchronisation cudaMalloc
+// and cudaFree imply in the middle of a step. The per-block metric partials live in the static
+// 4 MiB device array above instead of a buffer allocated per call. The first call on a device
+// looks up the array's device address (cudaGetSymbolAddress); make that first call before any
+// stream capture. Every call shares the one array, so calls that overlap on the GPU (two
+// streams, two host threads) race on it; each call overwrites the partials it reads, so nothing
+// needs clearing between calls. At most 524,288 samples per call.
+int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, const int64_t* actions,
+                                   const float* old_log_probabilities, const float* old_values, const float* advantages,
+                                   const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
+                                   float* gradients, double* metric_sums, void* stream) {
+    return guarded([&] {
+        if (!outputs || !masks || !actions || !old_log_probabilities || !old_values || !advantages || !returns ||
+            !gradients || !config || n == 0) {
+            raise(T8B_EINVAL, "invalid PPO objective input");
+        }
+        if (n > kStaticObjectiveSamples) {
+            raise(T8B_EINVAL, "n exceeds the static scratch of this entry point (at most 524288 samples)");
+        }
+        if (action_count < 2 || action_count > 32 * kMaxLogitSlots) raise(T8B_EINVAL, "action_count must be 2..512");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        double* scratch = metric_sums ? objective_scratch() : nullptr;
+        const unsigned grid = blocks(n, ppo::kWarps);
+        k_logit_objective<<<grid, 32 * ppo::kWarps, 0, st>>>(
+            outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
+            1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
+            config->entropy_coefficient, gradients, scratch);
+        check(cudaGetLastError(), "PPO objective");
+        if (metric_sums) {
+            ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(scratch, static_cast<int>(grid), ppo::kMetrics,
+                                                               metric_sums, 0);
+            check(cudaGetLastError(), "PPO objective metrics");
         }
     });
 }

@@ -317,6 +317,8 @@ PROTOTYPES.update({
     "t8b_policy_download_activation": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_size_t]),
     "t8b_ppo_output_gradient": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_size_t, C.c_int, C.POINTER(PpoConfig),
                                           vp, vp, vp]),
+    "t8b_ppo_output_gradient_static": (C.c_int, [vp, vp, vp, vp, vp, vp, vp, C.c_size_t, C.c_int,
+                                                 C.POINTER(PpoConfig), vp, vp, vp]),
     "t8b_rollout_create": (C.c_int, [C.c_size_t, C.c_size_t, C.POINTER(ActorConfig), C.POINTER(vp)]),
     "t8b_rollout_destroy": (C.c_int, [vp]),
     "t8b_rollout_device_view": (C.c_int, [vp, C.POINTER(RolloutView)]),
