@@ -288,14 +288,24 @@ int t8b_sim_synchronize(t8b_sim* sim);
  * random legal candidate with a PCG32 stream (seed, stream = fight index); a finished
  * round restarts with next_round at the fight's start positions. hashes[fight*frames+f]
  * is the FNV-1a hash of the packed state after frame f. All pointers are device. */
+int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32_t* p2, const double* p1_x,
+                        const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done);
+
 /* Test hook for the tcgen05 GEMM (no reference counterpart): c[m][n] = sum_k a . b^T in fp32,
  * a bf16 [m][k] (or [k][m] when a_mn_major), b bf16 [n][k] (or [k][n]); bn is the tile width
  * (64, 192 or 256) and splits the split-K factor. All pointers are device. */
 int t8b_debug_gemm(const void* a, int a_mn_major, const void* b, int b_mn_major, float* c, int m, int n, int k,
                    int bn, int splits, void* stream);
 
-int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32_t* p2, const double* p1_x,
-                        const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done);
+/* Launch accounting (no reference counterpart). t8b_launch_count is the number of kernels the
+ * library has launched since it was loaded. t8b_profile_enable(1) clears earlier results and
+ * brackets every later launch with a pair of CUDA events on the launch's stream (0 stops);
+ * t8b_profile_report synchronises the device, adds the elapsed times up per kernel label and
+ * writes one "label launches total_ms" line per label into `text` (NUL-terminated, truncated
+ * to `capacity`); it returns the size the whole report needs. */
+uint64_t t8b_launch_count(void);
+void t8b_profile_enable(int on);
+size_t t8b_profile_report(char* text, size_t capacity);
 
 /* ------------------------------------------------------------------ policy and PPO
  * class GpuActorCritic (include/t8_v2/ppo.hpp:112-193). Every matrix product runs bf16 x bf16
@@ -428,6 +438,9 @@ typedef struct t8b_rollout t8b_rollout;
 int t8b_rollout_create(size_t environments, size_t horizon, const t8b_actor_config_t* config, t8b_rollout** out);
 int t8b_rollout_destroy(t8b_rollout* rollout);
 int t8b_rollout_device_view(const t8b_rollout* rollout, t8b_rollout_view_t* out); /* ppo.hpp:239 */
+/* The same view with packed masks only (action_masks NULL): no uint8 expansion (no reference
+ * counterpart; update_ppo reads action_mask_bits). */
+int t8b_rollout_packed_view(const t8b_rollout* rollout, t8b_rollout_view_t* out);
 /* record_policy_device  ppo.hpp:241-250 (uint8 masks), or packed masks with mask_bits. */
 int t8b_rollout_record_policy_device(t8b_rollout* rollout, size_t step, const float* observations, const uint8_t* masks,
                                      const uint32_t* mask_bits, const int64_t* actions, const float* log_probabilities,

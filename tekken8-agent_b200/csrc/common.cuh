@@ -11,6 +11,7 @@
 #include <utility>
 #include <vector>
 
+#include "launch.cuh"
 #include "t8b.h"
 
 namespace t8b {

@@ -37,9 +37,9 @@ void debug_gemm(const void* a, const void* b, float* c, int m, int n, int k, int
     const int used = splits < 1 ? 1 : (splits > k_blocks ? k_blocks : splits);
     Buffer<float> part(static_cast<size_t>(used) * m * n);
     Buffer<int> error(1);
-    gemm<BN, A_MN, B_MN>(oa, ob, used, error.data(), EpiPartial{part.data(), m, n}, stream);
+    gemm<BN, A_MN, B_MN>("gemm_debug", oa, ob, used, error.data(), EpiPartial{part.data(), m, n}, stream);
     const size_t count = static_cast<size_t>(m) * n;
-    k_reduce_splits<<<blocks(count, 256), 256, 0, stream>>>(part.data(), c, count, used);
+    launch("k_reduce_splits", k_reduce_splits, blocks(count, 256), 256, 0, stream, part.data(), c, count, used);
     check(cudaGetLastError(), "reduce splits");
     int flag = 0;
     error.download(&flag, 1, stream);

@@ -66,7 +66,7 @@ struct Operand {
 
 // C[m][n] = A . B^T over k, epilogue `epi`; `splits` partitions the k blocks (split-K).
 template <int BN, bool A_MN, bool B_MN, class Epi>
-void gemm(const Operand& a, const Operand& b, int splits, int* error, Epi epi, cudaStream_t stream) {
+void gemm(const char* label, const Operand& a, const Operand& b, int splits, int* error, Epi epi, cudaStream_t stream) {
     using L = tc::Layout<BN>;
     if (a.k != b.k || a.mn_major != A_MN || b.mn_major != B_MN) raise(T8B_EINVAL, "GEMM operand mismatch");
     tc::Shape s{};
@@ -88,7 +88,7 @@ void gemm(const Operand& a, const Operand& b, int splits, int* error, Epi epi, c
     }
     const int work = s.tiles_m * s.tiles_n * s.splits;
     const int grid = work < sm_count() ? work : sm_count();
-    kernel<<<grid, tc::kThreads, L::kSmemBytes, stream>>>(ma, mb, s, epi);
+    launch(label, kernel, grid, tc::kThreads, L::kSmemBytes, stream, ma, mb, s, epi);
     check(cudaGetLastError(), "GEMM launch");
 }
 

@@ -139,15 +139,15 @@ struct t8b_policy {
     int bn_hidden() const { return hidden % 256 == 0 ? 256 : 64; }
 
     void refresh_operands(cudaStream_t stream) {
-        ppo::k_adam<<<blocks(param_count, 256), 256, 0, stream>>>(params.data(), grads.data(), m1.data(), m2.data(),
+        launch("k_adam", ppo::k_adam, blocks(param_count, 256), 256, 0, stream, params.data(), grads.data(), m1.data(), m2.data(),
                                                                   param_count, norm_sq.data(), 1.0f, 0.0f, 0.9f, 0.999f,
                                                                   1e-5f, 1.0f, 1.0f, adam, 0);
         check(cudaGetLastError(), "refresh operand copies");
     }
 
     template <int BN, class Epi>
-    void dense(const Operand& a, const Operand& b, Epi epi, cudaStream_t stream, int splits = 1) {
-        gemm<BN, false, false>(a, b, splits, error.data(), epi, stream);
+    void dense(const char* label, const Operand& a, const Operand& b, Epi epi, cudaStream_t stream, int splits = 1) {
+        gemm<BN, false, false>(label, a, b, splits, error.data(), epi, stream);
     }
 
     // forward of the network on x[0..n) -> out [n][64]
@@ -157,11 +157,11 @@ struct t8b_policy {
             const Operand a = l == 0 ? Operand{x.data(), m, padded, padded, false} : Operand{h[l - 1].data(), m, hidden, hidden, false};
             const Operand b{w_bf[l].data(), hidden, a.k, a.k, false};
             const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data(), hidden, m};
-            if (bn_hidden() == 256) dense<256>(a, b, epi, stream); else dense<64>(a, b, epi, stream);
+            if (bn_hidden() == 256) dense<256>("gemm_forward_hidden", a, b, epi, stream); else dense<64>("gemm_forward_hidden", a, b, epi, stream);
         }
         const Operand a{h[layers - 1].data(), m, hidden, hidden, false};
         const Operand b{w_bf[layers].data(), kOutPad, hidden, hidden, false};
-        dense<64>(a, b, ppo::EpiBias{params.data() + b_off[layers], out.data(), kOutPad, m, outputs}, stream);
+        dense<64>("gemm_forward_output", a, b, ppo::EpiBias{params.data() + b_off[layers], out.data(), kOutPad, m, outputs}, stream);
     }
 
     int splits_for(int tiles) const {
@@ -178,10 +178,10 @@ struct t8b_policy {
             const Operand a{h[layers - 1].data(), hidden, m, hidden, true};
             const Operand b{dout.data(), kOutPad, m, kOutPad, true};
             const int splits = splits_for(hidden / tc::BM);
-            gemm<64, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, kOutPad}, stream);
+            gemm<64, true, true>("gemm_weight_grad", a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, kOutPad}, stream);
             const int k_blocks = (m + tc::BK - 1) / tc::BK;
             const int used = std::min(splits, k_blocks);
-            ppo::k_reduce_split<<<blocks(static_cast<size_t>(outputs) * hidden, 256), 256, 0, stream>>>(
+            launch("k_reduce_split", ppo::k_reduce_split, blocks(static_cast<size_t>(outputs) * hidden, 256), 256, 0, stream, 
                 split_part.data(), used, hidden, kOutPad, grads.data() + w_off[layers], outputs, hidden, 1);
         }
         // output layer input gradient through tanh of the top hidden layer
@@ -189,7 +189,7 @@ struct t8b_policy {
             const Operand a{dout.data(), m, kOutPad, kOutPad, false};
             const Operand b{wt_bf[layers].data(), hidden, kOutPad, kOutPad, false};
             const ppo::EpiTanhGrad epi{h[layers - 1].data(), dz[layers - 1].data(), colsum[layers - 1].data(), hidden, m};
-            if (bn_hidden() == 256) dense<256>(a, b, epi, stream); else dense<64>(a, b, epi, stream);
+            if (bn_hidden() == 256) dense<256>("gemm_input_grad", a, b, epi, stream); else dense<64>("gemm_input_grad", a, b, epi, stream);
         }
         for (int l = layers - 1; l >= 0; --l) {
             column_sums(colsum[l].data(), tiles_rows * 4, hidden, hidden, grads.data() + b_off[l], stream);
@@ -203,18 +203,18 @@ struct t8b_policy {
                 const int tiles = (hidden / tc::BM) * ((in_rows + 191) / 192);
                 const int splits = splits_for(tiles);
                 if (padded == 192) {
-                    gemm<192, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                    gemm<192, true, true>("gemm_weight_grad", a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
                 } else {
-                    gemm<64, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                    gemm<64, true, true>("gemm_weight_grad", a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
                 }
-                ppo::k_reduce_split<<<blocks(static_cast<size_t>(hidden) * width, 256), 256, 0, stream>>>(
+                launch("k_reduce_split", ppo::k_reduce_split, blocks(static_cast<size_t>(hidden) * width, 256), 256, 0, stream, 
                     split_part.data(), std::min(splits, k_blocks), hidden, in_rows, grads.data() + w_off[0], hidden, width, 0);
             } else {
                 const int tiles = (hidden / tc::BM) * (in_rows / 256);
                 const int splits = splits_for(tiles);
-                gemm<256, true, true>(a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
+                gemm<256, true, true>("gemm_weight_grad", a, b, splits, error.data(), ppo::EpiSplit{split_part.data(), hidden, in_rows}, stream);
                 const int cols = l == 0 ? width : hidden;
-                ppo::k_reduce_split<<<blocks(static_cast<size_t>(hidden) * cols, 256), 256, 0, stream>>>(
+                launch("k_reduce_split", ppo::k_reduce_split, blocks(static_cast<size_t>(hidden) * cols, 256), 256, 0, stream, 
                     split_part.data(), std::min(splits, k_blocks), hidden, in_rows, grads.data() + w_off[l], hidden, cols, 0);
             }
             if (l > 0) {
@@ -222,7 +222,7 @@ struct t8b_policy {
                 const Operand da{dz[l].data(), m, hidden, hidden, false};
                 const Operand db{wt_bf[l].data(), hidden, hidden, hidden, false};
                 const ppo::EpiTanhGrad epi{h[l - 1].data(), dz[l - 1].data(), colsum[l - 1].data(), hidden, m};
-                if (bn_hidden() == 256) dense<256>(da, db, epi, stream); else dense<64>(da, db, epi, stream);
+                if (bn_hidden() == 256) dense<256>("gemm_input_grad", da, db, epi, stream); else dense<64>("gemm_input_grad", da, db, epi, stream);
             }
         }
         check(cudaGetLastError(), "backward");
@@ -234,8 +234,8 @@ struct t8b_policy {
         const size_t need = static_cast<size_t>(ppo::kColumnChunks) * cols;
         if (column_scratch.size() < need) column_scratch.allocate(std::max<size_t>(need, ppo::kColumnChunks * 1024));
         dim3 grid((cols + 31) / 32, ppo::kColumnChunks);
-        ppo::k_column_partials<<<grid, dim3(32, 8), 0, stream>>>(in, rows, ld, cols, column_scratch.data());
-        ppo::k_reduce_columns<<<blocks(cols, 128), 128, 0, stream>>>(column_scratch.data(), ppo::kColumnChunks, cols, cols, grad);
+        launch("k_column_partials", ppo::k_column_partials, grid, dim3(32, 8), 0, stream, in, rows, ld, cols, column_scratch.data());
+        launch("k_reduce_columns", ppo::k_reduce_columns, blocks(cols, 128), 128, 0, stream, column_scratch.data(), ppo::kColumnChunks, cols, cols, grad);
         check(cudaGetLastError(), "column sums");
     }
 
@@ -502,7 +502,7 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
         const std::vector<float> zeros(p->width, 0.0f), ones(p->width, 1.0f);
         p->obs_mean.upload(zeros.data(), p->width, nullptr);
         p->obs_var.upload(ones.data(), p->width, nullptr);
-        ppo::k_refresh_istd<<<blocks(p->width, 128), 128>>>(p->obs_var.data(), p->obs_istd.data(), p->width,
+        launch("k_refresh_istd", ppo::k_refresh_istd, blocks(p->width, 128), 128, 0, nullptr, p->obs_var.data(), p->obs_istd.data(), p->width,
                                                            c.observation_epsilon);
         // initial weights: hidden layers, then the output layer, from one mt19937_64(seed)
         std::mt19937_64 random(seed);
@@ -574,7 +574,7 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         prep.normalize = s.normalizing() ? 1 : 0;
         prep.count = n;
         prep.x = s.x.data();
-        ppo::k_prep<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(prep);
+        launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
         check(cudaGetLastError(), "prepare inputs");
         s.network(n, st);
         ppo::Sample smp{};
@@ -595,7 +595,7 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         smp.log_probs = s.log_probs.data();
         smp.values = s.values.data();
         smp.entropies = s.entropies.data();
-        ppo::k_sample<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(smp);
+        launch("k_sample", ppo::k_sample, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
         check(cudaGetLastError(), "sample actions");
         if (out) {
             out->logits = want_logits ? s.logits.data() : nullptr;
@@ -655,7 +655,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         const size_t samples = r.sample_count;
         // validate_rollout_kernel (src/ppo.cu:423-451, 1545-1559)
         s.invalid.zero(st);
-        k_validate<<<blocks(samples, 256), 256, 0, st>>>(r.observations, s.width, r.action_masks, r.action_mask_bits,
+        launch("k_validate", k_validate, blocks(samples, 256), 256, 0, st, r.observations, s.width, r.action_masks, r.action_mask_bits,
                                                          r.actions, r.old_log_probabilities, r.old_values, r.advantages,
                                                          r.returns, samples, s.invalid.data());
         check(cudaGetLastError(), "validate rollout");
@@ -717,7 +717,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 prep.ret = s.mb_ret.data();
                 prep.src_tables = r.feature_tables;
                 prep.tables = s.mb_tables.data();
-                ppo::k_prep<<<blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st>>>(prep);
+                launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
                 check(cudaGetLastError(), "gather minibatch");
                 s.network(n, st);
                 ppo::Loss loss{};
@@ -748,9 +748,9 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 loss.perm = s.perm.data();
                 loss.offset = offset;
                 const unsigned loss_blocks = blocks(n, ppo::kWarps);
-                ppo::k_loss<<<loss_blocks, 32 * ppo::kWarps, 0, st>>>(loss);
+                launch("k_loss", ppo::k_loss, loss_blocks, 32 * ppo::kWarps, 0, st, loss);
                 check(cudaGetLastError(), "PPO objective");
-                ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(s.block_metrics.data(), static_cast<int>(loss_blocks),
+                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, s.block_metrics.data(), static_cast<int>(loss_blocks),
                                                                    ppo::kMetrics, s.metrics.data(), 1);
                 s.column_sums(s.out_colsum.data(), static_cast<int>(loss_blocks), kOutPad, s.outputs,
                               s.grads.data() + s.b_off[s.layers], st);
@@ -758,15 +758,15 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 if (s.comm.active()) {
                     // data parallel: the mean of the ranks' minibatch gradients, before the norm clip
                     s.comm.hooks.allreduce_sum_f32(s.grads.data(), s.param_count, stream, s.comm.hooks.user);
-                    ppo::k_scale<<<blocks(s.param_count, 256), 256, 0, st>>>(s.grads.data(), s.param_count,
+                    launch("k_scale", ppo::k_scale, blocks(s.param_count, 256), 256, 0, st, s.grads.data(), s.param_count,
                                                                               1.0f / static_cast<float>(s.comm.hooks.world_size));
                 }
-                ppo::k_square_partials<<<norm_blocks, 256, 0, st>>>(s.grads.data(), s.param_count, s.norm_partial.data());
-                ppo::k_norm_finish<<<1, 32, 0, st>>>(s.norm_partial.data(), norm_blocks, s.norm_sq.data(), s.metrics.data());
+                launch("k_square_partials", ppo::k_square_partials, norm_blocks, 256, 0, st, s.grads.data(), s.param_count, s.norm_partial.data());
+                launch("k_norm_finish", ppo::k_norm_finish, 1, 32, 0, st, s.norm_partial.data(), norm_blocks, s.norm_sq.data(), s.metrics.data());
                 ++s.optimizer_step;
                 const float bc1 = 1.0f - std::pow(cfg->adam_beta1, static_cast<float>(s.optimizer_step));
                 const float bc2 = 1.0f - std::pow(cfg->adam_beta2, static_cast<float>(s.optimizer_step));
-                ppo::k_adam<<<blocks(s.param_count, 256), 256, 0, st>>>(
+                launch("k_adam", ppo::k_adam, blocks(s.param_count, 256), 256, 0, st, 
                     s.params.data(), s.grads.data(), s.m1.data(), s.m2.data(), s.param_count, s.norm_sq.data(),
                     cfg->max_gradient_norm, cfg->learning_rate, cfg->adam_beta1, cfg->adam_beta2, cfg->adam_epsilon, bc1,
                     bc2, s.adam, 1);
@@ -802,8 +802,8 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
             const size_t chunks = (samples + chunk - 1) / chunk;
             if (s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
             dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((s.width + 31) / 32));
-            ppo::k_obs_moments<<<grid, 256, 0, st>>>(r.observations, samples, s.width, chunk, s.obs_chunks.data());
-            ppo::k_obs_merge<<<blocks(s.width, 128), 128, 0, st>>>(s.obs_chunks.data(), static_cast<int>(chunks), s.width,
+            launch("k_obs_moments", ppo::k_obs_moments, grid, 256, 0, st, r.observations, samples, s.width, chunk, s.obs_chunks.data());
+            launch("k_obs_merge", ppo::k_obs_merge, blocks(s.width, 128), 128, 0, st, s.obs_chunks.data(), static_cast<int>(chunks), s.width,
                                                                    static_cast<double>(s.obs_count), s.obs_mean.data(),
                                                                    s.obs_var.data(), s.obs_istd.data(),
                                                                    s.config.observation_epsilon, nullptr);
@@ -813,13 +813,13 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         // rollout decision entropy (src/ppo.cu:1671-1683)
         const int dblocks = 256;
         if (r.entropies) {
-            k_decision_partials<<<dblocks, 256, 0, st>>>(r.entropies, nullptr, r.action_mask_bits ? nullptr : r.action_masks,
+            launch("k_decision_partials", k_decision_partials, dblocks, 256, 0, st, r.entropies, nullptr, r.action_mask_bits ? nullptr : r.action_masks,
                                                         r.action_mask_bits, samples, s.entropy_sums.data());
         } else {
-            k_decision_partials<<<dblocks, 256, 0, st>>>(s.sample_entropy.data(), s.sample_decision.data(), nullptr, nullptr,
+            launch("k_decision_partials", k_decision_partials, dblocks, 256, 0, st, s.sample_entropy.data(), s.sample_decision.data(), nullptr, nullptr,
                                                         samples, s.entropy_sums.data());
         }
-        k_decision_finish<<<1, 32, 0, st>>>(s.entropy_sums.data(), dblocks, s.entropy_sums.data() + 2 * 1024);
+        launch("k_decision_finish", k_decision_finish, 1, 32, 0, st, s.entropy_sums.data(), dblocks, s.entropy_sums.data() + 2 * 1024);
         check(cudaGetLastError(), "decision entropy");
         double m[ppo::kMetrics];
         s.metrics.download(m, ppo::kMetrics, st);
@@ -902,7 +902,7 @@ int t8b_policy_set_observation_statistics(t8b_policy* p, const float* mean, cons
     return with_policy(p, [&](t8b_policy& s) {
         s.obs_mean.upload(mean, s.width, nullptr);
         s.obs_var.upload(variance, s.width, nullptr);
-        ppo::k_refresh_istd<<<blocks(s.width, 128), 128>>>(s.obs_var.data(), s.obs_istd.data(), s.width,
+        launch("k_refresh_istd", ppo::k_refresh_istd, blocks(s.width, 128), 128, 0, nullptr, s.obs_var.data(), s.obs_istd.data(), s.width,
                                                            s.config.observation_epsilon);
         check(cudaStreamSynchronize(nullptr), "set observation statistics");
         s.obs_count = count;

@@ -330,8 +330,40 @@ __device__ __forceinline__ float transpose_sum32(float* g, int lane) {
     return g[0];
 }
 
+// The legal candidates of one sample, ascending, compacted into `list` by ballots (12 words
+// held by every lane); returns how many. Nothing legal: candidate 0 alone (src/ppo.cu:254-258).
+__device__ __forceinline__ int compact_legal(const uint32_t* words, bool any, int lane, int16_t* list) {
+    int count = 0;
+    if (!any) {
+        if (lane == 0) list[0] = 0;
+        count = 1;
+    } else {
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const uint32_t bits = words[w];
+            if ((bits >> lane) & 1u) list[count + __popc(bits & ((1u << lane) - 1u))] = static_cast<int16_t>(w * 32 + lane);
+            count += __popc(bits);
+        }
+    }
+    __syncwarp();
+    return count;
+}
+
+// Position of candidate c in the compacted list.
+__device__ __forceinline__ int legal_rank(const uint32_t* words, bool any, int c) {
+    if (!any) return 0;
+    int rank = 0;
+#pragma unroll
+    for (int w = 0; w < kMaskWords; ++w) {
+        if (w < (c >> 5)) rank += __popc(words[w]);
+    }
+    return rank + __popc(words[(c >> 5) % kMaskWords] & ((1u << (c & 31)) - 1u));
+}
+
 __global__ void k_sample(Sample p) {
     __shared__ float qs[kWarps][64];
+    __shared__ int16_t lists[kWarps][kCandidates];
+    __shared__ float scores[kWarps][kCandidates];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
     if (i >= p.count) return;
@@ -350,78 +382,71 @@ __global__ void k_sample(Sample p) {
         words[w] = mask_word(p.bits, p.bytes, i, w, lane);
         any = any || words[w] != 0;
     }
-    float s[kMaskWords];
-    float best = -3.402823466e38f;
-    int best_at = kCandidates;
-#pragma unroll
-    for (int w = 0; w < kMaskWords; ++w) {
-        const int c = w * 32 + lane;
-        const bool legal = any ? ((words[w] >> lane) & 1u) != 0 : c == 0;
-        s[w] = 0.0f;
-        if (c < kCandidates && (legal || p.logits)) s[w] = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale);
-        if (p.logits && c < kCandidates) p.logits[i * kCandidates + c] = s[w];
-        if (legal && c < kCandidates && (s[w] > best || best_at == kCandidates)) {
-            best = s[w];
-            best_at = c;
+    if (p.logits) {
+        for (int c = lane; c < kCandidates; c += 32) {
+            p.logits[i * kCandidates + c] =
+                bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale);
         }
     }
-    // argmax: largest score, then the lowest candidate (the reference's first-seen maximum)
+    int16_t* list = lists[warp];
+    float* sc = scores[warp];
+    const int count = compact_legal(words, any, lane, list);
+    // scores of the legal candidates; argmax = largest score, then the lowest candidate
+    float best = -3.402823466e38f;
+    int best_j = kCandidates;
+    for (int j = lane; j < count; j += 32) {
+        const float s = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + list[j] * p.feature_size, p.feature_size, scale);
+        sc[j] = s;
+        if (s > best || best_j == kCandidates) {
+            best = s;
+            best_j = j;
+        }
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-        const int oa = __shfl_xor_sync(0xffffffffu, best_at, off);
-        if (ob > best || (ob == best && oa < best_at)) {
+        const int oj = __shfl_xor_sync(0xffffffffu, best_j, off);
+        if (ob > best || (ob == best && oj < best_j)) {
             best = ob;
-            best_at = oa;
+            best_j = oj;
         }
     }
+    __syncwarp();
     const float maximum = best;
-    float e[kMaskWords];
     float local = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMaskWords; ++w) {
-        const int c = w * 32 + lane;
-        const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-        e[w] = legal ? expf(s[w] - maximum) : 0.0f;
-        local += e[w];
-    }
+    for (int j = lane; j < count; j += 32) local += expf(sc[j] - maximum);
     const float sum = fmaxf(warp_sum(local), 1e-20f);
-    int selected = best_at;
+    int selected_j = best_j;
     if (!p.deterministic) {
+        // inverse CDF in candidate order (src/ppo.cu:271-284)
         const float target = uniform01(p.seed, p.step, i + p.lane_offset) * sum;
         float running = 0.0f;
         int found = -1;
-#pragma unroll
-        for (int w = 0; w < kMaskWords; ++w) {
-            float x = e[w];
+        for (int base = 0; base < count && found < 0; base += 32) {
+            const int j = base + lane;
+            const float e = j < count ? expf(sc[j] - maximum) : 0.0f;
+            float x = e;
 #pragma unroll
             for (int off = 1; off < 32; off <<= 1) {
                 const float y = __shfl_up_sync(0xffffffffu, x, off);
                 if (lane >= off) x += y;
             }
-            const float cumulative = running + x;
-            const uint32_t hit = __ballot_sync(0xffffffffu, found < 0 && e[w] > 0.0f && target <= cumulative);
-            if (found < 0 && hit) found = w * 32 + __ffs(hit) - 1;
+            const uint32_t hit = __ballot_sync(0xffffffffu, j < count && target <= running + x);
+            if (hit) found = base + __ffs(hit) - 1;
             running += __shfl_sync(0xffffffffu, x, 31);
         }
-        if (found >= 0) selected = found;
+        if (found >= 0) selected_j = found;
     }
     const float log_sum = logf(sum) + maximum;
     float entropy = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMaskWords; ++w) {
-        const int c = w * 32 + lane;
-        const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-        if (legal) {
-            const float lp = s[w] - log_sum;
-            entropy -= expf(lp) * lp;
-        }
+    for (int j = lane; j < count; j += 32) {
+        const float lp = sc[j] - log_sum;
+        entropy -= expf(lp) * lp;
     }
     entropy = warp_sum(entropy);
-    const float chosen = __shfl_sync(0xffffffffu, s[selected >> 5], selected & 31);
     if (lane == 0) {
-        p.actions[i] = selected;
-        p.log_probs[i] = chosen - log_sum;
+        p.actions[i] = list[selected_j];
+        p.log_probs[i] = sc[selected_j] - log_sum;
         p.values[i] = bad_table ? __int_as_float(0x7fc00000) : q[p.feature_size];
         p.entropies[i] = entropy;
     }
@@ -460,6 +485,8 @@ __global__ void k_loss(Loss p) {
     __shared__ float qs[kWarps][64];
     __shared__ float grads[kWarps][64];
     __shared__ float metric[kWarps][kMetrics];
+    __shared__ int16_t lists[kWarps][kCandidates];
+    __shared__ float scores[kWarps][kCandidates];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
     const bool live = i < p.count;
@@ -481,28 +508,23 @@ __global__ void k_loss(Loss p) {
             words[w] = p.bits[i * kMaskWords + w];
             any = any || words[w] != 0;
         }
-        float s[kMaskWords];
+        int16_t* list = lists[warp];
+        float* sc = scores[warp];
+        const int count = compact_legal(words, any, lane, list);
         float local_max = -3.402823466e38f;
-#pragma unroll
-        for (int w = 0; w < kMaskWords; ++w) {
-            const int c = w * 32 + lane;
-            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-            s[w] = legal ? (bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale)) : 0.0f;
-            if (legal) local_max = fmaxf(local_max, s[w]);
+        for (int j = lane; j < count; j += 32) {
+            const float s = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + list[j] * p.feature_size, p.feature_size, scale);
+            sc[j] = s;
+            local_max = fmaxf(local_max, s);
         }
         const float maximum = warp_max(local_max);
+        __syncwarp();
         float local = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kMaskWords; ++w) {
-            const int c = w * 32 + lane;
-            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-            if (legal) local += expf(s[w] - maximum);
-        }
+        for (int j = lane; j < count; j += 32) local += expf(sc[j] - maximum);
         const float sum = fmaxf(warp_sum(local), 1e-20f);
         const float log_sum = logf(sum) + maximum;
         const int selected = any ? p.actions[i] : 0;
-        const float chosen = __shfl_sync(0xffffffffu, s[(selected >> 5) % kMaskWords], selected & 31);
-        const float new_lp = chosen - log_sum;
+        const float new_lp = sc[legal_rank(words, any, selected)] - log_sum;
         const float log_ratio = new_lp - p.old_lp[i];
         const float ratio = expf(log_ratio);
         const float advantage = p.adv[i];
@@ -512,34 +534,22 @@ __global__ void k_loss(Loss p) {
         const float policy_loss = -fminf(unclipped, clipped);
         const float lp_grad = use_unclipped ? -advantage * ratio : 0.0f;
         float entropy = 0.0f;
-        int legal_count = 0;
-        float prob[kMaskWords], lps[kMaskWords];
-#pragma unroll
-        for (int w = 0; w < kMaskWords; ++w) {
-            const int c = w * 32 + lane;
-            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-            lps[w] = s[w] - log_sum;
-            prob[w] = legal ? expf(lps[w]) : 0.0f;
-            if (legal) {
-                entropy -= prob[w] * lps[w];
-                ++legal_count;
-            }
+        for (int j = lane; j < count; j += 32) {
+            const float lp = sc[j] - log_sum;
+            entropy -= expf(lp) * lp;
         }
         entropy = warp_sum(entropy);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) legal_count += __shfl_xor_sync(0xffffffffu, legal_count, o);
-        // d(objective)/d(score) for legal candidates, folded straight into d/dq
+        // d(objective)/d(score) of each legal candidate folded into d/dq
         float dq_local[kFeatures];
 #pragma unroll
         for (int f = 0; f < kFeatures; ++f) dq_local[f] = 0.0f;
-#pragma unroll
-        for (int w = 0; w < kMaskWords; ++w) {
-            const int c = w * 32 + lane;
-            const bool legal = c < kCandidates && (any ? ((words[w] >> lane) & 1u) != 0 : c == 0);
-            if (!legal) continue;
-            float g = (lp_grad * ((c == selected ? 1.0f : 0.0f) - prob[w])) * p.inv_batch;
-            g += p.entropy_coef * prob[w] * (lps[w] + entropy) * p.inv_batch;
-            if (!bad_table) {
+        if (!bad_table) {
+            for (int j = lane; j < count; j += 32) {
+                const int c = list[j];
+                const float lp = sc[j] - log_sum;
+                const float prob = expf(lp);
+                float g = (lp_grad * ((c == selected ? 1.0f : 0.0f) - prob)) * p.inv_batch;
+                g += p.entropy_coef * prob * (lp + entropy) * p.inv_batch;
                 const float4* f4 = reinterpret_cast<const float4*>(ftab + c * kFeatures);
 #pragma unroll
                 for (int k = 0; k < kFeatures / 4; ++k) {
@@ -574,12 +584,12 @@ __global__ void k_loss(Loss p) {
             metric[warp][2] = entropy;
             metric[warp][3] = (ratio - 1.0f) - log_ratio;
             metric[warp][4] = fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f;
-            metric[warp][6] = legal_count > 1 ? 1.0f : 0.0f;
-            metric[warp][7] = legal_count > 1 ? entropy : 0.0f;
+            metric[warp][6] = count > 1 ? 1.0f : 0.0f;
+            metric[warp][7] = count > 1 ? entropy : 0.0f;
             if (p.sample_entropy) {
                 const size_t sample = p.perm[p.offset + i];
                 p.sample_entropy[sample] = entropy;
-                p.sample_decision[sample] = legal_count > 1 ? 1 : 0;
+                p.sample_decision[sample] = count > 1 ? 1 : 0;
             }
         }
         __syncwarp();

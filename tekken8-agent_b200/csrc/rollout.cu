@@ -320,7 +320,7 @@ struct t8b_rollout {
         for (uint8_t b : bytes_current) stale = stale || b == 0;
         if (!stale) return;
         if (masks.size() == 0) masks.allocate(samples * 368);
-        k_expand<<<blocks(samples * 368, 256), 256, 0, stream>>>(mask_bits.data(), masks.data(), samples);
+        launch("k_expand", k_expand, blocks(samples * 368, 256), 256, 0, stream, mask_bits.data(), masks.data(), samples);
         check(cudaGetLastError(), "expand masks");
         std::fill(bytes_current.begin(), bytes_current.end(), 1);
     }
@@ -328,9 +328,9 @@ struct t8b_rollout {
     // (sum, sum of squares) of values[0..n) in fixed order -> stats[0..1], then the global totals
     void moments(const float* values, size_t n, cudaStream_t stream, void* raw_stream) {
         const int grid = static_cast<int>(std::min<size_t>(1024, (n + 255) / 256));
-        k_moments<<<grid, 256, 0, stream>>>(values, n, partial.data());
-        k_pair_total<<<1, 32, 0, stream>>>(partial.data(), grid, stats.data());
-        k_set_count<<<1, 32, 0, stream>>>(stats.data(), static_cast<double>(n));
+        launch("k_moments", k_moments, grid, 256, 0, stream, values, n, partial.data());
+        launch("k_pair_total", k_pair_total, 1, 32, 0, stream, partial.data(), grid, stats.data());
+        launch("k_set_count", k_set_count, 1, 32, 0, stream, stats.data(), static_cast<double>(n));
         check(cudaGetLastError(), "moments");
         if (comm_active()) comm.allreduce_sum_f64(stats.data(), 3, raw_stream, comm.user);
     }
@@ -391,13 +391,13 @@ int t8b_rollout_destroy(t8b_rollout* r) {
     });
 }
 
-int t8b_rollout_device_view(const t8b_rollout* rc, t8b_rollout_view_t* out) {
+static int rollout_view(const t8b_rollout* rc, t8b_rollout_view_t* out, bool bytes) {
     t8b_rollout* r = const_cast<t8b_rollout*>(rc);
     return with_rollout(r, [&](t8b_rollout& s) {
-        s.expand_masks(nullptr);
+        if (bytes) s.expand_masks(nullptr);
         std::memset(out, 0, sizeof *out);
         out->observations = s.observations.data();
-        out->action_masks = s.masks.data();
+        out->action_masks = bytes ? s.masks.data() : nullptr;
         out->action_mask_bits = s.mask_bits.data();
         out->actions = s.actions.data();
         out->old_log_probabilities = s.log_probs.data();
@@ -418,6 +418,9 @@ int t8b_rollout_device_view(const t8b_rollout* rc, t8b_rollout_view_t* out) {
     });
 }
 
+int t8b_rollout_device_view(const t8b_rollout* r, t8b_rollout_view_t* out) { return rollout_view(r, out, true); }
+int t8b_rollout_packed_view(const t8b_rollout* r, t8b_rollout_view_t* out) { return rollout_view(r, out, false); }
+
 int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* observations, const uint8_t* masks,
                                      const uint32_t* mask_bits, const int64_t* actions, const float* log_probabilities,
                                      const float* values, void* stream, const int32_t* feature_tables,
@@ -436,7 +439,7 @@ int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* o
             check(cudaMemcpyAsync(s.mask_bits.data() + at * 12, mask_bits, sizeof(uint32_t) * n * 12,
                                   cudaMemcpyDeviceToDevice, st), "record masks");
         } else {
-            k_pack_masks<<<blocks(n * 12, 256), 256, 0, st>>>(masks, s.mask_bits.data() + at * 12, n);
+            launch("k_pack_masks", k_pack_masks, blocks(n * 12, 256), 256, 0, st, masks, s.mask_bits.data() + at * 12, n);
             check(cudaGetLastError(), "pack masks");
         }
         s.bytes_current[step] = 0;
@@ -463,7 +466,7 @@ int t8b_rollout_record_outcome_device(t8b_rollout* r, size_t step, const float* 
         if (!rewards || !terminated || !truncated || !next_values) raise(T8B_EINVAL, "outcome device pointers cannot be null");
         if (!std::isfinite(reward_scale) || reward_scale <= 0.0f) raise(T8B_EINVAL, "reward scale must be finite and positive");
         const size_t at = step * s.envs;
-        k_record_outcome<<<blocks(s.envs, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        launch("k_record_outcome", k_record_outcome, blocks(s.envs, 256), 256, 0, static_cast<cudaStream_t>(stream), 
             s.rewards.data() + at, s.terminated.data() + at, s.truncated.data() + at, s.next_values.data() + at, rewards,
             terminated, truncated, next_values, reward_scale, s.envs);
         check(cudaGetLastError(), "record outcome");
@@ -479,15 +482,15 @@ int t8b_rollout_compute_gae(t8b_rollout* r, float gamma, float gae_lambda, int n
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         const unsigned grid = blocks(s.envs, kGaeThreads);
         if (s.partial.size() < 2 * static_cast<size_t>(grid)) s.partial.allocate(2 * static_cast<size_t>(grid));
-        k_gae<<<grid, kGaeThreads, 0, st>>>(s.rewards.data(), s.values.data(), s.terminated.data(), s.truncated.data(),
+        launch("k_gae", k_gae, grid, kGaeThreads, 0, st, s.rewards.data(), s.values.data(), s.terminated.data(), s.truncated.data(),
                                             s.next_values.data(), s.envs, s.horizon, gamma, gae_lambda, s.advantages.data(),
                                             s.returns.data(), s.partial.data());
         check(cudaGetLastError(), "GAE");
         if (normalize) {
-            k_pair_total<<<1, 32, 0, st>>>(s.partial.data(), static_cast<int>(grid), s.stats.data());
-            k_set_count<<<1, 32, 0, st>>>(s.stats.data(), static_cast<double>(s.samples));
+            launch("k_pair_total", k_pair_total, 1, 32, 0, st, s.partial.data(), static_cast<int>(grid), s.stats.data());
+            launch("k_set_count", k_set_count, 1, 32, 0, st, s.stats.data(), static_cast<double>(s.samples));
             if (s.comm_active()) s.comm.allreduce_sum_f64(s.stats.data(), 3, stream, s.comm.user);
-            k_normalize<<<blocks(s.samples, 256), 256, 0, st>>>(s.advantages.data(), s.samples, s.stats.data());
+            launch("k_normalize", k_normalize, blocks(s.samples, 256), 256, 0, st, s.advantages.data(), s.samples, s.stats.data());
             check(cudaGetLastError(), "normalize advantages");
         }
     });
@@ -499,7 +502,7 @@ int t8b_rollout_normalize_rewards(t8b_rollout* r, float gamma, float clip, void*
         if (!std::isfinite(gamma) || gamma < 0.0f || gamma > 1.0f) raise(T8B_EINVAL, "return normalization gamma must be in [0, 1]");
         if (!std::isfinite(clip) || clip <= 0.0f) raise(T8B_EINVAL, "return normalization clip must be finite and positive");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        k_discounted<<<blocks(s.envs, 256), 256, 0, st>>>(s.rewards.data(), s.terminated.data(), s.truncated.data(), s.envs,
+        launch("k_discounted", k_discounted, blocks(s.envs, 256), 256, 0, st, s.rewards.data(), s.terminated.data(), s.truncated.data(), s.envs,
                                                           s.horizon, gamma, s.discounted.data(), s.return_samples.data());
         s.moments(s.return_samples.data(), s.samples, st, stream);
         double sums[3];
@@ -517,7 +520,7 @@ int t8b_rollout_normalize_rewards(t8b_rollout* r, float gamma, float clip, void*
         s.return_mean += delta * batch_count / total;
         s.return_count += static_cast<uint64_t>(batch_count);
         const float deviation = static_cast<float>(std::sqrt(s.return_variance + 1e-8));
-        k_scale_rewards<<<blocks(s.samples, 256), 256, 0, st>>>(s.rewards.data(), s.samples, 1.0f / deviation, clip);
+        launch("k_scale_rewards", k_scale_rewards, blocks(s.samples, 256), 256, 0, st, s.rewards.data(), s.samples, 1.0f / deviation, clip);
         check(cudaGetLastError(), "scale rewards");
         if (std_out) *std_out = deviation;
     });
@@ -582,13 +585,13 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
         const unsigned grid = blocks(n, ppo::kWarps);
         Buffer<double> partial;
         if (metric_sums) partial.allocate(static_cast<size_t>(grid) * ppo::kMetrics);
-        k_logit_objective<<<grid, 32 * ppo::kWarps, 0, st>>>(
+        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st, 
             outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
             1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
             config->entropy_coefficient, gradients, metric_sums ? partial.data() : nullptr);
         check(cudaGetLastError(), "PPO objective");
         if (metric_sums) {
-            ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(partial.data(), static_cast<int>(grid), ppo::kMetrics,
+            launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, partial.data(), static_cast<int>(grid), ppo::kMetrics,
                                                                metric_sums, 0);
             check(cudaStreamSynchronize(st), "PPO objective metrics");
         }
@@ -620,13 +623,13 @@ int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, c
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         double* scratch = metric_sums ? objective_scratch() : nullptr;
         const unsigned grid = blocks(n, ppo::kWarps);
-        k_logit_objective<<<grid, 32 * ppo::kWarps, 0, st>>>(
+        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st, 
             outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
             1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
             config->entropy_coefficient, gradients, scratch);
         check(cudaGetLastError(), "PPO objective");
         if (metric_sums) {
-            ppo::k_sum_rows_f64<<<ppo::kMetrics, 256, 0, st>>>(scratch, static_cast<int>(grid), ppo::kMetrics,
+            launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, scratch, static_cast<int>(grid), ppo::kMetrics,
                                                                metric_sums, 0);
             check(cudaGetLastError(), "PPO objective metrics");
         }

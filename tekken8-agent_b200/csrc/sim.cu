@@ -697,7 +697,7 @@ struct t8b_sim {
 
     void masks(const uint8_t* only) {
         const unsigned warps_per_block = kMaskThreads / 32;
-        k_masks<<<blocks(2 * n, warps_per_block), kMaskThreads, smem(), stream>>>(view(), only);
+        launch("k_masks", k_masks, blocks(2 * n, warps_per_block), kMaskThreads, smem(), stream, view(), only);
         launched("candidate masks");
     }
     void check_characters(const int32_t* values, bool allow_keep, const char* what) const {
@@ -843,7 +843,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         const std::vector<double> left(n, -0.8), right(n, 0.8);
         sim->x1.upload(left.data(), n, s);
         sim->x2.upload(right.data(), n, s);
-        k_engine_reset<<<blocks(n, kStepThreads), kStepThreads, sim->smem(), s>>>(sim->view(), sim->x1.data(), sim->x2.data());
+        launch("k_engine_reset", k_engine_reset, blocks(n, kStepThreads), kStepThreads, sim->smem(), s, sim->view(), sim->x1.data(), sim->x2.data());
         sim->launched("initial reset");
         check(cudaStreamSynchronize(s), "create simulator");
         *out = sim.release();
@@ -879,7 +879,7 @@ int t8b_sim_reset_engine(t8b_sim* sim, const double* p1_x, const double* p2_x) {
     return with_sim(sim, [&](t8b_sim& s) {
         s.x1.upload(p1_x, s.n, s.stream);
         s.x2.upload(p2_x, s.n, s.stream);
-        k_engine_reset<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(s.view(), s.x1.data(), s.x2.data());
+        launch("k_engine_reset", k_engine_reset, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view(), s.x1.data(), s.x2.data());
         s.launched("engine reset");
         check(cudaStreamSynchronize(s.stream), "engine reset");
     });
@@ -895,7 +895,7 @@ int t8b_sim_step_engine(t8b_sim* sim, const t8b_input_t* inputs, const uint8_t* 
             s.x1.upload(p1_x, s.n, s.stream);
             s.x2.upload(p2_x, s.n, s.stream);
         }
-        k_engine_step<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(
+        launch("k_engine_step", k_engine_step, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, 
             s.view(), s.inputs.data(), rounds ? s.new_round.data() : nullptr, s.x1.data(), s.x2.data(), s.events.data());
         s.launched("engine step");
         check(cudaStreamSynchronize(s.stream), "engine step");
@@ -921,7 +921,7 @@ int t8b_sim_download_legal_mask(t8b_sim* sim, int player, uint8_t* out) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (player != 0 && player != 1) raise(T8B_ERANGE, "player must be 0 or 1");
         if (s.legal_bytes.size() == 0) s.legal_bytes.allocate(s.n * kMaxCandidates);
-        k_legal_mask<<<blocks(s.n * kMaxCandidates, 256), 256, s.smem(), s.stream>>>(s.view(), player, s.legal_bytes.data());
+        launch("k_legal_mask", k_legal_mask, blocks(s.n * kMaxCandidates, 256), 256, s.smem(), s.stream, s.view(), player, s.legal_bytes.data());
         s.launched("legal mask");
         s.legal_bytes.download(out, s.n * kMaxCandidates, s.stream);
     });
@@ -971,7 +971,7 @@ int t8b_sim_set_pending_learners(t8b_sim* sim, const int32_t* characters) {
 
 int t8b_sim_reset_all(t8b_sim* sim, uint64_t seed, uint64_t counter) {
     return with_sim(sim, [&](t8b_sim& s) {
-        k_reset<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(s.view(), nullptr, seed, counter);
+        launch("k_reset", k_reset, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view(), nullptr, seed, counter);
         s.launched("reset all");
         s.terminated.zero(s.stream);
         s.masks(nullptr);
@@ -980,7 +980,7 @@ int t8b_sim_reset_all(t8b_sim* sim, uint64_t seed, uint64_t counter) {
 
 int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter) {
     return with_sim(sim, [&](t8b_sim& s) {
-        k_reset<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(s.view(), s.terminated.data(), seed, counter);
+        launch("k_reset", k_reset, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view(), s.terminated.data(), seed, counter);
         s.launched("reset done");
         s.masks(s.terminated.data());
     });
@@ -989,7 +989,7 @@ int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter) {
 int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
-        k_step<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(s.view(), learner, opponent, seed, counter);
+        launch("k_step", k_step, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter);
         s.launched("step");
         s.masks(nullptr);
     });
@@ -1005,7 +1005,7 @@ static const uint8_t* expand(t8b_sim* sim, bool learner) {
     const int status = with_sim(sim, [&](t8b_sim& s) {
         Buffer<uint8_t>& bytes = learner ? s.learner_bytes : s.opponent_bytes;
         if (bytes.size() == 0) bytes.allocate(s.n * kMaxCandidates);
-        k_expand_masks<<<blocks(s.n * kMaxCandidates, 256), 256, 0, s.stream>>>(
+        launch("k_expand_masks", k_expand_masks, blocks(s.n * kMaxCandidates, 256), 256, 0, s.stream, 
             learner ? s.learner_bits.data() : s.opponent_bits.data(), bytes.data(), s.n);
         s.launched("expand masks");
         result = bytes.data();
@@ -1096,10 +1096,10 @@ int t8b_sim_restore(t8b_sim* sim, const t8b_state_t* states, const int32_t* p1, 
         s.pending_learners.upload(pending_learners, s.n, s.stream);
         s.terminated.upload(terminated, s.n, s.stream);
         if (s.config.live_noise) {
-            k_draw_noise<<<blocks(s.n, 256), 256, 0, s.stream>>>(s.view(), 0x5eedull);
+            launch("k_draw_noise", k_draw_noise, blocks(s.n, 256), 256, 0, s.stream, s.view(), 0x5eedull);
             s.launched("draw noise levels");
         }
-        k_observe<<<blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream>>>(s.view());
+        launch("k_observe", k_observe, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view());
         s.launched("observe");
         s.masks(nullptr);
         check(cudaStreamSynchronize(s.stream), "restore");
@@ -1114,7 +1114,7 @@ int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32
                         const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (fights <= 0 || frames <= 0 || !p1 || !p2 || !p1_x || !p2_x || !hashes) raise(T8B_EINVAL, "random play arguments");
-        k_random_play<<<blocks(static_cast<size_t>(fights), kStepThreads), kStepThreads, s.smem(), s.stream>>>(
+        launch("k_random_play", k_random_play, blocks(static_cast<size_t>(fights), kStepThreads), kStepThreads, s.smem(), s.stream, 
             s.view(), fights, p1, p2, p1_x, p2_x, frames, seed, hashes);
         s.launched("random play");
         if (frames_done != nullptr) *frames_done = static_cast<uint64_t>(fights) * static_cast<uint64_t>(frames);

@@ -1,14 +1,16 @@
 """ctypes binding of include/t8b.h: struct layouts, prototypes, status handling.
 
-The shared library is loaded from ../lib/libt8b.so (built in-tree by build.py). There is
-no fallback: importing this module without the library raises.
+The shared library is loaded from ../lib/libt8b.so (built in-tree by build.py), or from the
+path in the T8B_LIBRARY environment variable. There is no fallback: importing this module
+without the library raises.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent.parent / "lib" / "libt8b.so"
+LIB_PATH = Path(os.environ.get("T8B_LIBRARY") or Path(__file__).resolve().parent.parent / "lib" / "libt8b.so")
 
 T8B_OK, T8B_EINVAL, T8B_ERANGE, T8B_ECUDA, T8B_ENONFINITE, T8B_ESTATE = range(6)
 UNIVERSAL_COUNT, MAX_CANDIDATES, FEATURE_SIZE, ROSTER_SLOTS = 22, 368, 32, 42
@@ -291,6 +293,9 @@ for _name, _cls in (("t8b_actor_config_t", ActorConfig), ("t8b_ppo_config_t", Pp
 fp = C.POINTER(C.c_float)
 PROTOTYPES.update({
     "t8b_debug_gemm": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+    "t8b_launch_count": (u64, []),
+    "t8b_profile_enable": (None, [C.c_int]),
+    "t8b_profile_report": (C.c_size_t, [C.c_char_p, C.c_size_t]),
     "t8b_actor_config_default": (None, [C.POINTER(ActorConfig)]),
     "t8b_ppo_config_default": (None, [C.POINTER(PpoConfig)]),
     "t8b_policy_create": (C.c_int, [C.c_size_t, C.POINTER(ActorConfig), u64, C.POINTER(vp)]),
@@ -322,6 +327,7 @@ PROTOTYPES.update({
     "t8b_rollout_create": (C.c_int, [C.c_size_t, C.c_size_t, C.POINTER(ActorConfig), C.POINTER(vp)]),
     "t8b_rollout_destroy": (C.c_int, [vp]),
     "t8b_rollout_device_view": (C.c_int, [vp, C.POINTER(RolloutView)]),
+    "t8b_rollout_packed_view": (C.c_int, [vp, C.POINTER(RolloutView)]),
     "t8b_rollout_record_policy_device": (C.c_int, [vp, C.c_size_t, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "t8b_rollout_record_outcome_device": (C.c_int, [vp, C.c_size_t, vp, vp, vp, vp, C.c_float, vp]),
     "t8b_rollout_compute_gae": (C.c_int, [vp, C.c_float, C.c_float, C.c_int, vp]),

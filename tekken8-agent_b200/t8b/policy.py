@@ -206,9 +206,10 @@ class GpuRolloutBuffer:
         except Exception:
             pass
 
-    def device_view(self) -> RolloutView:
+    def device_view(self, packed: bool = False) -> RolloutView:
+        """GpuRolloutView; packed=True leaves the uint8 masks unexpanded (action_masks NULL)."""
         v = RolloutView()
-        call("t8b_rollout_device_view", self._handle, C.byref(v))
+        call("t8b_rollout_packed_view" if packed else "t8b_rollout_device_view", self._handle, C.byref(v))
         return v
 
     def record_policy_device(self, step, observations, masks=None, actions=None, log_probabilities=None, values=None,

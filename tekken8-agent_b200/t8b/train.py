@@ -114,7 +114,7 @@ class SelfPlayTrainer:
             marker.record()
         rollout.normalize_rewards(0.99)
         rollout.compute_gae(0.99, 0.95, True)
-        return policy.update_ppo(rollout.device_view(), self.ppo, self.seed + update)
+        return policy.update_ppo(rollout.device_view(packed=True), self.ppo, self.seed + update)
 
     def host_boundary(self):
         """The per-update host traffic of the reference trainer (schedule upload, tally and
