@@ -126,6 +126,60 @@ def cpu_baseline(args, features, env, sample_envs=2048, sample_horizon=16):
                       f"PPO objective, backward and Adam ({args.epochs} epochs x {args.minibatches} minibatches)"}
 
 
+# Algorithmic work of the hot kernels, per unit they process, for the roofline figures.
+# Frame step (k_step): the per-env-step bytes of a decision at the engine boundary: state in and
+# out 2 x 280, noise levels 16, action 8, observations 2 x 151 x 4, masks 2 x 368 (uint8),
+# reward and flags 14, table ids 8 = 2,550 B.
+STEP_BYTES_PER_ENV = 2550
+OBS, HIDDEN, OUTPUTS = 151, 512, 33
+# GEMM FLOPs per sample, unpadded shapes (obs 151 -> 512 -> 512 -> 33).
+GEMM_FLOPS_PER_SAMPLE = {
+    "gemm_forward_hidden": 2 * (OBS * HIDDEN + HIDDEN * HIDDEN),
+    "gemm_forward_output": 2 * HIDDEN * OUTPUTS,
+    "gemm_weight_grad": 2 * (OBS * HIDDEN + HIDDEN * HIDDEN + HIDDEN * OUTPUTS),
+    "gemm_input_grad": 2 * (HIDDEN * OUTPUTS + HIDDEN * HIDDEN),
+}
+# GAE: read reward, value, next value (4 B each), terminated, truncated (1 B each); write
+# advantage and return (4 B each) = 22 B per sample.
+GAE_BYTES_PER_SAMPLE = 22
+# PPO loss with on-chip scores: read the 33 output floats, 12 mask words, action, table id, old
+# log-prob, advantage, return, old value; write the 33 output gradients = 364 B per sample.
+LOSS_BYTES_PER_SAMPLE = 33 * 4 + 12 * 4 + 8 + 4 + 4 * 4 + 33 * 4 + 24
+
+
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from an ncu capture of
+# the kernel, scaled to one launch of this workload by the fights it processes. Writes of the
+# frame step stay in the 126 MB L2 within a launch, so its DRAM traffic is mostly reads.
+TRAFFIC = {"k_step": 4.968e6 * 32768 / 8192}
+
+
+def kernel_table(args, profile, steps, peaks):
+    """Per-kernel device time over the timed steps, with roofline fractions where the
+    algorithmic work of the kernel is known."""
+    peak_hbm, peak_bf16 = peaks
+    n, t = args.envs, args.horizon
+    rollout_samples = (t + 1) * n
+    update_samples = args.epochs * t * n
+    samples = {"gemm_forward_hidden": rollout_samples + update_samples,
+               "gemm_forward_output": rollout_samples + update_samples,
+               "gemm_weight_grad": update_samples, "gemm_input_grad": update_samples}
+    total = sum(ms for _, ms in profile.values()) or 1.0
+    rows = []
+    for label, (launches, ms) in sorted(profile.items(), key=lambda kv: -kv[1][1]):
+        row = {"kernel": label, "launches_per_step": launches / steps, "ms_per_step": ms / steps,
+               "share": ms / total}
+        if label in GEMM_FLOPS_PER_SAMPLE:
+            tflops = GEMM_FLOPS_PER_SAMPLE[label] * samples[label] * steps / (ms / 1000.0) / 1e12
+            row.update(bound="tensor", achieved=tflops, peak=peak_bf16, unit="TFLOP/s", frac=tflops / peak_bf16)
+        elif label in ("k_step", "k_gae", "k_loss"):
+            per = {"k_step": STEP_BYTES_PER_ENV * n, "k_gae": GAE_BYTES_PER_SAMPLE * t * n,
+                   "k_loss": LOSS_BYTES_PER_SAMPLE * n * t // args.minibatches}[label]
+            gbs = per * launches / (ms / 1000.0) / 1e9
+            row.update(bound="hbm", achieved=gbs, peak=peak_hbm, unit="GB/s", frac=gbs / peak_hbm)
+        rows.append(row)
+    return rows
+
+
 def run_reference(args):
     world, rank, local = distributed()
     if rank != 0:
@@ -175,6 +229,7 @@ def run_ours(args):
     from t8b import roster as roster_module
     from t8b.train import SelfPlayTrainer
     from t8b.sim import GpuFullMoveSimulator  # noqa: F401  (loads the library)
+    from t8b import profile
     roster = roster_module.parse(roster_raw())
     trainer = SelfPlayTrainer(roster, environments=args.envs, horizon=args.horizon, epochs=args.epochs,
                               minibatches=args.minibatches, seed=3, comm=comm, rank=rank)
@@ -189,6 +244,8 @@ def run_ours(args):
     rollout_ms = []
     bytes_up = bytes_down = 0
     frames_before = trainer.sim.frames_simulated()
+    launches_before = profile.launch_count()
+    profile.enable(True)
     with ClockSampler(local) as clocks:
         wall0 = time.perf_counter()
         for _ in range(args.steps):
@@ -207,6 +264,9 @@ def run_ours(args):
         if world > 1:
             torch.distributed.barrier()
         wall = time.perf_counter() - wall0
+    launches = profile.launch_count() - launches_before
+    kernels = profile.report()
+    profile.enable(False)
     frames = trainer.sim.frames_simulated() - frames_before
     total_device = sum(device_ms)
     vals = torch.tensor([total_device, wall, sum(rollout_ms)], dtype=torch.float64, device="cuda")
@@ -217,6 +277,15 @@ def run_ours(args):
     value = units / (total_device / 1000.0)
     e2e = units / wall
     peak_hbm, peak_bf16, peak_bf16_sustained, peak_kind = measured_peaks()
+    # Kernels run inside a seconds-long step: the sustained tensor peak applies; HBM is the copy peak.
+    table = kernel_table(args, kernels, args.steps, (peak_hbm, peak_bf16_sustained))
+    top = table[0] if table else None
+    roofline = None
+    if top is not None and "bound" in top:
+        roofline = {"kernel": top["kernel"], "bound": top["bound"], "achieved": top["achieved"], "peak": top["peak"],
+                    "unit": top["unit"], "frac": top["frac"], "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)"
+                    if peak_kind == "measured" else "fallback", "traffic": TRAFFIC.get(top["kernel"]),
+                    "avg_launch_ms": top["ms_per_step"] / top["launches_per_step"]}
     line = {
         "metric": METRIC, "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_device / args.steps, "higher_is_better": True, "scaling": "weak",
@@ -232,7 +301,10 @@ def run_ours(args):
         "engine_frames_per_s": frames / (total_device / 1000.0) * world,
         "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": bytes_up // args.steps,
                 "d2h_bytes_per_step": bytes_down // args.steps},
-        "gpu_launches": None,
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / args.steps,
+        "roofline": roofline,
+        "kernels": [{k: (round(v, 6) if isinstance(v, float) else v) for k, v in row.items()} for row in table[:12]],
         "clocks": clocks.summary(),
         "last_metrics": {k: float(v) for k, v in metrics.items()},
     }

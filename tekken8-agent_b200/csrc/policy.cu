@@ -105,7 +105,8 @@ struct t8b_policy {
     Buffer<float> logits, log_probs, values, entropies;
     Buffer<int64_t> actions;
     // minibatch side data
-    Buffer<uint32_t> mb_bits, perm;
+    Buffer<uint32_t> mb_bits, perm, grouped, group_counts;
+    Buffer<int32_t> bucket_start;
     Buffer<int32_t> mb_actions, mb_tables;
     Buffer<float> mb_old_lp, mb_old_v, mb_adv, mb_ret;
     Buffer<double> block_metrics, metrics, norm_partial, norm_sq, entropy_sums;
@@ -349,6 +350,34 @@ __global__ void k_decision_finish(const double* partial, int blocks, double* out
     out[1] = d;
 }
 
+// Grid of k_loss for a minibatch of n rows: one block per run of at most kLossRows rows of one
+// feature table; the runs of the kBuckets tables add at most one partial run each.
+size_t loss_blocks(size_t n) { return (n + ppo::kLossRows - 1) / ppo::kLossRows + ppo::kBuckets; }
+
+// Reorders every minibatch slice of the epoch permutation (s.perm) by feature table into
+// s.grouped and records each slice's table offsets in s.bucket_start.
+void group_minibatches(t8b_policy& s, const t8b_rollout_view_t& r, size_t samples, size_t minibatch, cudaStream_t st) {
+    const size_t slices = (samples + minibatch - 1) / minibatch;
+    const int per_slice = static_cast<int>((minibatch + ppo::kGroupRows - 1) / ppo::kGroupRows);
+    const size_t grid = slices * static_cast<size_t>(per_slice);
+    if (s.group_counts.size() < grid * ppo::kBuckets) s.group_counts.allocate(grid * ppo::kBuckets);
+    if (s.bucket_start.size() < slices * (ppo::kBuckets + 1)) s.bucket_start.allocate(slices * (ppo::kBuckets + 1));
+    ppo::Group g{};
+    g.perm = s.perm.data();
+    g.tables = r.feature_tables;
+    g.table_count = s.tables;
+    g.samples = samples;
+    g.minibatch = minibatch;
+    g.blocks_per_slice = per_slice;
+    g.counts = s.group_counts.data();
+    g.sorted = s.grouped.data();
+    g.bucket_start = s.bucket_start.data();
+    launch("k_group_count", ppo::k_group_count, static_cast<unsigned>(grid), 256, 0, st, g);
+    launch("k_group_offsets", ppo::k_group_offsets, static_cast<unsigned>(slices), 64, 0, st, g);
+    launch("k_group_scatter", ppo::k_group_scatter, static_cast<unsigned>(grid), 256, 0, st, g);
+    check(cudaGetLastError(), "group minibatches by feature table");
+}
+
 }  // namespace
 
 extern "C" {
@@ -471,7 +500,10 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
         }
         p->out.allocate(cap * kOutPad);
         p->dout.allocate(cap * kOutPad);
-        p->out_colsum.allocate(((cap + ppo::kWarps - 1) / ppo::kWarps) * kOutPad);
+        const size_t partial_rows = std::max((cap + ppo::kWarps - 1) / ppo::kWarps, loss_blocks(cap));
+        p->out_colsum.allocate(partial_rows * kOutPad);
+        check(cudaFuncSetAttribute(ppo::k_loss, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kTableBytes),
+              "objective shared memory");
         const size_t sms = static_cast<size_t>(sm_count());
         const size_t part = std::max({sms * p->hidden * kOutPad, sms * static_cast<size_t>(p->hidden) * p->hidden,
                                       sms * static_cast<size_t>(p->hidden) * p->padded});
@@ -488,7 +520,7 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
         p->mb_old_v.allocate(cap);
         p->mb_adv.allocate(cap);
         p->mb_ret.allocate(cap);
-        p->block_metrics.allocate(((cap + ppo::kWarps - 1) / ppo::kWarps) * ppo::kMetrics);
+        p->block_metrics.allocate(partial_rows * ppo::kMetrics);
         p->metrics.allocate(ppo::kMetrics);
         p->norm_partial.allocate(1024);
         p->norm_sq.allocate(1);
@@ -668,7 +700,10 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
             s.sample_entropy.allocate(samples);
             s.sample_decision.allocate(samples);
         }
-        if (s.perm.size() < samples) s.perm.allocate(samples);
+        if (s.perm.size() < samples) {
+            s.perm.allocate(samples);
+            s.grouped.allocate(samples);
+        }
         // permutations: prepared in the background when the caller announced them
         std::vector<std::vector<uint32_t>> perms;
         if (s.shuffler.joinable()) s.shuffler.join();
@@ -687,6 +722,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         const int norm_blocks = 256;
         for (int epoch = 0; epoch < cfg->epochs; ++epoch) {
             s.perm.upload(perms[static_cast<size_t>(epoch)].data(), samples, st);
+            group_minibatches(s, r, samples, mb, st);
             for (size_t offset = 0; offset < samples; offset += mb) {
                 const size_t n = std::min(mb, samples - offset);
                 ++minibatches;
@@ -698,7 +734,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 prep.istd = s.obs_istd.data();
                 prep.clip = s.config.observation_clip;
                 prep.normalize = s.normalizing() ? 1 : 0;
-                prep.perm = s.perm.data();
+                prep.perm = s.grouped.data();
                 prep.offset = offset;
                 prep.count = n;
                 prep.x = s.x.data();
@@ -745,14 +781,15 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 loss.out_colsum = s.out_colsum.data();
                 loss.sample_entropy = epoch == 0 ? s.sample_entropy.data() : nullptr;
                 loss.sample_decision = epoch == 0 ? s.sample_decision.data() : nullptr;
-                loss.perm = s.perm.data();
+                loss.perm = s.grouped.data();
                 loss.offset = offset;
-                const unsigned loss_blocks = blocks(n, ppo::kWarps);
-                launch("k_loss", ppo::k_loss, loss_blocks, 32 * ppo::kWarps, 0, st, loss);
+                loss.bucket_start = s.bucket_start.data() + (offset / mb) * (ppo::kBuckets + 1);
+                const unsigned loss_grid = static_cast<unsigned>(loss_blocks(n));
+                launch("k_loss", ppo::k_loss, loss_grid, 32 * ppo::kWarps, ppo::kTableBytes, st, loss);
                 check(cudaGetLastError(), "PPO objective");
-                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, s.block_metrics.data(), static_cast<int>(loss_blocks),
+                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, s.block_metrics.data(), static_cast<int>(loss_grid),
                                                                    ppo::kMetrics, s.metrics.data(), 1);
-                s.column_sums(s.out_colsum.data(), static_cast<int>(loss_blocks), kOutPad, s.outputs,
+                s.column_sums(s.out_colsum.data(), static_cast<int>(loss_grid), kOutPad, s.outputs,
                               s.grads.data() + s.b_off[s.layers], st);
                 s.backward(n, st);
                 if (s.comm.active()) {

@@ -452,6 +452,125 @@ __global__ void k_sample(Sample p) {
     }
 }
 
+// ------------------------------------------------------------------ minibatch grouping
+// Each minibatch of an epoch's permutation is stably reordered by feature table (the
+// minibatch is the same set of samples; only the row order inside it changes), so the
+// objective kernel can stage one table per block. Three passes over 1024-row blocks:
+// per-block table counts, per-minibatch offsets, and a scatter whose ranks come from warp
+// matches in row order, so the result is deterministic.
+constexpr int kBuckets = 43;     // feature tables 0..41, then samples with no valid table
+constexpr int kGroupRows = 1024;  // rows per block of the grouping kernels
+
+struct Group {
+    const uint32_t* perm;    // [samples] the epoch's order
+    const int32_t* tables;   // [samples] feature table per rollout sample (null: table 0)
+    int table_count;
+    size_t samples, minibatch;
+    int blocks_per_slice;
+    uint32_t* counts;        // [blocks][kBuckets]; turned into each block's first row per table
+    uint32_t* sorted;        // [samples] the epoch's order, each minibatch grouped by table
+    int32_t* bucket_start;   // [minibatches][kBuckets + 1] row offsets inside each minibatch
+};
+
+__device__ __forceinline__ bool group_range(const Group& p, size_t& slice_start, size_t& start, size_t& end) {
+    const size_t slice = blockIdx.x / p.blocks_per_slice;
+    slice_start = slice * p.minibatch;
+    const size_t slice_end = min(slice_start + p.minibatch, p.samples);
+    start = slice_start + static_cast<size_t>(blockIdx.x % p.blocks_per_slice) * kGroupRows;
+    end = min(start + kGroupRows, slice_end);
+    return start < end;
+}
+
+__device__ __forceinline__ int bucket_of(const Group& p, size_t row) {
+    if (!p.tables) return 0;
+    const int t = p.tables[p.perm[row]];
+    return t >= 0 && t < p.table_count ? t : kBuckets - 1;
+}
+
+__global__ void k_group_count(Group p) {
+    __shared__ uint32_t hist[kBuckets];
+    for (int t = threadIdx.x; t < kBuckets; t += blockDim.x) hist[t] = 0;
+    __syncthreads();
+    size_t slice_start, start, end;
+    if (group_range(p, slice_start, start, end)) {
+        for (size_t r = start + threadIdx.x; r < end; r += blockDim.x) atomicAdd(&hist[bucket_of(p, r)], 1u);
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < kBuckets; t += blockDim.x) p.counts[static_cast<size_t>(blockIdx.x) * kBuckets + t] = hist[t];
+}
+
+// One block per minibatch, one thread per table.
+__global__ void k_group_offsets(Group p) {
+    __shared__ uint32_t total[kBuckets];
+    const size_t first = static_cast<size_t>(blockIdx.x) * p.blocks_per_slice;
+    const int t = threadIdx.x;
+    if (t < kBuckets) {
+        uint32_t sum = 0;
+        for (int b = 0; b < p.blocks_per_slice; ++b) sum += p.counts[(first + b) * kBuckets + t];
+        total[t] = sum;
+    }
+    __syncthreads();
+    if (t < kBuckets) {
+        uint32_t base = 0;
+        for (int u = 0; u < t; ++u) base += total[u];
+        int32_t* starts = p.bucket_start + static_cast<size_t>(blockIdx.x) * (kBuckets + 1);
+        starts[t] = static_cast<int32_t>(base);
+        if (t == kBuckets - 1) starts[kBuckets] = static_cast<int32_t>(base + total[t]);
+        uint32_t running = base;
+        for (int b = 0; b < p.blocks_per_slice; ++b) {
+            uint32_t* c = p.counts + (first + b) * kBuckets + t;
+            const uint32_t n = *c;
+            *c = running;
+            running += n;
+        }
+    }
+}
+
+__global__ void k_group_scatter(Group p) {
+    constexpr int kRuns = kGroupRows / 32;
+    __shared__ uint32_t base[kRuns][kBuckets];
+    for (int i = threadIdx.x; i < kRuns * kBuckets; i += blockDim.x) (&base[0][0])[i] = 0;
+    __syncthreads();
+    size_t slice_start, start, end;
+    const bool any = group_range(p, slice_start, start, end);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const uint32_t below = (1u << lane) - 1u;
+    if (any) {
+        for (int g = warp; g < kRuns; g += warps) {
+            const size_t r = start + static_cast<size_t>(g) * 32 + lane;
+            const bool live = r < end;
+            const uint32_t active = __ballot_sync(0xffffffffu, live);
+            if (live) {
+                const int b = bucket_of(p, r);
+                const uint32_t same = __match_any_sync(active, b);
+                if ((same & below) == 0) base[g][b] = __popc(same);
+            }
+        }
+    }
+    __syncthreads();
+    if (any && threadIdx.x < kBuckets) {
+        uint32_t running = p.counts[static_cast<size_t>(blockIdx.x) * kBuckets + threadIdx.x];
+        for (int g = 0; g < kRuns; ++g) {
+            const uint32_t n = base[g][threadIdx.x];
+            base[g][threadIdx.x] = running;
+            running += n;
+        }
+    }
+    __syncthreads();
+    if (any) {
+        for (int g = warp; g < kRuns; g += warps) {
+            const size_t r = start + static_cast<size_t>(g) * 32 + lane;
+            const bool live = r < end;
+            const uint32_t active = __ballot_sync(0xffffffffu, live);
+            if (live) {
+                const int b = bucket_of(p, r);
+                const uint32_t same = __match_any_sync(active, b);
+                p.sorted[slice_start + base[g][b] + __popc(same & below)] = p.perm[r];
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ PPO objective
 // ppo_output_gradient_kernel + parametric_policy_gradient_kernel (src/ppo.cu:453-565, 350-381):
 // one warp per sample; the clipped policy objective, the clipped value loss and the entropy
@@ -479,28 +598,84 @@ struct Loss {
     uint8_t* sample_decision;
     const uint32_t* perm;
     size_t offset;
+    const int32_t* bucket_start;  // [kBuckets + 1] first row of each table's rows in the minibatch
 };
 
-__global__ void k_loss(Loss p) {
+// Rows of one feature table that a k_loss block scores; the block's table sits in shared
+// memory, so each candidate row is read from L2 once per block instead of once per sample.
+constexpr int kLossRows = 256;
+constexpr int kTableBytes = kCandidates * kFeatures * 4;
+
+// Chunk k (4 floats) of candidate c's feature row in the staged table: chunks are rotated by
+// c & 7 so that lanes reading different rows at the same chunk hit different banks.
+__device__ __forceinline__ float4 staged_chunk(const float4* table, int c, int k) {
+    return table[c * (kFeatures / 4) + (k ^ (c & 7))];
+}
+__device__ __forceinline__ float staged_score(const float* q, const float4* table, int c, float scale) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kFeatures / 4; ++k) {
+        const float4 f = staged_chunk(table, c, k);
+        s += q[4 * k] * f.x;
+        s += q[4 * k + 1] * f.y;
+        s += q[4 * k + 2] * f.z;
+        s += q[4 * k + 3] * f.w;
+    }
+    return s * scale;
+}
+
+// The minibatch rows are grouped by feature table (k_group_*); block b takes the b-th run of at
+// most kLossRows rows of one table, counted over the tables in order. Blocks past the last run
+// only write zero partials.
+__global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
+    extern __shared__ float4 table[];  // kCandidates x kFeatures floats, see staged_chunk
     __shared__ float qs[kWarps][64];
     __shared__ float grads[kWarps][64];
-    __shared__ float metric[kWarps][kMetrics];
+    __shared__ float colsum[kWarps][64];
+    __shared__ double metric[kWarps][kMetrics];
     __shared__ int16_t lists[kWarps][kCandidates];
     __shared__ float scores[kWarps][kCandidates];
+    __shared__ int run[3];  // bucket, first row, end row
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
-    const bool live = i < p.count;
+    if (threadIdx.x == 0) {
+        int b = static_cast<int>(blockIdx.x);
+        run[0] = -1;
+        run[1] = run[2] = 0;
+        for (int t = 0; t < kBuckets; ++t) {
+            const int lo = p.bucket_start[t], hi = p.bucket_start[t + 1];
+            const int runs = (hi - lo + kLossRows - 1) / kLossRows;
+            if (b < runs) {
+                run[0] = t;
+                run[1] = lo + b * kLossRows;
+                run[2] = min(lo + (b + 1) * kLossRows, hi);
+                break;
+            }
+            b -= runs;
+        }
+    }
+    __syncthreads();
+    const int bucket = run[0];
+    const bool bad_table = bucket < 0 || bucket >= p.table_count;
+    if (!bad_table) {
+        const float4* src = reinterpret_cast<const float4*>(p.features + static_cast<size_t>(bucket) * kCandidates * kFeatures);
+        for (int i = threadIdx.x; i < kCandidates * (kFeatures / 4); i += blockDim.x) {
+            const int c = i / (kFeatures / 4), k = i % (kFeatures / 4);
+            table[c * (kFeatures / 4) + (k ^ (c & 7))] = __ldg(src + i);
+        }
+    }
+    float col_lo = 0.0f, col_hi = 0.0f;
+    if (lane < kMetrics) metric[warp][lane] = 0.0;
     for (int f = lane; f < 64; f += 32) grads[warp][f] = 0.0f;
-    if (lane < kMetrics) metric[warp][lane] = 0.0f;
-    if (live) {
+    __syncthreads();
+    const float scale = rsqrtf(static_cast<float>(p.feature_size));
+    for (int row = run[1] + warp; bucket >= 0 && row < run[2]; row += kWarps) {
+        const size_t i = static_cast<size_t>(row);
         const float* o = p.out + i * p.ld;
         for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
         __syncwarp();
-        const float* q = qs[warp];
-        const float scale = rsqrtf(static_cast<float>(p.feature_size));
-        const int table = p.tables[i];
-        const bool bad_table = table < 0 || table >= p.table_count;
-        const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * kCandidates * p.feature_size;
+        float q[kFeatures];
+#pragma unroll
+        for (int f = 0; f < kFeatures; ++f) q[f] = qs[warp][f];
         uint32_t words[kMaskWords];
         bool any = false;
 #pragma unroll
@@ -513,7 +688,7 @@ __global__ void k_loss(Loss p) {
         const int count = compact_legal(words, any, lane, list);
         float local_max = -3.402823466e38f;
         for (int j = lane; j < count; j += 32) {
-            const float s = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + list[j] * p.feature_size, p.feature_size, scale);
+            const float s = bad_table ? __int_as_float(0x7fc00000) : staged_score(q, table, list[j], scale);
             sc[j] = s;
             local_max = fmaxf(local_max, s);
         }
@@ -550,10 +725,9 @@ __global__ void k_loss(Loss p) {
                 const float prob = expf(lp);
                 float g = (lp_grad * ((c == selected ? 1.0f : 0.0f) - prob)) * p.inv_batch;
                 g += p.entropy_coef * prob * (lp + entropy) * p.inv_batch;
-                const float4* f4 = reinterpret_cast<const float4*>(ftab + c * kFeatures);
 #pragma unroll
                 for (int k = 0; k < kFeatures / 4; ++k) {
-                    const float4 f = __ldg(f4 + k);
+                    const float4 f = staged_chunk(table, c, k);
                     dq_local[4 * k] += g * f.x;
                     dq_local[4 * k + 1] += g * f.y;
                     dq_local[4 * k + 2] += g * f.z;
@@ -563,7 +737,7 @@ __global__ void k_loss(Loss p) {
         }
         const float total = transpose_sum32(dq_local, lane);
         grads[warp][lane] = bad_table ? __int_as_float(0x7fc00000) : total * scale;
-        const float value = q[p.feature_size];
+        const float value = qs[warp][p.feature_size];
         const float error = value - p.ret[i];
         float vgrad = error;
         float vloss = 0.5f * error * error;
@@ -579,13 +753,14 @@ __global__ void k_loss(Loss p) {
         }
         if (lane == 0) {
             grads[warp][p.feature_size] = p.value_coef * vgrad * p.inv_batch;
-            metric[warp][0] = policy_loss;
-            metric[warp][1] = vloss;
-            metric[warp][2] = entropy;
-            metric[warp][3] = (ratio - 1.0f) - log_ratio;
-            metric[warp][4] = fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f;
-            metric[warp][6] = count > 1 ? 1.0f : 0.0f;
-            metric[warp][7] = count > 1 ? entropy : 0.0f;
+            double* m = metric[warp];
+            m[0] += policy_loss;
+            m[1] += vloss;
+            m[2] += entropy;
+            m[3] += (ratio - 1.0f) - log_ratio;
+            m[4] += fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f;
+            m[6] += count > 1 ? 1.0f : 0.0f;
+            m[7] += count > 1 ? entropy : 0.0f;
             if (p.sample_entropy) {
                 const size_t sample = p.perm[p.offset + i];
                 p.sample_entropy[sample] = entropy;
@@ -593,13 +768,18 @@ __global__ void k_loss(Loss p) {
             }
         }
         __syncwarp();
+        col_lo += grads[warp][lane];
+        col_hi += grads[warp][32 + lane];
         for (int f = lane; f < p.ld_grad; f += 32) p.dout[i * p.ld_grad + f] = __float2bfloat16_rn(grads[warp][f]);
+        __syncwarp();
     }
+    colsum[warp][lane] = col_lo;
+    colsum[warp][32 + lane] = col_hi;
     __syncthreads();
     // block partials in warp order (deterministic)
     if (threadIdx.x < p.ld_grad) {
         float sum = 0.0f;
-        for (int w = 0; w < kWarps; ++w) sum += grads[w][threadIdx.x];
+        for (int w = 0; w < kWarps; ++w) sum += colsum[w][threadIdx.x];
         p.out_colsum[static_cast<size_t>(blockIdx.x) * p.ld_grad + threadIdx.x] = sum;
     }
     if (threadIdx.x < kMetrics) {

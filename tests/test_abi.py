@@ -64,3 +64,10 @@ def test_roster_fixture_parses(roster):
     assert all(c.roster_id == i for i, c in enumerate(roster.characters))
     assert max(c.candidate_count for c in roster.characters) <= 368
     assert roster.characters[3].candidate_count == 182  # tests/full_move_gpu_tests.cpp:134
+
+
+def test_launch_accounting_without_gpu():
+    """The launch counter and the empty profile report work without a device."""
+    from t8b import profile
+    assert profile.launch_count() >= 0
+    assert profile.report() == {}
