@@ -112,6 +112,18 @@ def measured_peaks():
     return 6650.0, 1590.0, 1400.0, "fallback"
 
 
+def max_over_ranks(values, device):
+    """Each value's maximum over the ranks of the default process group (values unchanged when
+    not distributed)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return list(values)
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def cpu_baseline(args, features, env, sample_envs=2048, sample_horizon=16):
     """The CPU leg on the host cores, on a bounded sample of the same workload."""
     from oracle.cpu_iteration import CpuIteration
@@ -269,10 +281,7 @@ def run_ours(args):
     profile.enable(False)
     frames = trainer.sim.frames_simulated() - frames_before
     total_device = sum(device_ms)
-    vals = torch.tensor([total_device, wall, sum(rollout_ms)], dtype=torch.float64, device="cuda")
-    if world > 1:
-        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
-    total_device, wall, rollout_total = vals.tolist()
+    total_device, wall, rollout_total = max_over_ranks([total_device, wall, sum(rollout_ms)], "cuda")
     units = args.envs * args.horizon * world * args.steps
     value = units / (total_device / 1000.0)
     e2e = units / wall

@@ -113,7 +113,7 @@ struct t8b_policy {
     Buffer<float> sample_entropy;
     Buffer<uint8_t> sample_decision;
     Buffer<int> error, invalid;
-    Buffer<double> kl_pair;
+    Buffer<double> kl_pair, obs_gathered;
     // features
     Buffer<float> features;
     int tables = 0;
@@ -840,12 +840,29 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
             if (s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
             dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((s.width + 31) / 32));
             launch("k_obs_moments", ppo::k_obs_moments, grid, 256, 0, st, r.observations, samples, s.width, chunk, s.obs_chunks.data());
-            launch("k_obs_merge", ppo::k_obs_merge, blocks(s.width, 128), 128, 0, st, s.obs_chunks.data(), static_cast<int>(chunks), s.width,
-                                                                   static_cast<double>(s.obs_count), s.obs_mean.data(),
-                                                                   s.obs_var.data(), s.obs_istd.data(),
-                                                                   s.config.observation_epsilon, nullptr);
+            if (s.comm.active() && s.comm.hooks.allreduce_sum_f64) {
+                // data parallel: every rank's batch moments land in its own slot of a zeroed
+                // [world][width][3] buffer, a sum all-reduce gathers them, and each rank merges
+                // the slots in rank order into identical running statistics
+                const int world = s.comm.hooks.world_size;
+                const size_t slot = static_cast<size_t>(s.width) * 3;
+                if (s.obs_gathered.size() < world * slot) s.obs_gathered.allocate(world * slot);
+                s.obs_gathered.zero(st);
+                launch("k_obs_merge", ppo::k_obs_merge, blocks(s.width, 128), 128, 0, st, s.obs_chunks.data(), static_cast<int>(chunks),
+                       s.width, 0.0, nullptr, nullptr, nullptr, s.config.observation_epsilon,
+                       s.obs_gathered.data() + static_cast<size_t>(s.comm.hooks.rank) * slot);
+                s.comm.hooks.allreduce_sum_f64(s.obs_gathered.data(), world * slot, stream, s.comm.hooks.user);
+                launch("k_obs_merge", ppo::k_obs_merge, blocks(s.width, 128), 128, 0, st, s.obs_gathered.data(), world, s.width,
+                       static_cast<double>(s.obs_count), s.obs_mean.data(), s.obs_var.data(), s.obs_istd.data(),
+                       s.config.observation_epsilon, nullptr);
+                s.obs_count += samples * static_cast<uint64_t>(world);  // ranks hold equal-size rollouts
+            } else {
+                launch("k_obs_merge", ppo::k_obs_merge, blocks(s.width, 128), 128, 0, st, s.obs_chunks.data(), static_cast<int>(chunks),
+                       s.width, static_cast<double>(s.obs_count), s.obs_mean.data(), s.obs_var.data(), s.obs_istd.data(),
+                       s.config.observation_epsilon, nullptr);
+                s.obs_count += samples;
+            }
             check(cudaGetLastError(), "merge observation statistics");
-            s.obs_count += samples;
         }
         // rollout decision entropy (src/ppo.cu:1671-1683)
         const int dblocks = 256;
@@ -858,6 +875,10 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         }
         launch("k_decision_finish", k_decision_finish, 1, 32, 0, st, s.entropy_sums.data(), dblocks, s.entropy_sums.data() + 2 * 1024);
         check(cudaGetLastError(), "decision entropy");
+        if (s.comm.active() && s.comm.hooks.allreduce_sum_f64) {
+            // the entropy-floor controller sees the decision entropy of every rank's rollout
+            s.comm.hooks.allreduce_sum_f64(s.entropy_sums.data() + 2 * 1024, 2, stream, s.comm.hooks.user);
+        }
         double m[ppo::kMetrics];
         s.metrics.download(m, ppo::kMetrics, st);
         double ent[2];

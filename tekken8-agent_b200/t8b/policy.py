@@ -43,30 +43,44 @@ def _p(value):
 
 
 class TorchComm:
-    """t8b_comm_t over torch.distributed (NCCL): sum all-reduces on tensors aliasing the
-    library's device buffers, on the library's stream."""
+    """t8b_comm_t over torch.distributed: sum all-reduces on tensors aliasing the library's
+    buffers. On CUDA (NCCL) the reduce is ordered on the stream the library passes; with
+    device="cpu" the buffers are host memory (gloo), which is how the hooks are exercised
+    without a GPU."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, device: str = "cuda"):
         import torch.distributed as dist
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        device = torch.cuda.current_device()
+        self.host = device == "cpu"
+        self.device = None if self.host else torch.cuda.current_device()
 
         def f32(pointer, count, stream, user):
-            self._reduce(pointer, count, torch.float32, device)
+            self._reduce(pointer, count, torch.float32, stream)
 
         def f64(pointer, count, stream, user):
-            self._reduce(pointer, count, torch.float64, device)
+            self._reduce(pointer, count, torch.float64, stream)
 
         self._f32 = _lib.ALLREDUCE_F32(f32)
         self._f64 = _lib.ALLREDUCE_F64(f64)
         self.struct = Comm(self._f32, self._f64, None, self.world, self.rank)
 
-    def _reduce(self, pointer, count, dtype, device):
-        tensor = view(pointer, (count,), dtype, device)
-        self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM, group=self.group)
+    def _reduce(self, pointer, count, dtype, stream):
+        if count == 0:
+            return
+        if self.host:
+            ctype = C.c_float if dtype == torch.float32 else C.c_double
+            tensor = torch.frombuffer((ctype * count).from_address(pointer), dtype=dtype)
+            self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM, group=self.group)
+            return
+        tensor = view(pointer, (count,), dtype, self.device)
+        if stream:
+            with torch.cuda.stream(torch.cuda.ExternalStream(stream, device=self.device)):
+                self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM, group=self.group)
+        else:
+            self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM, group=self.group)
 
 
 class GpuActorCritic:
