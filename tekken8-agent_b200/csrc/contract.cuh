@@ -585,17 +585,20 @@ T8B_HD bool is_held(const Input& in) {
         (in.universal == kIdle || in.universal == kWalkForward || in.universal == kWalkBack || in.universal == kCrouch);
 }
 
-// env_step (full_move_contract.hpp:1071-1154). `profiles` is the 331-entry bot table;
-// opponent_candidate < 0 means the scripted opponent plays.
-T8B_HD StepOut decision(const Match& m, Fight& s, int learner, int learner_candidate, int opponent_candidate,
-                        double aggression, const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream,
-                        uint64_t counter, const Noise* noise) {
+// env_step (full_move_contract.hpp:1071-1154) for a learner on side L. `profiles` is the
+// 331-entry bot table; opponent_candidate < 0 means the scripted opponent plays. The side is a
+// template argument so that every fighter index in the frame loop is a constant.
+template <int L>
+T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int opponent_candidate, double aggression,
+                           const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream, uint64_t counter,
+                           const Noise* noise) {
+    constexpr int learner = L;
     StepOut r{0.0F, 0.0F, 0, 0, 0};
     int lag = 0;
     if (noise != nullptr && noise->latency > 0) {
         lag = noise->latency + (unit(hash3(noise->key, 0x1a7u, counter)) < 0.25 ? 1 : 0);
     }
-    const int op = 1 - learner;
+    constexpr int op = 1 - learner;
     const double max_health = m.cfg->max_health;
     const double own_before = s.f[learner].health;
     const double opp_before = s.f[op].health;
@@ -653,6 +656,15 @@ T8B_HD StepOut decision(const Match& m, Fight& s, int learner, int learner_candi
         r.reward += r.sparse;
     }
     return r;
+}
+
+T8B_HD StepOut decision(const Match& m, Fight& s, int learner, int learner_candidate, int opponent_candidate,
+                        double aggression, const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream,
+                        uint64_t counter, const Noise* noise) {
+    return learner == 0 ? decision_as<0>(m, s, learner_candidate, opponent_candidate, aggression, ec, profiles, seed,
+                                         stream, counter, noise)
+                        : decision_as<1>(m, s, learner_candidate, opponent_candidate, aggression, ec, profiles, seed,
+                                         stream, counter, noise);
 }
 
 }  // namespace t8b

@@ -1086,6 +1086,28 @@ T8B_HD bool find_contact(const Match& m, const Fight& s, int ap, Pending& out) {
 }
 
 // step (full_combat_core.hpp:877-1296)
+// One contact found in phase 4 by attacker A (full_combat_core.hpp:1269-1290).
+template <int A>
+T8B_HD void apply_contact(const Match& m, Fight& s, const Pending& d, Events& e) {
+    Fighter& a = s.f[A];
+    Fighter& t = s.f[1 - A];
+    a.hits_landed |= 1u << static_cast<unsigned>(d.hit_index);
+    if (d.contact == kThrowHeld) {
+        if (a.move < 0) return;
+        a.pending_throw_hit = d.hit_index;
+        t.break_frames = m.cfg->throw_break_window;
+        t.flags &= ~(fBreakAttempted | fInBlockstun);
+        t.stance = -1;
+        t.move = -1;
+        t.universal = kIdle;
+        t.stun = 0;
+        t.dash_from = kNoContactFrom;
+        add_contact(e, A, d.hit_index, kThrowHeld, 0.0);
+        return;
+    }
+    resolve(m, s, A, d.move_index, d.defense_move, d.hit_index, d.contact, 0, e);
+}
+
 T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& in1, Events& e) {
     e.contact_count = 0;
     e.transition_count = 0;
@@ -1095,6 +1117,7 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
     const Cfg& c = *m.cfg;
 
     // 0. timers
+#pragma unroll
     for (int p = 0; p < 2; ++p) {
         Fighter& f = s.f[p];
         if (f.ki_frames > 0 && --f.ki_frames == 0) f.flags &= ~fKiBoost;
@@ -1112,6 +1135,7 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
 
     // 2. advance
     bool stepping = false;
+#pragma unroll
     for (int p = 0; p < 2; ++p) {
         const Fighter& f = s.f[p];
         stepping = stepping || (f.move < 0 && (f.universal == kSidestepLeft || f.universal == kSidestepRight));
@@ -1128,6 +1152,7 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
     }
 
     // 3. walls and body collision
+#pragma unroll
     for (int p = 0; p < 2; ++p) s.f[p].x = clampd(s.f[p].x, s.left_wall, s.right_wall);
     {
         Fighter& a = s.f[0];
@@ -1139,6 +1164,7 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
             const double dir = dx >= 0.0 ? 1.0 : -1.0;
             a.x -= dir * push;
             b.x += dir * push;
+#pragma unroll
             for (int k = 0; k < 2; ++k) {
                 Fighter& f = s.f[k];
                 Fighter& other = s.f[1 - k];
@@ -1149,17 +1175,20 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
                     other.x += over;
                 }
             }
+#pragma unroll
             for (int p = 0; p < 2; ++p) s.f[p].x = clampd(s.f[p].x, s.left_wall, s.right_wall);
         }
     }
 
     // 4. contacts from one snapshot
-    Pending pend[2];
-    int pending = 0;
-    if (find_contact(m, s, 0, pend[pending])) ++pending;
-    if (find_contact(m, s, 1, pend[pending])) ++pending;
+    Pending pend0, pend1;
+    const bool found0 = find_contact(m, s, 0, pend0);
+    const bool found1 = find_contact(m, s, 1, pend1);
 
-    // 5. a held throw whose window closes lands first, then the new contacts
+    // 5. a held throw whose window closes lands first, then the new contacts (attacker 0's,
+    // then attacker 1's). Every fighter index here is a constant, so a caller that keeps the
+    // fight in registers is not forced into local memory.
+#pragma unroll
     for (int p = 0; p < 2; ++p) {
         Fighter& held = s.f[p];
         Fighter& thrower = s.f[1 - p];
@@ -1178,26 +1207,8 @@ T8B_HD void frame_step(const Match& m, Fight& s, const Input& in0, const Input& 
             thrower.action_frame = action_length(kIdle, c);
         }
     }
-    for (int k = 0; k < pending; ++k) {
-        const Pending& d = pend[k];
-        Fighter& a = s.f[d.attacker];
-        Fighter& t = s.f[1 - d.attacker];
-        a.hits_landed |= 1u << static_cast<unsigned>(d.hit_index);
-        if (d.contact == kThrowHeld) {
-            if (a.move < 0) continue;
-            a.pending_throw_hit = d.hit_index;
-            t.break_frames = c.throw_break_window;
-            t.flags &= ~(fBreakAttempted | fInBlockstun);
-            t.stance = -1;
-            t.move = -1;
-            t.universal = kIdle;
-            t.stun = 0;
-            t.dash_from = kNoContactFrom;
-            add_contact(e, d.attacker, d.hit_index, kThrowHeld, 0.0);
-            continue;
-        }
-        resolve(m, s, d.attacker, d.move_index, d.defense_move, d.hit_index, d.contact, 0, e);
-    }
+    if (found0) apply_contact<0>(m, s, pend0, e);
+    if (found1) apply_contact<1>(m, s, pend1, e);
 
     const bool down0 = s.f[0].health <= 0.0;
     const bool down1 = s.f[1].health <= 0.0;

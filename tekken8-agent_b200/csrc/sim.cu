@@ -54,6 +54,7 @@ struct SimView {
     int32_t* p1;
     int32_t* p2;
     const uint8_t* learner_is_p1;
+    const uint32_t* side_order;  // fights with the learner on P1 first, then on P2
     float* aggression;
     const int32_t* pending_opponents;
     const float* pending_aggression;
@@ -115,17 +116,19 @@ __device__ __forceinline__ Match match_of(const Staged& st, int p1, int p2) {
     return m;
 }
 
-// observe_kernel (src/full_move_gpu.cu:131-166): both sides of one fight.
+// observe_kernel (src/full_move_gpu.cu:131-166): both sides of one fight, the learner on side L.
+template <int L>
 __device__ void write_observations(const SimView& v, const Staged& st, const Match& m, const Fight& s, size_t env,
-                                   int p1, int p2, int learner) {
+                                   int p1, int p2) {
     const EnvCfg& ec = *st.ecfg;
-    const int own = learner == 0 ? p1 : p2;
-    const int other = learner == 0 ? p2 : p1;
+    const int own = L == 0 ? p1 : p2;
+    const int other = L == 0 ? p2 : p1;
     float* lo = v.learner_obs + env * static_cast<size_t>(v.width);
     float* oo = v.opponent_obs + env * static_cast<size_t>(v.width);
     float buf[kObservationBase + 3];
+#pragma unroll
     for (int side = 0; side < 2; ++side) {
-        const int player = side == 0 ? learner : 1 - learner;
+        const int player = side == 0 ? L : 1 - L;
         const int me = side == 0 ? own : other;
         const int them = side == 0 ? other : own;
         observe(m, s, player, ec.max_round_frames, st.chars[me].roster_id, st.chars[them].roster_id, buf,
@@ -143,47 +146,88 @@ __device__ void write_observations(const SimView& v, const Staged& st, const Mat
     v.opponent_tables[env] = other;
 }
 
+__device__ __forceinline__ void write_observations(const SimView& v, const Staged& st, const Match& m, const Fight& s,
+                                                   size_t env, int p1, int p2, int learner) {
+    if (learner == 0) write_observations<0>(v, st, m, s, env, p1, p2);
+    else write_observations<1>(v, st, m, s, env, p1, p2);
+}
+
 __device__ __forceinline__ void add_frames(const SimView& v, unsigned long long frames) {
     // one atomic per warp
     for (int offset = 16; offset > 0; offset >>= 1) frames += __shfl_down_sync(0xffffffffu, frames, offset);
     if ((threadIdx.x & 31) == 0 && frames != 0) atomicAdd(v.frames, frames);
 }
 
-// env_step_kernel (src/full_move_gpu.cu:188-229) with the observation pass fused in.
-__global__ void __launch_bounds__(kStepThreads) k_step(SimView v, const int64_t* learner_candidates,
+// One fight's decision with the learner on side L: the state stays in registers through the
+// frame loop (every fighter index is a constant), then the outcome, tallies and observations.
+template <int L>
+__device__ __forceinline__ unsigned long long step_fight(const SimView& v, const Staged& st, size_t env,
+                                                         const int64_t* learner_candidates,
                                                          const int64_t* opponent_candidates, uint64_t seed,
                                                          uint64_t counter) {
+    const int p1 = v.p1[env], p2 = v.p2[env];
+    const Match m = match_of(st, p1, p2);
+    Fight s = v.states[env];
+    const float aggression = v.aggression[env];
+    const Noise* noise = v.noise != nullptr ? v.noise + env : nullptr;
+    const StepOut r = decision_as<L>(m, s, static_cast<int>(learner_candidates[env]),
+                                     opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1,
+                                     aggression, *st.ecfg, v.profiles, seed, env, counter, noise);
+    v.states[env] = s;
+    v.rewards[env] = r.reward;
+    v.sparse[env] = r.sparse;
+    v.terminated[env] = r.terminated ? 1 : 0;
+    v.outcomes[env] = static_cast<int8_t>(r.outcome);
+    if (r.terminated) {
+        const int opponent_character = L == 0 ? p2 : p1;
+        const int bucket = min(4, max(0, static_cast<int>(aggression * 4.0F + 0.5F)));
+        const int column = r.outcome > 0 ? 0 : (r.outcome < 0 ? 1 : 2);
+        atomicAdd(&v.tally[((opponent_character * 5 + bucket) * 2 + L) * 3 + column], 1u);
+        atomicAdd(&v.scenario_tally[v.scenarios[env] * 3 + column], 1u);
+        atomicAdd(&v.learner_tally[(L == 0 ? p1 : p2) * 3 + column], 1u);
+        const int bot = bot_id(aggression);
+        if (bot >= 0 && bot < T8B_SCRIPTED_PROFILES) atomicAdd(&v.bot_tally[bot * 3 + column], 1u);
+    }
+    write_observations<L>(v, st, m, s, env, p1, p2);
+    return static_cast<unsigned long long>(r.frames);
+}
+
+// env_step_kernel (src/full_move_gpu.cu:188-229) with the observation pass fused in.
+//
+// The frame loop is compiled once per learner side (step_fight<0>, step_fight<1>), and an SM
+// that runs both copies at once thrashes its instruction cache. So the grid is two blocks per
+// SM, each block takes the side its SM serves (SMs below the P1 share of the fights serve P1)
+// and pulls 128-fight chunks of that side (side_order lists P1-learner fights first) from a
+// per-side ticket; when its side runs out it helps with the other side.
+__global__ void __launch_bounds__(kStepThreads, 1) k_step(SimView v, const int64_t* learner_candidates,
+                                                            const int64_t* opponent_candidates, uint64_t seed,
+                                                            uint64_t counter, unsigned* tickets, uint32_t p1_fights) {
     const Staged st = stage_tables(v);
+    __shared__ unsigned chunk;
+    unsigned smid, nsmid;
+    asm("mov.u32 %0, %%smid;" : "=r"(smid));
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsmid));
+    int side = static_cast<uint64_t>(smid) * v.count < static_cast<uint64_t>(p1_fights) * nsmid ? 0 : 1;
     const unsigned lane = threadIdx.x & 31u;
-    const size_t env = static_cast<size_t>(blockIdx.x) * kStepFightsPerBlock + (threadIdx.x >> 5) * kStepLanes + lane;
+    const unsigned offset = (threadIdx.x >> 5) * kStepLanes + lane;
     unsigned long long frames = 0;
-    if (lane < kStepLanes && env < v.count) {
-        const int p1 = v.p1[env], p2 = v.p2[env];
-        const Match m = match_of(st, p1, p2);
-        const int learner = v.learner_is_p1[env] ? 0 : 1;
-        Fight s = v.states[env];
-        const float aggression = v.aggression[env];
-        const Noise* noise = v.noise != nullptr ? v.noise + env : nullptr;
-        const StepOut r = decision(m, s, learner, static_cast<int>(learner_candidates[env]),
-                                   opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1,
-                                   aggression, *st.ecfg, v.profiles, seed, env, counter, noise);
-        v.states[env] = s;
-        v.rewards[env] = r.reward;
-        v.sparse[env] = r.sparse;
-        v.terminated[env] = r.terminated ? 1 : 0;
-        v.outcomes[env] = static_cast<int8_t>(r.outcome);
-        frames = static_cast<unsigned long long>(r.frames);
-        if (r.terminated) {
-            const int opponent_character = learner == 0 ? p2 : p1;
-            const int bucket = min(4, max(0, static_cast<int>(aggression * 4.0F + 0.5F)));
-            const int column = r.outcome > 0 ? 0 : (r.outcome < 0 ? 1 : 2);
-            atomicAdd(&v.tally[((opponent_character * 5 + bucket) * 2 + learner) * 3 + column], 1u);
-            atomicAdd(&v.scenario_tally[v.scenarios[env] * 3 + column], 1u);
-            atomicAdd(&v.learner_tally[(learner == 0 ? p1 : p2) * 3 + column], 1u);
-            const int bot = bot_id(aggression);
-            if (bot >= 0 && bot < T8B_SCRIPTED_PROFILES) atomicAdd(&v.bot_tally[bot * 3 + column], 1u);
+    for (int sides_done = 0; sides_done < 2;) {
+        __syncthreads();
+        if (threadIdx.x == 0) chunk = atomicAdd(tickets + side, 1u);
+        __syncthreads();
+        const size_t first = static_cast<size_t>(chunk) * kStepFightsPerBlock;
+        const size_t count = side == 0 ? p1_fights : v.count - p1_fights;
+        if (first >= count) {
+            side ^= 1;
+            ++sides_done;
+            continue;
         }
-        write_observations(v, st, m, s, env, p1, p2, learner);
+        const size_t in_side = first + offset;
+        if (lane < kStepLanes && in_side < count) {
+            const size_t env = v.side_order[(side == 0 ? 0 : p1_fights) + in_side];
+            frames += side == 0 ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter)
+                                : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter);
+        }
     }
     add_frames(v, frames);
 }
@@ -670,6 +714,10 @@ struct t8b_sim {
     Buffer<double> x1, x2;
     Buffer<int32_t> p1, p2, pending_opponents, pending_learners, scenarios, pending_scenarios;
     Buffer<uint8_t> learner_is_p1, terminated, truncated;
+    Buffer<uint32_t> side_order;
+    Buffer<unsigned> step_tickets;
+    uint32_t p1_fights = 0;
+    int sm_count = 1;
     Buffer<float> aggression, pending_aggression;
     Buffer<Noise> noise;
     Buffer<float> learner_obs, opponent_obs;
@@ -686,6 +734,7 @@ struct t8b_sim {
         SimView v{};
         v.chars = chars.data(); v.cfg = cfg.data(); v.ecfg = ecfg.data(); v.profiles = profiles.data();
         v.states = states.data(); v.p1 = p1.data(); v.p2 = p2.data(); v.learner_is_p1 = learner_is_p1.data();
+        v.side_order = side_order.data();
         v.aggression = aggression.data(); v.pending_opponents = pending_opponents.data();
         v.pending_aggression = pending_aggression.data(); v.scenarios = scenarios.data();
         v.pending_scenarios = pending_scenarios.data(); v.pending_learners = pending_learners.data();
@@ -700,6 +749,19 @@ struct t8b_sim {
         return v;
     }
     size_t smem() const { return stage_bytes(roster); }
+    // Learner sides from the host, plus the fight order k_step walks: fights with the learner
+    // on P1 first, then those on P2 (each in index order).
+    void set_sides(const uint8_t* host) {
+        learner_is_p1.upload(host, n, stream);
+        std::vector<uint32_t> order;
+        order.reserve(n);
+        for (size_t i = 0; i < n; ++i) if (host[i]) order.push_back(static_cast<uint32_t>(i));
+        p1_fights = static_cast<uint32_t>(order.size());
+        for (size_t i = 0; i < n; ++i) if (!host[i]) order.push_back(static_cast<uint32_t>(i));
+        if (side_order.size() < n) side_order.allocate(n);
+        side_order.upload(order.data(), n, stream);
+        check(cudaStreamSynchronize(stream), "learner sides");
+    }
     void launched(const char* what) const { check(cudaGetLastError(), what); }
 
     void masks(const uint8_t* only) {
@@ -775,6 +837,11 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         if (config->memory) raise(T8B_EINVAL, "the --memory observation is not supported by this simulator");
         auto sim = std::make_unique<t8b_sim>();
         sim->n = environments;
+        {
+            int device = 0;
+            check(cudaGetDevice(&device), "cudaGetDevice");
+            check(cudaDeviceGetAttribute(&sim->sm_count, cudaDevAttrMultiProcessorCount, device), "SM count");
+        }
         sim->roster = roster_count;
         sim->config = *config;
         sim->width = kObservationBase + (config->live_noise ? T8B_NOISE_FEATURES : 0);
@@ -846,7 +913,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         const std::vector<int32_t> keep(n, -1);
         sim->pending_learners.upload(keep.data(), n, s);
         const std::vector<uint8_t> p1_learners(n, 1);
-        sim->learner_is_p1.upload(p1_learners.data(), n, s);
+        sim->set_sides(p1_learners.data());
         const std::vector<double> left(n, -0.8), right(n, 0.8);
         sim->x1.upload(left.data(), n, s);
         sim->x2.upload(right.data(), n, s);
@@ -936,8 +1003,7 @@ int t8b_sim_download_legal_mask(t8b_sim* sim, int player, uint8_t* out) {
 
 int t8b_sim_set_learner_sides(t8b_sim* sim, const uint8_t* learner_is_p1) {
     return with_sim(sim, [&](t8b_sim& s) {
-        s.learner_is_p1.upload(learner_is_p1, s.n, s.stream);
-        check(cudaStreamSynchronize(s.stream), "set learner sides");
+        s.set_sides(learner_is_p1);
     });
 }
 
@@ -996,7 +1062,11 @@ int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter) {
 int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
-        launch("k_step", k_step, blocks(s.n, kStepFightsPerBlock), kStepThreads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter);
+        if (s.step_tickets.size() == 0) s.step_tickets.allocate(2);
+        s.step_tickets.zero(s.stream);
+        const unsigned grid = std::min<unsigned>(blocks(s.n, kStepFightsPerBlock), 2u * static_cast<unsigned>(s.sm_count));
+        launch("k_step", k_step, grid, kStepThreads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter,
+               s.step_tickets.data(), s.p1_fights);
         s.launched("step");
         s.masks(nullptr);
     });
@@ -1094,7 +1164,7 @@ int t8b_sim_restore(t8b_sim* sim, const t8b_state_t* states, const int32_t* p1, 
         s.p1.upload(p1, s.n, s.stream);
         s.p2.upload(p2, s.n, s.stream);
         s.states.upload(reinterpret_cast<const Fight*>(states), s.n, s.stream);
-        s.learner_is_p1.upload(learner_is_p1, s.n, s.stream);
+        s.set_sides(learner_is_p1);
         s.aggression.upload(aggression, s.n, s.stream);
         s.pending_opponents.upload(pending_opponents, s.n, s.stream);
         s.pending_aggression.upload(pending_aggression, s.n, s.stream);
