@@ -8,7 +8,10 @@
 //              commits each stage back to empty[stage]; the accumulator of a finished tile is
 //              committed to acc_full[buffer];
 //   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (lane quarter = warp % 4), 32 columns
-//              at a time, handed to the epilogue functor; then acc_empty[buffer] frees the buffer.
+//              at a time, handed to the epilogue functor with an 8 KB warp-private shared-memory
+//              scratch (for staging a 32 x 32 chunk so global rows are read and written whole);
+//              the functor's prefetch of chunk c + 1 is issued before chunk c is loaded from
+//              tensor memory; then acc_empty[buffer] frees the buffer.
 // Two accumulator buffers of BN columns let the epilogue of tile i overlap the MMAs of tile i+1.
 // Operands are K-major (row-major [rows][K]) or MN-major (row-major [K][rows]); the MN-major form
 // lets weight gradients read activations [samples][features] directly with the samples as K.
@@ -108,6 +111,33 @@ __host__ __device__ constexpr uint32_t instr_desc(int n, bool a_mn, bool b_mn) {
         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
 }
 
+// What an epilogue functor sees for one 32 x 32 chunk of a tile (one warp, 32 rows).
+struct EpiCtx {
+    int row;      // this lane's row (row0 + lane)
+    int row0;     // first of the warp's 32 rows
+    int col0;     // first of the chunk's 32 columns
+    int split, tm, quarter, lane;
+    unsigned char* scratch;  // warp-private, kEpiWarpBytes
+    int buffer;   // prefetch buffer (0 or 1) holding this chunk's inputs
+    bool more;    // the next chunk's prefetch has been issued after this one's
+};
+constexpr int kEpiWarpBytes = 8192;
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Byte offset of 16-byte piece q of row r in a 32-row tile with `pieces` pieces per row,
+// rotated so that a warp writing one piece of 8 consecutive rows, or reading whole rows 8 at
+// a time, touches every bank once.
+__device__ __forceinline__ int staged_piece(int r, int q, int pieces) {
+    return pieces == 4 ? r * 64 + ((q ^ ((r >> 1) & 3)) << 4) : r * (pieces * 16) + ((q ^ (r & 7)) << 4);
+}
+
 struct Shape {
     int m, n, k;        // GEMM extents (m rows of A and C, n rows of B, k reduction)
     int tiles_m, tiles_n, splits;
@@ -120,9 +150,12 @@ struct Layout {
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+    // stages fill what the 227 KB of a CTA leaves after the epilogue scratch and barriers
+    static constexpr int kStageBudget = 232448 - 1024 - 256 - kEpiBytes;
+    static constexpr int kStages = kStageBudget / kStageBytes > 8 ? 8 : kStageBudget / kStageBytes;
     static constexpr int kTmemCols = 2 * BN <= 32 ? 32 : 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
-    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;
+    static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kEpiBytes + 256;
 };
 
 template <int BN, bool A_MN, bool B_MN, class Epi>
@@ -134,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) unsigned char raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     unsigned char* stages = base;
-    uint64_t* full = reinterpret_cast<uint64_t*>(base + L::kStages * L::kStageBytes);
+    unsigned char* epi_scratch = base + L::kStages * L::kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(epi_scratch + L::kEpiBytes);
     uint64_t* empty = full + L::kStages;
     uint64_t* acc_full = empty + L::kStages;
     uint64_t* acc_empty = acc_full + 2;
@@ -258,29 +292,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        unsigned char* scratch = epi_scratch + (warp - 2) * kEpiWarpBytes;
         int acc = 0;
         uint32_t acc_phase = 0;
         float v[32];
         for (int work = blockIdx.x; work < total && !*abort; work += gridDim.x) {
             int tm, tn, kb0, kb1, split;
             decode(work, tm, tn, kb0, kb1, split);
+            EpiCtx x;
+            x.row0 = tm * BM + quarter * 32;
+            x.row = x.row0 + lane;
+            x.split = split;
+            x.tm = tm;
+            x.quarter = quarter;
+            x.lane = lane;
+            x.scratch = scratch;
+            x.col0 = tn * BN;
+            x.buffer = 0;
+            epi.prefetch(x);
             if (!bar_wait(acc_full + acc, acc_phase, abort)) {
                 stop();
                 break;
             }
             fence_after();
             const uint32_t t = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-            const int row = tm * BM + row_in_tile;
             const bool empty_k = kb1 <= kb0;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
+                x.more = c + 1 < BN / 32;
+                if (x.more) {
+                    EpiCtx next = x;
+                    next.col0 = tn * BN + (c + 1) * 32;
+                    next.buffer = (c + 1) & 1;
+                    epi.prefetch(next);
+                }
                 tmem_load32(t + static_cast<uint32_t>(c * 32), v);
                 if (empty_k) {
 #pragma unroll
                     for (int i = 0; i < 32; ++i) v[i] = 0.0f;
                 }
-                epi(row, tn * BN + c * 32, v, split, tm, quarter, lane);
+                x.col0 = tn * BN + c * 32;
+                x.buffer = c & 1;
+                epi(x, v);
             }
             fence_before();
             bar_arrive(acc_empty + acc);

@@ -7,11 +7,13 @@ namespace t8b {
 
 // Split-K partials: part[split][row][col] (fp32), rows < m, cols < n.
 struct EpiPartial {
+    __device__ void prefetch(const tc::EpiCtx&) const {}
     float* part;
     int m, n;
-    __device__ void operator()(int row, int col0, const float* v, int split, int, int, int) const {
+    __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
+        const int row = x.row, col0 = x.col0;
         if (row >= m) return;
-        float* out = part + (static_cast<size_t>(split) * m + row) * n + col0;
+        float* out = part + (static_cast<size_t>(x.split) * m + row) * n + col0;
         if (col0 + 32 <= n && (n & 3) == 0) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);

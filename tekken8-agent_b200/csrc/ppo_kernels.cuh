@@ -121,81 +121,123 @@ __global__ void k_prep(Prep p) {
 }
 
 // ------------------------------------------------------------------ GEMM epilogues
+// Epilogue stores go through the warp's scratch: each lane writes its own row's 32 values,
+// then the warp writes 8 (bf16) or 4 (fp32) whole 64/128-byte row segments per instruction.
+__device__ __forceinline__ void store_rows_bf16(const tc::EpiCtx& x, const uint32_t* packed, __nv_bfloat16* out, int ld,
+                                                int m) {
+    unsigned char* stage = x.scratch + 4096;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        *reinterpret_cast<uint4*>(stage + tc::staged_piece(x.lane, q, 4)) =
+            make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int r = i * 8 + (x.lane >> 2), q = x.lane & 3;
+        const uint4 piece = *reinterpret_cast<const uint4*>(stage + tc::staged_piece(r, q, 4));
+        if (x.row0 + r < m) *reinterpret_cast<uint4*>(out + static_cast<size_t>(x.row0 + r) * ld + x.col0 + q * 8) = piece;
+    }
+    __syncwarp();
+}
+
 // Hidden layer forward: h = tanh(acc + b) as bf16 [rows][ld].
 struct EpiTanh {
+    __device__ void prefetch(const tc::EpiCtx&) const {}
     const float* bias;
     __nv_bfloat16* out;
     int ld, m;
-    __device__ void operator()(int row, int col0, const float* v, int, int, int, int) const {
-        if (row >= m) return;
+    __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
+        const float b = bias[x.col0 + x.lane];
         uint32_t packed[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-            const float a = tanh_fast(v[2 * i] + bias[col0 + 2 * i]);
-            const float b = tanh_fast(v[2 * i + 1] + bias[col0 + 2 * i + 1]);
-            __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+            const float a0 = tanh_fast(v[2 * i] + __shfl_sync(0xffffffffu, b, 2 * i));
+            const float a1 = tanh_fast(v[2 * i + 1] + __shfl_sync(0xffffffffu, b, 2 * i + 1));
+            __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
             packed[i] = *reinterpret_cast<uint32_t*>(&h);
         }
-        uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ld + col0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+        store_rows_bf16(x, packed, out, ld, m);
     }
 };
 
-// Output layer: o = acc + b for the valid columns, fp32 [rows][ld].
+// Output layer: o = acc + b for the valid columns (zero beyond), fp32 [rows][ld].
 struct EpiBias {
+    __device__ void prefetch(const tc::EpiCtx&) const {}
     const float* bias;
     float* out;
     int ld, m, valid;
-    __device__ void operator()(int row, int col0, const float* v, int, int, int, int) const {
-        if (row >= m) return;
-        float* dst = out + static_cast<size_t>(row) * ld + col0;
+    __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
+        const float b = x.col0 + x.lane < valid ? bias[x.col0 + x.lane] : 0.0f;
+        unsigned char* stage = x.scratch;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) dst[i] = col0 + i < valid ? v[i] + bias[col0 + i] : 0.0f;
+        for (int q = 0; q < 8; ++q) {
+            float o[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int i = 4 * q + k;
+                o[k] = x.col0 + i < valid ? v[i] + __shfl_sync(0xffffffffu, b, i) : 0.0f;
+            }
+            *reinterpret_cast<float4*>(stage + tc::staged_piece(x.lane, q, 8)) = make_float4(o[0], o[1], o[2], o[3]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (x.lane >> 3), q = x.lane & 7;
+            const float4 piece = *reinterpret_cast<const float4*>(stage + tc::staged_piece(r, q, 8));
+            if (x.row0 + r < m) *reinterpret_cast<float4*>(out + static_cast<size_t>(x.row0 + r) * ld + x.col0 + q * 4) = piece;
+        }
+        __syncwarp();
     }
 };
 
-// Backward through tanh: g = acc * (1 - h^2) as bf16 [rows][ld], plus per-32-row column sums of g
-// (fp32 [tile_m * 4 + quarter][ld]) for the bias gradient.
+// Backward through tanh: dz = g (1 - h^2) as bf16, and per (row tile, lane quarter) column
+// sums of dz (the bias gradient, reduced later in a fixed order). The h chunk is prefetched
+// with cp.async into one of two 2 KB buffers while the previous chunk is processed.
 struct EpiTanhGrad {
     const __nv_bfloat16* h;
     __nv_bfloat16* out;
     float* colsum;
     int ld, m;
-    __device__ void operator()(int row, int col0, const float* v, int, int tm, int quarter, int lane) const {
-        float g[32];
-        const bool live = row < m;
-        if (live) {
-            const uint4* src = reinterpret_cast<const uint4*>(h + static_cast<size_t>(row) * ld + col0);
+    __device__ void prefetch(const tc::EpiCtx& x) const {
+        unsigned char* buf = x.scratch + x.buffer * 2048;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 q = src[i];
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const __nv_bfloat162 pair = *reinterpret_cast<const __nv_bfloat162*>(&w[k]);
-                    const float2 f = __bfloat1622float2(pair);
-                    g[8 * i + 2 * k] = v[8 * i + 2 * k] * (1.0f - f.x * f.x);
-                    g[8 * i + 2 * k + 1] = v[8 * i + 2 * k + 1] * (1.0f - f.y * f.y);
-                }
-            }
-            uint32_t packed[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                __nv_bfloat162 pair = __floats2bfloat162_rn(g[2 * i], g[2 * i + 1]);
-                packed[i] = *reinterpret_cast<uint32_t*>(&pair);
-            }
-            uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * ld + col0);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) g[i] = 0.0f;
+        for (int i = 0; i < 4; ++i) {
+            const int r = i * 8 + (x.lane >> 2), q = x.lane & 3;
+            const bool valid = x.row0 + r < m;
+            const __nv_bfloat16* src = valid ? h + static_cast<size_t>(x.row0 + r) * ld + x.col0 + q * 8 : h;
+            tc::cp_async16(buf + tc::staged_piece(r, q, 4), src, valid);
         }
+        tc::cp_async_commit();
+    }
+    __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
+        if (x.more) tc::cp_async_wait<1>(); else tc::cp_async_wait<0>();
+        __syncwarp();
+        const unsigned char* buf = x.scratch + x.buffer * 2048;
+        const bool live = x.row < m;
+        float g[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint4 piece = *reinterpret_cast<const uint4*>(buf + tc::staged_piece(x.lane, q, 4));
+            const uint32_t w[4] = {piece.x, piece.y, piece.z, piece.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+                g[8 * q + 2 * k] = live ? v[8 * q + 2 * k] * (1.0f - f.x * f.x) : 0.0f;
+                g[8 * q + 2 * k + 1] = live ? v[8 * q + 2 * k + 1] * (1.0f - f.y * f.y) : 0.0f;
+            }
+        }
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            __nv_bfloat162 pair = __floats2bfloat162_rn(g[2 * i], g[2 * i + 1]);
+            packed[i] = *reinterpret_cast<uint32_t*>(&pair);
+        }
+        store_rows_bf16(x, packed, out, ld, m);
         // Transpose-reduce across the warp: after 5 halving steps lane c holds column c's sum.
 #pragma unroll
         for (int width = 16; width >= 1; width >>= 1) {
-            const bool upper = (lane & width) != 0;
+            const bool upper = (x.lane & width) != 0;
 #pragma unroll
             for (int i = 0; i < width; ++i) {
                 const float send = upper ? g[i] : g[i + width];
@@ -203,17 +245,18 @@ struct EpiTanhGrad {
                 g[i] = keep + __shfl_xor_sync(0xffffffffu, send, width);
             }
         }
-        colsum[(static_cast<size_t>(tm) * 4 + quarter) * ld + col0 + lane] = g[0];
+        colsum[(static_cast<size_t>(x.tm) * 4 + x.quarter) * ld + x.col0 + x.lane] = g[0];
     }
 };
 
 // Split-K partial of a weight gradient: part[split][row][col] (fp32).
 struct EpiSplit {
+    __device__ void prefetch(const tc::EpiCtx&) const {}
     float* part;
     int m, n;
-    __device__ void operator()(int row, int col0, const float* v, int split, int, int, int) const {
-        if (row >= m) return;
-        float* out = part + (static_cast<size_t>(split) * m + row) * n + col0;
+    __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
+        if (x.row >= m) return;
+        float* out = part + (static_cast<size_t>(x.split) * m + x.row) * n + x.col0;
 #pragma unroll
         for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
     }
