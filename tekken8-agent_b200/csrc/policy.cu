@@ -157,7 +157,7 @@ struct t8b_policy {
         for (int l = 0; l < layers; ++l) {
             const Operand a = l == 0 ? Operand{x.data(), m, padded, padded, false} : Operand{h[l - 1].data(), m, hidden, hidden, false};
             const Operand b{w_bf[l].data(), hidden, a.k, a.k, false};
-            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data(), hidden, m};
+            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data(), hidden, m, hidden};
             if (bn_hidden() == 256) dense<256>("gemm_forward_hidden", a, b, epi, stream); else dense<64>("gemm_forward_hidden", a, b, epi, stream);
         }
         const Operand a{h[layers - 1].data(), m, hidden, hidden, false};

@@ -141,21 +141,36 @@ __device__ __forceinline__ void store_rows_bf16(const tc::EpiCtx& x, const uint3
     __syncwarp();
 }
 
+// The chunk's 32 bias values, fetched asynchronously into the scratch at `at` (one 128 B
+// buffer per prefetch buffer); columns at or past `valid` read as zero.
+__device__ __forceinline__ void prefetch_bias(const tc::EpiCtx& x, const float* bias, int valid, int at) {
+    float* dst = reinterpret_cast<float*>(x.scratch + at + x.buffer * 128);
+    const bool ok = x.col0 + x.lane < valid;
+    tc::cp_async4(dst + x.lane, ok ? bias + x.col0 + x.lane : bias, ok);
+    tc::cp_async_commit();
+}
+__device__ __forceinline__ void wait_prefetch(const tc::EpiCtx& x) {
+    if (x.more) tc::cp_async_wait<1>(); else tc::cp_async_wait<0>();
+    __syncwarp();
+}
+
 // Hidden layer forward: h = tanh(acc + b) as bf16 [rows][ld].
 struct EpiTanh {
-    __device__ void prefetch(const tc::EpiCtx&) const {}
     const float* bias;
     __nv_bfloat16* out;
-    int ld, m;
+    int ld, m, cols;
+    __device__ void prefetch(const tc::EpiCtx& x) const { prefetch_bias(x, bias, cols, 0); }
     __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
-        const float b = bias[x.col0 + x.lane];
+        wait_prefetch(x);
+        const float4* b = reinterpret_cast<const float4*>(x.scratch + x.buffer * 128);
         uint32_t packed[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            const float a0 = tanh_fast(v[2 * i] + __shfl_sync(0xffffffffu, b, 2 * i));
-            const float a1 = tanh_fast(v[2 * i + 1] + __shfl_sync(0xffffffffu, b, 2 * i + 1));
-            __nv_bfloat162 h = __floats2bfloat162_rn(a0, a1);
-            packed[i] = *reinterpret_cast<uint32_t*>(&h);
+        for (int q = 0; q < 8; ++q) {
+            const float4 bq = b[q];
+            __nv_bfloat162 lo = __floats2bfloat162_rn(tanh_fast(v[4 * q] + bq.x), tanh_fast(v[4 * q + 1] + bq.y));
+            __nv_bfloat162 hi = __floats2bfloat162_rn(tanh_fast(v[4 * q + 2] + bq.z), tanh_fast(v[4 * q + 3] + bq.w));
+            packed[2 * q] = *reinterpret_cast<uint32_t*>(&lo);
+            packed[2 * q + 1] = *reinterpret_cast<uint32_t*>(&hi);
         }
         store_rows_bf16(x, packed, out, ld, m);
     }
@@ -163,22 +178,21 @@ struct EpiTanh {
 
 // Output layer: o = acc + b for the valid columns (zero beyond), fp32 [rows][ld].
 struct EpiBias {
-    __device__ void prefetch(const tc::EpiCtx&) const {}
     const float* bias;
     float* out;
     int ld, m, valid;
+    __device__ void prefetch(const tc::EpiCtx& x) const { prefetch_bias(x, bias, valid, 6144); }
     __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
-        const float b = x.col0 + x.lane < valid ? bias[x.col0 + x.lane] : 0.0f;
+        wait_prefetch(x);
+        const float4* b = reinterpret_cast<const float4*>(x.scratch + 6144 + x.buffer * 128);
         unsigned char* stage = x.scratch;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-            float o[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int i = 4 * q + k;
-                o[k] = x.col0 + i < valid ? v[i] + __shfl_sync(0xffffffffu, b, i) : 0.0f;
-            }
-            *reinterpret_cast<float4*>(stage + tc::staged_piece(x.lane, q, 8)) = make_float4(o[0], o[1], o[2], o[3]);
+            const float4 bq = b[q];
+            const int c = x.col0 + 4 * q;
+            const float4 o = make_float4(c < valid ? v[4 * q] + bq.x : 0.0f, c + 1 < valid ? v[4 * q + 1] + bq.y : 0.0f,
+                                         c + 2 < valid ? v[4 * q + 2] + bq.z : 0.0f, c + 3 < valid ? v[4 * q + 3] + bq.w : 0.0f);
+            *reinterpret_cast<float4*>(stage + tc::staged_piece(x.lane, q, 8)) = o;
         }
         __syncwarp();
 #pragma unroll
@@ -211,8 +225,7 @@ struct EpiTanhGrad {
         tc::cp_async_commit();
     }
     __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
-        if (x.more) tc::cp_async_wait<1>(); else tc::cp_async_wait<0>();
-        __syncwarp();
+        wait_prefetch(x);
         const unsigned char* buf = x.scratch + x.buffer * 2048;
         const bool live = x.row < m;
         float g[32];
