@@ -87,7 +87,23 @@ __global__ void k_prep(Prep p) {
     const size_t src = p.perm ? p.perm[p.offset + i] : p.offset + i;
     const float* row = p.obs + src * static_cast<size_t>(p.width);
     __nv_bfloat16* out = p.x + i * static_cast<size_t>(p.padded);
-    for (int j = lane; j < p.padded; j += 32) {
+    // the row's first 256 columns: every load issued before the first use
+    constexpr int kHeld = 8;
+    float held[kHeld];
+#pragma unroll
+    for (int k = 0; k < kHeld; ++k) {
+        const int j = lane + 32 * k;
+        held[k] = j < p.width ? row[j] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kHeld; ++k) {
+        const int j = lane + 32 * k;
+        if (j >= p.padded) break;
+        float v = held[k];
+        if (j < p.width && p.normalize) v = fminf(p.clip, fmaxf(-p.clip, (v - p.mean[j]) * p.istd[j]));
+        out[j] = __float2bfloat16_rn(v);
+    }
+    for (int j = lane + 32 * kHeld; j < p.padded; j += 32) {
         float v = 0.0f;
         if (j < p.width) {
             v = row[j];
