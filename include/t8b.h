@@ -394,6 +394,24 @@ int t8b_policy_update_ppo(t8b_policy* policy, const t8b_rollout_view_t* rollout,
  * the same std::shuffle permutations, ready when the update starts). */
 int t8b_policy_prepare_shuffle(t8b_policy* policy, size_t sample_count, int epochs, uint64_t shuffle_seed);
 int t8b_policy_set_comm(t8b_policy* policy, const t8b_comm_t* comm);
+/* save_checkpoint / load_checkpoint  ppo.hpp:162-166, the reference's .t8ppo format
+ * (src/ppo.cu:1704-1845): files written by either implementation load in the other. The
+ * contract's text fields are those of ActorCriticConfig (catalog_sha256, roster_version,
+ * observation_contract, action_contract); null means the reference's defaults. Saving
+ * refuses to overwrite an existing file (T8B_ESTATE) and non-finite tensors; loading checks
+ * the architecture, the contract, the normaliser block, the size and the FNV-1a checksum,
+ * adopts the file's normaliser setting, and with load_optimizer_state 0 zeroes Adam's moments
+ * and step. */
+typedef struct t8b_checkpoint_contract { /* CheckpointContract text (src/ppo.cu:1719-1726) */
+    char catalog_sha256[64];
+    char roster_version[24];
+    char observation_contract[32];
+    char action_contract[32];
+} t8b_checkpoint_contract_t;
+int t8b_policy_save_checkpoint(t8b_policy* policy, const char* path, const t8b_checkpoint_contract_t* contract,
+                               void* stream);
+int t8b_policy_load_checkpoint(t8b_policy* policy, const char* path, int load_optimizer_state,
+                               const t8b_checkpoint_contract_t* contract, void* stream);
 /* Parameters, gradients and Adam state in the canonical order w1, b1, ..., w_out, b_out
  * (the checkpoint payload of src/ppo.cu:1780-1845). */
 int t8b_policy_get_parameters(t8b_policy* policy, float* host, size_t count);

@@ -19,6 +19,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <filesystem>
+#include <fstream>
+#include <string>
 #include <memory>
 #include <numeric>
 #include <random>
@@ -964,6 +967,230 @@ int t8b_policy_set_observation_statistics(t8b_policy* p, const float* mean, cons
                                                            s.config.observation_epsilon);
         check(cudaStreamSynchronize(nullptr), "set observation statistics");
         s.obs_count = count;
+    });
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ checkpoints
+// The reference's .t8ppo file (src/ppo.cu:1704-1845), field for field so that checkpoints
+// move between the two implementations: a 40-byte header, the 160-byte contract block, the
+// 24-byte normaliser block (version 4+), the 16-byte integrity block and the payload
+// (parameters, Adam first and second moments in the canonical order, then the observation
+// mean and variance), checksummed with 64-bit FNV-1a over the payload bytes.
+namespace t8b {
+namespace ckpt {
+
+struct CkptHeader {
+    char magic[8];
+    uint32_t version, observation_size, action_count, hidden_size;
+    uint64_t optimizer_step, parameter_count;
+};
+struct CkptContract {
+    char catalog_sha256[64], roster_version[24], observation_contract[32], action_contract[32];
+    uint32_t action_feature_size, universal_action_count;
+};
+struct CkptNormalizer {
+    uint32_t enabled, architecture;
+    uint64_t count;
+    float clip, epsilon;
+};
+struct CkptIntegrity {
+    uint64_t payload_bytes, payload_checksum;
+};
+static_assert(sizeof(CkptHeader) == 40 && sizeof(CkptContract) == 160 && sizeof(CkptNormalizer) == 24 &&
+                  sizeof(CkptIntegrity) == 16,
+              "checkpoint blocks have the reference's sizes");
+
+constexpr char kCkptMagic[8] = {'T', '8', 'V', '2', 'P', 'P', 'O', '\0'};
+constexpr uint32_t kCkptVersion = 4, kCkptLayersVersion = 5;
+
+inline uint32_t architecture_code(const t8b_actor_config_t& c) {
+    if (c.shared_layers == 2 && c.head_layers == 0) return 0;
+    return (1u << 16) | static_cast<uint32_t>(c.shared_layers) | (static_cast<uint32_t>(c.head_layers) << 8);
+}
+
+inline uint64_t fnv1a(const std::vector<float>& payload) {
+    uint64_t h = 14695981039346656037ull;
+    const auto* bytes = reinterpret_cast<const unsigned char*>(payload.data());
+    for (size_t i = 0; i < payload.size() * sizeof(float); ++i) {
+        h ^= bytes[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+// The reference ActorCriticConfig's contract defaults (include/t8_v2/ppo.hpp:21-24).
+inline t8b_checkpoint_contract_t contract_or_default(const t8b_checkpoint_contract_t* c) {
+    if (c) return *c;
+    t8b_checkpoint_contract_t d{};
+    std::memset(d.catalog_sha256, '0', sizeof d.catalog_sha256);
+    std::memcpy(d.roster_version, "compatibility", 13);
+    std::memcpy(d.observation_contract, "v2-observation", 14);
+    std::memcpy(d.action_contract, "fixed-24-compatibility", 22);
+    return d;
+}
+
+template <size_t N>
+std::string text(const char (&field)[N]) {
+    size_t n = 0;
+    while (n < N && field[n] != '\0') ++n;
+    return std::string(field, n);
+}
+
+}  // namespace ckpt
+}  // namespace t8b
+
+extern "C" {
+
+int t8b_policy_save_checkpoint(t8b_policy* p, const char* path, const t8b_checkpoint_contract_t* contract, void* stream) {
+    using namespace t8b;
+    using namespace t8b::ckpt;
+    return with_policy(p, [&](t8b_policy& s) {
+        if (!path) raise(T8B_EINVAL, "null checkpoint path");
+        check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "synchronize before checkpoint save");
+        const size_t n = s.param_count, w = static_cast<size_t>(s.width);
+        std::vector<float> payload(3 * n + 2 * w);
+        s.params.download(payload.data(), n, nullptr);
+        s.m1.download(payload.data() + n, n, nullptr);
+        s.m2.download(payload.data() + 2 * n, n, nullptr);
+        s.obs_mean.download(payload.data() + 3 * n, w, nullptr);
+        s.obs_var.download(payload.data() + 3 * n + w, w, nullptr);
+        for (float v : payload) {
+            if (!std::isfinite(v)) raise(T8B_ENONFINITE, std::string("refusing to save checkpoint with non-finite tensors: ") + path);
+        }
+        const t8b_actor_config_t& c = s.config;
+        const uint32_t architecture = architecture_code(c);
+        CkptHeader header{};
+        std::memcpy(header.magic, kCkptMagic, 8);
+        header.version = architecture == 0 ? kCkptVersion : kCkptLayersVersion;
+        header.observation_size = static_cast<uint32_t>(c.observation_size);
+        header.action_count = static_cast<uint32_t>(c.action_count);
+        header.hidden_size = static_cast<uint32_t>(c.hidden_size);
+        header.optimizer_step = s.optimizer_step;
+        header.parameter_count = n;
+        const t8b_checkpoint_contract_t text_fields = contract_or_default(contract);
+        CkptContract block{};
+        std::memcpy(block.catalog_sha256, text_fields.catalog_sha256, 64);
+        std::memcpy(block.roster_version, text_fields.roster_version, 24);
+        std::memcpy(block.observation_contract, text_fields.observation_contract, 32);
+        std::memcpy(block.action_contract, text_fields.action_contract, 32);
+        block.action_feature_size = static_cast<uint32_t>(c.action_feature_size);
+        block.universal_action_count = static_cast<uint32_t>(c.universal_action_count);
+        const CkptNormalizer normalizer{c.observation_normalization ? 1u : 0u, architecture, s.obs_count,
+                                        c.observation_clip, c.observation_epsilon};
+        const CkptIntegrity integrity{payload.size() * sizeof(float), fnv1a(payload)};
+        const std::filesystem::path target(path);
+        if (!target.parent_path().empty()) std::filesystem::create_directories(target.parent_path());
+        if (std::filesystem::exists(target)) raise(T8B_ESTATE, std::string("refusing to overwrite checkpoint: ") + path);
+        std::filesystem::path temporary = target;
+        temporary += ".tmp";
+        std::error_code ignored;
+        std::filesystem::remove(temporary, ignored);
+        {
+            std::ofstream out(temporary, std::ios::binary | std::ios::trunc);
+            if (!out) raise(T8B_ECUDA, "could not open checkpoint for writing: " + temporary.string());
+            out.write(reinterpret_cast<const char*>(&header), sizeof header);
+            out.write(reinterpret_cast<const char*>(&block), sizeof block);
+            out.write(reinterpret_cast<const char*>(&normalizer), sizeof normalizer);
+            out.write(reinterpret_cast<const char*>(&integrity), sizeof integrity);
+            out.write(reinterpret_cast<const char*>(payload.data()), static_cast<std::streamsize>(payload.size() * sizeof(float)));
+            out.flush();
+            if (!out) raise(T8B_ECUDA, "checkpoint write failed: " + temporary.string());
+        }
+        std::filesystem::rename(temporary, target);
+    });
+}
+
+int t8b_policy_load_checkpoint(t8b_policy* p, const char* path, int load_optimizer_state,
+                               const t8b_checkpoint_contract_t* contract, void* stream) {
+    using namespace t8b;
+    using namespace t8b::ckpt;
+    return with_policy(p, [&](t8b_policy& s) {
+        if (!path) raise(T8B_EINVAL, "null checkpoint path");
+        const std::string where(path);
+        std::ifstream in(path, std::ios::binary);
+        if (!in) raise(T8B_ECUDA, "could not open checkpoint for reading: " + where);
+        t8b_actor_config_t& c = s.config;
+        CkptHeader header{};
+        in.read(reinterpret_cast<char*>(&header), sizeof header);
+        const bool magic = in && std::memcmp(header.magic, kCkptMagic, 8) == 0;
+        if (magic && header.version < 3) {
+            raise(T8B_ECUDA, "legacy fixed-action checkpoint is incompatible with the full-roster policy contract: " + where);
+        }
+        if (!magic || (header.version != 3 && header.version != kCkptVersion && header.version != kCkptLayersVersion) ||
+            header.observation_size != static_cast<uint32_t>(c.observation_size) ||
+            header.action_count != static_cast<uint32_t>(c.action_count) ||
+            header.hidden_size != static_cast<uint32_t>(c.hidden_size) || header.parameter_count != s.param_count) {
+            raise(T8B_ECUDA, "checkpoint architecture/version mismatch: " + where);
+        }
+        const t8b_checkpoint_contract_t want = contract_or_default(contract);
+        CkptContract block{};
+        in.read(reinterpret_cast<char*>(&block), sizeof block);
+        if (!in || text(block.catalog_sha256) != text(want.catalog_sha256) ||
+            text(block.roster_version) != text(want.roster_version) ||
+            text(block.observation_contract) != text(want.observation_contract) ||
+            text(block.action_contract) != text(want.action_contract) ||
+            block.action_feature_size != static_cast<uint32_t>(c.action_feature_size) ||
+            block.universal_action_count != static_cast<uint32_t>(c.universal_action_count)) {
+            raise(T8B_ECUDA, "checkpoint catalog/roster/action contract mismatch: " + where);
+        }
+        const bool has_normalizer = header.version >= 4;
+        CkptNormalizer normalizer{};
+        if (has_normalizer) {
+            in.read(reinterpret_cast<char*>(&normalizer), sizeof normalizer);
+            if (!in || normalizer.enabled > 1 || normalizer.architecture != architecture_code(c) ||
+                !std::isfinite(normalizer.clip) || normalizer.clip <= 0.0f || !std::isfinite(normalizer.epsilon) ||
+                normalizer.epsilon <= 0.0f) {
+                raise(T8B_ECUDA, "checkpoint observation normalizer block is invalid: " + where);
+            }
+        }
+        const size_t n = s.param_count, w = static_cast<size_t>(s.width);
+        const size_t count = 3 * n + (has_normalizer ? 2 * w : 0);
+        CkptIntegrity integrity{};
+        in.read(reinterpret_cast<char*>(&integrity), sizeof integrity);
+        if (!in || integrity.payload_bytes != count * sizeof(float)) raise(T8B_ECUDA, "checkpoint payload size mismatch: " + where);
+        std::vector<float> payload(count);
+        in.read(reinterpret_cast<char*>(payload.data()), static_cast<std::streamsize>(count * sizeof(float)));
+        if (!in) raise(T8B_ECUDA, "checkpoint tensor is truncated: " + where);
+        if (fnv1a(payload) != integrity.payload_checksum) raise(T8B_ECUDA, "checkpoint checksum mismatch: " + where);
+        for (float v : payload) {
+            if (!std::isfinite(v)) raise(T8B_ENONFINITE, "checkpoint contains non-finite tensors: " + where);
+        }
+        if (has_normalizer) {
+            for (size_t i = 0; i < w; ++i) {
+                if (payload[3 * n + w + i] < 0.0f) raise(T8B_ECUDA, "checkpoint observation variance is negative: " + where);
+            }
+        }
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        s.params.upload(payload.data(), n, st);
+        if (load_optimizer_state) {
+            s.m1.upload(payload.data() + n, n, st);
+            s.m2.upload(payload.data() + 2 * n, n, st);
+            s.optimizer_step = header.optimizer_step;
+        } else {
+            s.m1.zero(st);
+            s.m2.zero(st);
+            s.optimizer_step = 0;
+        }
+        if (has_normalizer) {
+            c.observation_normalization = static_cast<uint8_t>(normalizer.enabled);
+            c.observation_clip = normalizer.clip;
+            c.observation_epsilon = normalizer.epsilon;
+            s.obs_mean.upload(payload.data() + 3 * n, w, st);
+            s.obs_var.upload(payload.data() + 3 * n + w, w, st);
+            s.obs_count = normalizer.count;
+        } else {
+            c.observation_normalization = 0;
+            const std::vector<float> zeros(w, 0.0f), ones(w, 1.0f);
+            s.obs_mean.upload(zeros.data(), w, st);
+            s.obs_var.upload(ones.data(), w, st);
+            s.obs_count = 0;
+        }
+        launch("k_refresh_istd", ppo::k_refresh_istd, blocks(s.width, 128), 128, 0, st, s.obs_var.data(), s.obs_istd.data(),
+               s.width, c.observation_epsilon);
+        s.refresh_operands(st);
+        check(cudaStreamSynchronize(st), "synchronize checkpoint load");
     });
 }
 

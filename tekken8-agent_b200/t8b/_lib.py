@@ -283,11 +283,18 @@ class Comm(C.Structure):
                 ("world_size", C.c_int32), ("rank", C.c_int32)]
 
 
+class CheckpointContract(C.Structure):
+    _fields_ = [("catalog_sha256", C.c_char * 64), ("roster_version", C.c_char * 24),
+                ("observation_contract", C.c_char * 32), ("action_contract", C.c_char * 32)]
+
+
+SIZES.update({"t8b_checkpoint_contract_t": 152})
 SIZES.update({"t8b_actor_config_t": 44, "t8b_ppo_config_t": 56, "t8b_ppo_metrics_t": 56, "t8b_policy_output_t": 48,
               "t8b_rollout_view_t": 136, "t8b_comm_t": 32})
 for _name, _cls in (("t8b_actor_config_t", ActorConfig), ("t8b_ppo_config_t", PpoConfig),
                     ("t8b_ppo_metrics_t", PpoMetrics), ("t8b_policy_output_t", PolicyOutput),
-                    ("t8b_rollout_view_t", RolloutView), ("t8b_comm_t", Comm)):
+                    ("t8b_rollout_view_t", RolloutView), ("t8b_comm_t", Comm),
+                    ("t8b_checkpoint_contract_t", CheckpointContract)):
     assert C.sizeof(_cls) == SIZES[_name], (_name, C.sizeof(_cls))
 
 fp = C.POINTER(C.c_float)
@@ -310,6 +317,8 @@ PROTOTYPES.update({
                                         C.POINTER(PpoMetrics)]),
     "t8b_policy_prepare_shuffle": (C.c_int, [vp, C.c_size_t, C.c_int, u64]),
     "t8b_policy_set_comm": (C.c_int, [vp, C.POINTER(Comm)]),
+    "t8b_policy_save_checkpoint": (C.c_int, [vp, C.c_char_p, C.POINTER(CheckpointContract), vp]),
+    "t8b_policy_load_checkpoint": (C.c_int, [vp, C.c_char_p, C.c_int, C.POINTER(CheckpointContract), vp]),
     "t8b_policy_get_parameters": (C.c_int, [vp, vp, C.c_size_t]),
     "t8b_policy_set_parameters": (C.c_int, [vp, vp, C.c_size_t]),
     "t8b_policy_get_gradients": (C.c_int, [vp, vp, C.c_size_t]),

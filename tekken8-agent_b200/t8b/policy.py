@@ -9,7 +9,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import ActorConfig, PpoConfig, PpoMetrics, PolicyOutput, RolloutView, Comm, call
+from ._lib import ActorConfig, CheckpointContract, PpoConfig, PpoMetrics, PolicyOutput, RolloutView, Comm, call
 from .device import view, ptr
 
 
@@ -40,6 +40,14 @@ def _p(value):
     if isinstance(value, int):
         return value
     return ptr(value)
+
+
+def checkpoint_contract(catalog_sha256: str = "0" * 64, roster_version: str = "compatibility",
+                        observation_contract: str = "v2-observation",
+                        action_contract: str = "fixed-24-compatibility") -> CheckpointContract:
+    """The text fields a checkpoint must agree on (the reference ActorCriticConfig's defaults)."""
+    return CheckpointContract(catalog_sha256.encode(), roster_version.encode(), observation_contract.encode(),
+                              action_contract.encode())
 
 
 class TorchComm:
@@ -144,6 +152,17 @@ class GpuActorCritic:
     def set_comm(self, comm: TorchComm | None):
         self._comm = comm
         call("t8b_policy_set_comm", self._handle, C.byref(comm.struct) if comm else None)
+
+    def save_checkpoint(self, path, contract: CheckpointContract | None = None, stream=None):
+        """GpuActorCritic::save_checkpoint: the reference's .t8ppo file (refuses to overwrite)."""
+        call("t8b_policy_save_checkpoint", self._handle, str(path).encode(), C.byref(contract) if contract else None,
+             stream)
+
+    def load_checkpoint(self, path, load_optimizer_state: bool = True, contract: CheckpointContract | None = None,
+                        stream=None):
+        """GpuActorCritic::load_checkpoint; adopts the file's observation-normaliser setting."""
+        call("t8b_policy_load_checkpoint", self._handle, str(path).encode(), 1 if load_optimizer_state else 0,
+             C.byref(contract) if contract else None, stream)
 
     def _host(self, name, count, dtype=np.float32):
         out = np.zeros(count, dtype)

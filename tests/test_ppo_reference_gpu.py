@@ -1,0 +1,225 @@
+"""The library's policy, PPO update, rollout statistics and checkpoints against the reference's
+own GpuActorCritic / GpuRolloutBuffer (src/ppo.cu built for sm_100a by oracle/Makefile and run
+on the same GPU with the same inputs).
+
+Tolerances: the reference runs with matmul_precision "bf16" (multiply inputs rounded to bf16,
+fp32 accumulation in cuBLAS), the library on tcgen05 with the same rounding and its own
+accumulation order and tanh; network outputs agree within 2e-2 (relative norm), sampled
+actions in at least 98 % of samples (a different last bit moves a few inverse-CDF
+boundaries), and one well-conditioned PPO update's parameter change and gradient norm within
+5e-2 (relative norm). Initial weights, checkpoint files and GAE are compared exactly or to
+fp32 rounding."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ref():
+    from oracle import ppo_ref_run
+    try:
+        ppo_ref_run.lib()
+    except (OSError, RuntimeError) as error:
+        pytest.fail(f"reference PPO library unavailable: {error}")
+    return ppo_ref_run
+
+
+@pytest.fixture(scope="module")
+def features(roster):
+    return roster.feature_tables()
+
+
+def relative(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def batch(n, tables, rng, width=151):
+    from test_ppo_gpu import make_batch
+    return make_batch(n, tables, rng, width)
+
+
+def test_initial_weights_equal_the_reference(cuda, ref, features, tmp_path):
+    """Orthogonal initialisation from the same seed gives the reference's weights bit for bit
+    (read back through the reference's own checkpoint file)."""
+    from t8b.policy import GpuActorCritic, actor_config
+    actor = actor_config()
+    theirs = ref.RefPolicy(ref.config_from(actor), 256, 2027)
+    theirs.save(tmp_path / "reference.t8ppo")
+    ours = GpuActorCritic(256, actor, seed=2027)
+    loaded = GpuActorCritic(256, actor, seed=5)
+    loaded.load_checkpoint(tmp_path / "reference.t8ppo")
+    assert theirs.parameter_count() == ours.parameter_count()
+    assert np.array_equal(loaded.parameters(), ours.parameters())
+
+
+def test_checkpoint_files_are_interchangeable(cuda, ref, features, tmp_path):
+    """A library checkpoint (trained weights, Adam state, normaliser) loads in the reference,
+    whose re-save is byte-identical; a reference checkpoint loads back in the library."""
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config, ppo_config
+    from test_ppo_gpu import rollout_inputs, view_of
+    actor = actor_config()
+    ours = GpuActorCritic(2048, actor, seed=11)
+    ours.set_action_feature_tables(features)
+    arrays = rollout_inputs(ours, features, 2048, np.random.default_rng(4))
+    view, keep = view_of(arrays)
+    ours.update_ppo(view, ppo_config(epochs=1, minibatch_size=1024, target_kl=0.0), shuffle_seed=3)
+    torch.cuda.synchronize()
+    ours.save_checkpoint(tmp_path / "ours.t8ppo")
+    theirs = ref.RefPolicy(ref.config_from(actor), 256, 99)
+    theirs.load(tmp_path / "ours.t8ppo")
+    theirs.save(tmp_path / "theirs.t8ppo")
+    assert (tmp_path / "ours.t8ppo").read_bytes() == (tmp_path / "theirs.t8ppo").read_bytes()
+    back = GpuActorCritic(256, actor, seed=5)
+    back.load_checkpoint(tmp_path / "theirs.t8ppo")
+    assert np.array_equal(back.parameters(), ours.parameters())
+    m1, m2, step = ours.optimizer_state()
+    b1, b2, bstep = back.optimizer_state()
+    assert step == bstep == 2 and np.array_equal(m1, b1) and np.array_equal(m2, b2)
+    assert np.array_equal(back.observation_statistics()[0], ours.observation_statistics()[0])
+    fresh = GpuActorCritic(256, actor, seed=5)
+    fresh.load_checkpoint(tmp_path / "theirs.t8ppo", load_optimizer_state=False)
+    f1, f2, fstep = fresh.optimizer_state()
+    assert fstep == 0 and not f1.any() and not f2.any()
+
+
+def test_checkpoint_rejections(cuda, features, tmp_path):
+    from t8b._lib import T8bError
+    from t8b.policy import GpuActorCritic, actor_config, checkpoint_contract
+    policy = GpuActorCritic(256, actor_config(), seed=1)
+    path = tmp_path / "a.t8ppo"
+    policy.save_checkpoint(path)
+    with pytest.raises(T8bError):
+        policy.save_checkpoint(path)  # refuses to overwrite
+    with pytest.raises(T8bError):
+        policy.load_checkpoint(path, contract=checkpoint_contract(roster_version="other"))
+    raw = bytearray(path.read_bytes())
+    raw[-5] ^= 0x40
+    (tmp_path / "b.t8ppo").write_bytes(bytes(raw))
+    with pytest.raises(T8bError, match="checksum"):
+        policy.load_checkpoint(tmp_path / "b.t8ppo")
+    with pytest.raises(T8bError, match="architecture"):
+        GpuActorCritic(256, actor_config(hidden_size=256), seed=1).load_checkpoint(path)
+
+
+def test_forward_matches_the_reference(cuda, ref, features, tmp_path):
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config
+    actor = actor_config()
+    n = 8192
+    theirs = ref.RefPolicy(ref.config_from(actor), n, 2027)
+    theirs.set_features(features)
+    ours = GpuActorCritic(n, actor, seed=2027)
+    ours.set_action_feature_tables(features)
+    rng = np.random.default_rng(21)
+    # larger query weights so the policy is far from uniform
+    p = ours.parameters()
+    p[-(512 * 33 + 33):] *= 40.0
+    ours.set_parameters(p)
+    ours.save_checkpoint(tmp_path / "w.t8ppo")
+    theirs.load(tmp_path / "w.t8ppo")
+    obs, tables, masks = batch(n, features.shape[0], rng)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    for deterministic in (False, True):
+        got = ours.forward(d(obs), d(masks), n, seed=7, step=3, deterministic=deterministic, tables=d(tables))
+        want = theirs.forward(d(obs), d(masks), n, 7, 3, deterministic, d(tables))
+        values = got["values"].cpu().numpy()
+        assert relative(values, want["values"]) < 2e-2
+        assert relative(got["entropies"].cpu().numpy(), want["entropies"]) < 2e-2
+        actions = got["actions"].cpu().numpy()
+        same = actions == want["actions"]
+        assert same.mean() >= 0.98, same.mean()
+        lp = got["log_probabilities"].cpu().numpy()
+        assert relative(lp[same], want["log_probabilities"][same]) < 2e-2
+
+
+def test_update_matches_the_reference(cuda, ref, features, tmp_path):
+    """One update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
+    weights on the same rollout agrees with the reference's. The comparison is made well
+    conditioned: advantages are all positive and returns sit above the values, so the batch
+    gradient does not cancel, and Adam's epsilon is 1, which keeps the step near-linear in the
+    gradient (with the default 1e-5 the first Adam steps are close to lr * sign(gradient), and
+    the sign of near-zero components is rounding noise in either implementation)."""
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config, ppo_config
+    from test_ppo_gpu import rollout_inputs, view_of
+    actor = actor_config()
+    n = 8192
+    ours = GpuActorCritic(n, actor, seed=7)
+    ours.set_action_feature_tables(features)
+    p = ours.parameters()
+    p[-(512 * 33 + 33):] *= 30.0
+    ours.set_parameters(p)
+    before = ours.parameters().astype(np.float64)
+    ours.save_checkpoint(tmp_path / "start.t8ppo")
+    theirs = ref.RefPolicy(ref.config_from(actor), n, 1)
+    theirs.set_features(features)
+    theirs.load(tmp_path / "start.t8ppo")
+    rng = np.random.default_rng(31)
+    obs, tables, masks, actions, old_lp, old_v, adv, ret = rollout_inputs(ours, features, n, rng)
+    adv = (np.abs(adv) + 0.5).astype(np.float32)
+    ret = (old_v + 1.0).astype(np.float32)
+    arrays = (obs, tables, masks, actions, old_lp, old_v, adv, ret)
+    view, keep = view_of(arrays)
+    cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3, adam_epsilon=1.0)
+    got = ours.update_ppo(view, cfg, shuffle_seed=17)
+    zeros_f = torch.zeros(n, device="cuda")
+    zeros_b = torch.zeros(n, dtype=torch.uint8, device="cuda")
+    obs_t, masks_t, actions_t, lp_t, v_t, adv_t, ret_t, tables_t = keep
+    pointers = [obs_t.data_ptr(), masks_t.data_ptr(), actions_t.data_ptr(), lp_t.data_ptr(), v_t.data_ptr(),
+                zeros_f.data_ptr(), zeros_b.data_ptr(), zeros_b.data_ptr(), zeros_f.data_ptr(), adv_t.data_ptr(),
+                ret_t.data_ptr(), tables_t.data_ptr(), None]
+    ppo = ref.Ppo(cfg.epochs, cfg.minibatch_size, cfg.learning_rate, cfg.clip_range, cfg.value_clip_range,
+                  cfg.target_kl, cfg.value_coefficient, cfg.entropy_coefficient, cfg.max_gradient_norm,
+                  cfg.adam_beta1, cfg.adam_beta2, cfg.adam_epsilon)
+    want = theirs.update(pointers, n, 1, n, ppo, 17)
+    theirs.save(tmp_path / "after.t8ppo")
+    after = GpuActorCritic(256, actor, seed=3)
+    after.load_checkpoint(tmp_path / "after.t8ppo")
+    delta_ref = after.parameters().astype(np.float64) - before
+    delta_ours = ours.parameters().astype(np.float64) - before
+    assert relative(delta_ours, delta_ref) < 5e-2, relative(delta_ours, delta_ref)
+    for key in ("policy_loss", "value_loss", "entropy", "clip_fraction", "decision_fraction"):
+        assert abs(got[key] - want[key]) <= 2e-2 * max(1.0, abs(want[key])), (key, got[key], want[key])
+    # the pre-clip norm of the minibatch gradients, dominated by bf16-rounded activations
+    assert abs(got["gradient_norm"] - want["gradient_norm"]) <= 5e-2 * want["gradient_norm"]
+    assert got["minibatches"] == want["minibatches"] == 8
+    mean_ours = ours.observation_statistics()[0]
+    mean_ref = theirs.observation_statistics()[0]
+    assert np.allclose(mean_ours, mean_ref, rtol=1e-5, atol=1e-6)
+
+
+def test_gae_and_reward_normalisation_match_the_reference(cuda, ref):
+    import torch
+    from t8b.policy import GpuRolloutBuffer, actor_config
+    rng = np.random.default_rng(5)
+    t, n = 64, 4096
+    actor = actor_config()
+    ours = GpuRolloutBuffer(n, t, actor)
+    theirs = ref.RefRollout(n, t, ref.config_from(actor))
+    rewards = torch.as_tensor(rng.normal(scale=0.3, size=(t, n)).astype(np.float32), device="cuda")
+    values = torch.as_tensor(rng.normal(size=(t, n)).astype(np.float32), device="cuda")
+    done = torch.as_tensor((rng.random((t, n)) < 1 / 60).astype(np.uint8), device="cuda")
+    trunc = torch.as_tensor(((rng.random((t, n)) < 0.3) & (done.cpu().numpy() == 1)).astype(np.uint8), device="cuda")
+    for step in range(t):
+        ours.record_outcome_device(step, rewards[step], done[step], trunc[step], values[step])
+        theirs.record_outcome(step, rewards[step], done[step], trunc[step], values[step])
+    # old values feed the returns: record them through the policy side of both buffers
+    obs = torch.zeros((n, 151), device="cuda")
+    masks = torch.ones((n, 368), dtype=torch.uint8, device="cuda")
+    actions = torch.zeros(n, dtype=torch.int64, device="cuda")
+    lp = torch.zeros(n, device="cuda")
+    for step in range(t):
+        ours.record_policy_device(step, obs, masks, actions, lp, values[step])
+        theirs.record_policy(step, obs, masks, actions, lp, values[step])
+    std_ours = ours.normalize_rewards(0.99)
+    std_ref = theirs.normalize_rewards(0.99)
+    assert abs(std_ours - std_ref) <= 1e-6 * abs(std_ref)
+    ours.compute_gae(0.99, 0.95, True)
+    theirs.compute_gae(0.99, 0.95, True)
+    adv_ref, ret_ref, rew_ref = theirs.download()
+    assert np.allclose(ours.tensor("rewards").cpu().numpy(), rew_ref, rtol=1e-6, atol=1e-7)
+    assert np.allclose(ours.tensor("advantages").cpu().numpy(), adv_ref, rtol=1e-4, atol=1e-5)
+    assert np.allclose(ours.tensor("returns").cpu().numpy(), ret_ref, rtol=1e-4, atol=1e-5)
