@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--self-play", action="store_true",
+                    help="mirror self-play: a frozen copy of the initial policy plays the other side")
     return ap.parse_args()
 
 
@@ -243,8 +245,15 @@ def run_ours(args):
     from t8b.sim import GpuFullMoveSimulator  # noqa: F401  (loads the library)
     from t8b import profile
     roster = roster_module.parse(roster_raw())
+    opponent = None
+    if args.self_play:
+        import tempfile
+        from t8b.policy import GpuActorCritic, actor_config
+        frozen = GpuActorCritic(args.envs, actor_config(), 3)
+        opponent = Path(tempfile.mkdtemp()) / f"opponent_rank{rank}.t8ppo"
+        frozen.save_checkpoint(opponent)
     trainer = SelfPlayTrainer(roster, environments=args.envs, horizon=args.horizon, epochs=args.epochs,
-                              minibatches=args.minibatches, seed=3, comm=comm, rank=rank)
+                              minibatches=args.minibatches, seed=3, comm=comm, rank=rank, opponent=opponent)
     for _ in range(args.warmup):
         trainer.host_boundary()
         trainer.iterate()
@@ -301,7 +310,8 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "f64 engine, bf16 tensor-core policy (fp32 accumulate, fp32 master weights)",
         "data": "synthetic (41-fighter roster tables from the reference loader; random-init policy)",
         "config": {"workload": "config 4: self-play iteration, 32,768 fights/GPU, T=128, 4 epochs x 8 minibatches, "
-                               "screen view + live noise, scripted opponents",
+                               "screen view + live noise, " +
+                               ("mirror self-play against a frozen policy" if args.self_play else "scripted opponents"),
                    "envs_per_gpu": args.envs, "horizon": args.horizon, "epochs": args.epochs,
                    "minibatch": args.envs * args.horizon // args.minibatches, "parallelism": f"dp{world}",
                    "l2": "inputs larger than L2 (rollout buffers > 4 GB per GPU)", "target_kl": "off (full 4 epochs)"},

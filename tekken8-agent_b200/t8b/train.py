@@ -34,8 +34,13 @@ def config4_env(**overrides):
 
 
 class SelfPlayTrainer:
+    """With `opponent` (a checkpoint path, or a GpuActorCritic) the fights are mirror self-play:
+    the frozen policy plays the other side from the opponent observations, masks and feature
+    tables (src/full_move_train.cpp:1333-1358, 1382-1387), on a second stream that overlaps the
+    learner's forward; otherwise scripted opponents play."""
+
     def __init__(self, roster, environments=32768, horizon=128, epochs=4, minibatches=8, seed=3, hidden=512,
-                 layers=2, env=None, comm=None, rank=0, target_kl=0.0, scenario_share=0.25):
+                 layers=2, env=None, comm=None, rank=0, target_kl=0.0, scenario_share=0.25, opponent=None):
         self.roster = roster
         self.n = environments
         self.horizon = horizon
@@ -55,6 +60,15 @@ class SelfPlayTrainer:
             self.rollout.set_comm(comm)
         self.ppo = ppo_config(epochs=epochs, minibatch_size=self.minibatch, learning_rate=5e-4, target_kl=target_kl,
                               entropy_coefficient=0.01)
+        self.opponent = None
+        if opponent is not None:
+            if isinstance(opponent, GpuActorCritic):
+                self.opponent = opponent
+            else:
+                self.opponent = GpuActorCritic(environments, self.actor, seed + 1)
+                self.opponent.load_checkpoint(opponent, load_optimizer_state=False)
+            self.opponent.set_action_feature_tables(roster.feature_tables())
+            self.opponent_stream = torch.cuda.Stream()
         rng = np.random.default_rng(self.seed)
         count = len(roster)
         self.sides = (np.arange(environments) % 2 == 0).astype(np.uint8)
@@ -77,6 +91,9 @@ class SelfPlayTrainer:
         starts (src/full_move_train.cpp schedule_opponents)."""
         rng = self.rng
         opponents = rng.integers(0, len(self.roster), self.n).astype(np.int32)
+        if self.opponent is not None:
+            # self-play rounds start neutral, at the fixed aggression the reference gives them
+            return opponents, np.full(self.n, 0.5, np.float32), np.zeros(self.n, np.int32)
         aggression = rng.random(self.n).astype(np.float32)
         scenarios = np.where(rng.random(self.n) < self.scenario_share, rng.integers(1, 9, self.n), 0).astype(np.int32)
         return opponents, aggression, scenarios
@@ -98,12 +115,15 @@ class SelfPlayTrainer:
         for step in range(t):
             counter = update * t + step
             obs, bits = sim.learner_observations(), sim.learner_mask_bits()
+            opponent_actions = self.opponent_launch(counter) if self.opponent is not None else None
             out = policy.forward(obs, None, n, self.seed + 1, counter, False, None, tables, mask_bits=bits)
             if step > 0:
                 rollout.record_outcome_device(step - 1, sim.rewards(), sim.terminated(), sim.truncated(), out["values"])
             rollout.record_policy_device(step, obs, None, out["actions"], out["log_probabilities"], out["values"],
                                          None, tables, out["entropies"], mask_bits=bits)
-            sim.step(out["actions"], None, self.seed, counter + 1)
+            if opponent_actions is not None:
+                torch.cuda.current_stream().wait_stream(self.opponent_stream)
+            sim.step(out["actions"], opponent_actions, self.seed, counter + 1)
             if step == t - 1:
                 last = policy.forward(sim.learner_observations(), None, n, self.seed + 3, counter, True, None, tables,
                                       mask_bits=sim.learner_mask_bits())
@@ -115,6 +135,18 @@ class SelfPlayTrainer:
         rollout.normalize_rewards(0.99)
         rollout.compute_gae(0.99, 0.95, True)
         return policy.update_ppo(rollout.device_view(packed=True), self.ppo, self.seed + update)
+
+    def opponent_launch(self, counter):
+        """Enqueues the frozen policy's forward for this decision on the opponent stream, after
+        the simulator's last step; it overlaps the learner's forward, and the caller makes the
+        main stream wait for it before stepping the simulator."""
+        side = self.opponent_stream
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            out = self.opponent.forward(self.sim.opponent_observations(), None, self.n, self.seed + 2, counter, False,
+                                        side.cuda_stream, self.sim.opponent_feature_tables(),
+                                        mask_bits=self.sim.opponent_mask_bits())
+        return out["actions"]
 
     def host_boundary(self):
         """The per-update host traffic of the reference trainer (schedule upload, tally and

@@ -236,3 +236,23 @@ def test_snapshot_restore_round_trip(cuda, roster):
     # observations are recomputed from the restored state (noise levels are redrawn, as the reference)
     assert other.learner_observations().shape == (n, 151)
     assert np.array_equal(other.learner_masks().cpu().numpy(), sim.learner_masks().cpu().numpy())
+
+
+def test_self_play_iteration_with_a_checkpoint_opponent(cuda, roster, tmp_path):
+    """Mirror self-play: a frozen policy loaded from a .t8ppo file plays the other side from the
+    opponent observations on its own stream; an iteration runs and is reproducible."""
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config
+    from t8b.train import SelfPlayTrainer
+    frozen = GpuActorCritic(1024, actor_config(), 41)
+    frozen.save_checkpoint(tmp_path / "frozen.t8ppo")
+    results = []
+    for _ in range(2):
+        trainer = SelfPlayTrainer(roster, environments=1024, horizon=8, epochs=1, minibatches=2, seed=5,
+                                  opponent=tmp_path / "frozen.t8ppo")
+        metrics = trainer.iterate()
+        torch.cuda.synchronize()
+        assert all(np.isfinite(v) for v in metrics.values())
+        results.append((trainer.policy.parameters(), trainer.sim.download_state_bytes()))
+    assert np.array_equal(results[0][0], results[1][0])
+    assert np.array_equal(results[0][1], results[1][1])
