@@ -275,8 +275,8 @@ std::vector<std::vector<uint32_t>> make_permutations(size_t count, int epochs, u
 }
 
 __global__ void k_validate(const float* obs, int width, const uint8_t* bytes, const uint32_t* bits,
-                           const int64_t* actions, const float* lp, const float* v, const float* adv, const float* ret,
-                           size_t n, int* invalid) {
+                           int actions_per_sample, const int64_t* actions, const float* lp, const float* v,
+                           const float* adv, const float* ret, size_t n, int* invalid) {
     const size_t s = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (s >= n) return;
     bool finite = isfinite(lp[s]) && isfinite(v[s]) && isfinite(adv[s]) && isfinite(ret[s]);
@@ -290,19 +290,21 @@ __global__ void k_validate(const float* obs, int width, const uint8_t* bytes, co
             word = bits[s * 12 + w];
         } else {
             word = 0;
-            for (int b = 0; b < 32 && w * 32 + b < 368; ++b) word |= (bytes[s * 368 + w * 32 + b] != 0 ? 1u : 0u) << b;
+            for (int b = 0; b < 32 && w * 32 + b < actions_per_sample; ++b) {
+                word |= (bytes[s * actions_per_sample + w * 32 + b] != 0 ? 1u : 0u) << b;
+            }
         }
         any = any || word != 0;
         if (a >= w * 32 && a < w * 32 + 32) chosen = (word >> (a - w * 32)) & 1u;
     }
-    const bool valid = a >= 0 && a < 368 && ((any && chosen) || (!any && a == 0));
+    const bool valid = a >= 0 && a < actions_per_sample && ((any && chosen) || (!any && a == 0));
     if (!finite || !valid) atomicExch(invalid, 1);
 }
 
 // decision_flags_kernel + deterministic_decision_entropy_kernel (src/ppo.cu:570-610), multi-block:
 // per-block fp64 (entropy sum, decision count) in index order, then a fixed-order total.
 __global__ void k_decision_partials(const float* entropy, const uint8_t* decision, const uint8_t* bytes,
-                                    const uint32_t* bits, size_t n, double* partial) {
+                                    const uint32_t* bits, int actions_per_sample, size_t n, double* partial) {
     __shared__ double se[256], sd[256];
     double e = 0.0, d = 0.0;
     for (size_t s = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; s < n;
@@ -316,7 +318,9 @@ __global__ void k_decision_partials(const float* entropy, const uint8_t* decisio
                 if (bits) {
                     legal += __popc(bits[s * 12 + w]);
                 } else {
-                    for (int b = 0; b < 32 && w * 32 + b < 368; ++b) legal += bytes[s * 368 + w * 32 + b] != 0;
+                    for (int b = 0; b < 32 && w * 32 + b < actions_per_sample; ++b) {
+                        legal += bytes[s * actions_per_sample + w * 32 + b] != 0;
+                    }
                 }
             }
             choice = legal > 1;
@@ -431,8 +435,8 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
             raise(T8B_EINVAL, "actor-critic depth must be 1-8 shared layers and 0-6 head layers");
         }
         if (c.head_layers != 0) raise(T8B_EINVAL, "separate policy/value heads are not supported by this library");
-        if (c.action_feature_size != T8B_FEATURE_SIZE || c.action_count != T8B_MAX_CANDIDATES) {
-            raise(T8B_EINVAL, "this library implements the parametric full-move head (368 candidates x 32 features)");
+        if ((c.action_feature_size != 32 && c.action_feature_size != 48) || c.action_count > T8B_MAX_CANDIDATES) {
+            raise(T8B_EINVAL, "this library implements the parametric head with 32 or 48 features and at most 368 candidates");
         }
         if (c.hidden_size % 64 != 0 || c.hidden_size % tc::BM != 0) raise(T8B_EINVAL, "hidden_size must be a multiple of 128");
         if (!std::isfinite(c.observation_clip) || c.observation_clip <= 0.0f || !std::isfinite(c.observation_epsilon) ||
@@ -505,13 +509,15 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
         p->dout.allocate(cap * kOutPad);
         const size_t partial_rows = std::max((cap + ppo::kWarps - 1) / ppo::kWarps, loss_blocks(cap));
         p->out_colsum.allocate(partial_rows * kOutPad);
-        check(cudaFuncSetAttribute(ppo::k_loss, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kTableBytes),
+        check(cudaFuncSetAttribute(ppo::k_loss<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kMaxTableBytes),
+              "objective shared memory");
+        check(cudaFuncSetAttribute(ppo::k_loss<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kMaxTableBytes),
               "objective shared memory");
         const size_t sms = static_cast<size_t>(sm_count());
         const size_t part = std::max({sms * p->hidden * kOutPad, sms * static_cast<size_t>(p->hidden) * p->hidden,
                                       sms * static_cast<size_t>(p->hidden) * p->padded});
         p->split_part.allocate(part);
-        p->logits.allocate(cap * T8B_MAX_CANDIDATES);
+        p->logits.allocate(cap * static_cast<size_t>(c.action_count));
         p->log_probs.allocate(cap);
         p->values.allocate(cap);
         p->entropies.allocate(cap);
@@ -579,7 +585,7 @@ int t8b_policy_action_feature_tables(const t8b_policy* p) { return p ? p->tables
 int t8b_policy_set_action_feature_tables(t8b_policy* p, const float* features, int tables, void* stream) {
     return with_policy(p, [&](t8b_policy& s) {
         if (tables <= 0) raise(T8B_EINVAL, "at least one action feature table is required");
-        const size_t count = static_cast<size_t>(tables) * T8B_MAX_CANDIDATES * s.feature_size;
+        const size_t count = static_cast<size_t>(tables) * s.config.action_count * s.feature_size;
         for (size_t i = 0; i < count; ++i) {
             if (!std::isfinite(features[i])) raise(T8B_EINVAL, "parametric action feature tensor has non-finite values");
         }
@@ -616,6 +622,7 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         smp.out = s.out.data();
         smp.ld = kOutPad;
         smp.feature_size = s.feature_size;
+        smp.action_count = s.config.action_count;
         smp.features = s.features.data();
         smp.table_count = s.tables;
         smp.tables = tables;
@@ -630,7 +637,11 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         smp.log_probs = s.log_probs.data();
         smp.values = s.values.data();
         smp.entropies = s.entropies.data();
-        launch("k_sample", ppo::k_sample, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
+        if (s.feature_size == 48) {
+            launch("k_sample", ppo::k_sample<48>, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
+        } else {
+            launch("k_sample", ppo::k_sample<32>, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
+        }
         check(cudaGetLastError(), "sample actions");
         if (out) {
             out->logits = want_logits ? s.logits.data() : nullptr;
@@ -691,7 +702,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         // validate_rollout_kernel (src/ppo.cu:423-451, 1545-1559)
         s.invalid.zero(st);
         launch("k_validate", k_validate, blocks(samples, 256), 256, 0, st, r.observations, s.width, r.action_masks, r.action_mask_bits,
-                                                         r.actions, r.old_log_probabilities, r.old_values, r.advantages,
+                                                         s.config.action_count, r.actions, r.old_log_probabilities, r.old_values, r.advantages,
                                                          r.returns, samples, s.invalid.data());
         check(cudaGetLastError(), "validate rollout");
         int invalid = 0;
@@ -743,6 +754,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 prep.x = s.x.data();
                 prep.src_bits = r.action_mask_bits;
                 prep.src_bytes = r.action_mask_bits ? nullptr : r.action_masks;
+                prep.action_count = s.config.action_count;
                 prep.bits = s.mb_bits.data();
                 prep.src_actions = r.actions;
                 prep.actions = s.mb_actions.data();
@@ -763,6 +775,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 loss.out = s.out.data();
                 loss.ld = kOutPad;
                 loss.feature_size = s.feature_size;
+                loss.action_count = s.config.action_count;
                 loss.features = s.features.data();
                 loss.table_count = s.tables;
                 loss.tables = s.mb_tables.data();
@@ -788,7 +801,12 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 loss.offset = offset;
                 loss.bucket_start = s.bucket_start.data() + (offset / mb) * (ppo::kBuckets + 1);
                 const unsigned loss_grid = static_cast<unsigned>(loss_blocks(n));
-                launch("k_loss", ppo::k_loss, loss_grid, 32 * ppo::kWarps, ppo::kTableBytes, st, loss);
+                const size_t table_bytes = static_cast<size_t>(s.config.action_count) * s.feature_size * sizeof(float);
+                if (s.feature_size == 48) {
+                    launch("k_loss", ppo::k_loss<48>, loss_grid, 32 * ppo::kWarps, table_bytes, st, loss);
+                } else {
+                    launch("k_loss", ppo::k_loss<32>, loss_grid, 32 * ppo::kWarps, table_bytes, st, loss);
+                }
                 check(cudaGetLastError(), "PPO objective");
                 launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, s.block_metrics.data(), static_cast<int>(loss_grid),
                                                                    ppo::kMetrics, s.metrics.data(), 1);
@@ -871,10 +889,10 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         const int dblocks = 256;
         if (r.entropies) {
             launch("k_decision_partials", k_decision_partials, dblocks, 256, 0, st, r.entropies, nullptr, r.action_mask_bits ? nullptr : r.action_masks,
-                                                        r.action_mask_bits, samples, s.entropy_sums.data());
+                                                        r.action_mask_bits, s.config.action_count, samples, s.entropy_sums.data());
         } else {
             launch("k_decision_partials", k_decision_partials, dblocks, 256, 0, st, s.sample_entropy.data(), s.sample_decision.data(), nullptr, nullptr,
-                                                        samples, s.entropy_sums.data());
+                                                        s.config.action_count, samples, s.entropy_sums.data());
         }
         launch("k_decision_finish", k_decision_finish, 1, 32, 0, st, s.entropy_sums.data(), dblocks, s.entropy_sums.data() + 2 * 1024);
         check(cudaGetLastError(), "decision entropy");

@@ -63,7 +63,8 @@ struct Prep {
     __nv_bfloat16* x;
     // minibatch side data (null when preparing an inference batch)
     const uint32_t* src_bits;
-    const uint8_t* src_bytes;
+    const uint8_t* src_bytes;  // [samples][action_count]
+    int action_count;          // candidates per sample (the mask row of src_bytes)
     uint32_t* bits;
     const int64_t* src_actions;
     int32_t* actions;
@@ -118,8 +119,8 @@ __global__ void k_prep(Prep p) {
                 w = p.src_bits[src * kMaskWords + lane];
             } else {
                 w = 0;
-                const uint8_t* m = p.src_bytes + src * kCandidates + lane * 32;
-                for (int b = 0; b < 32 && lane * 32 + b < kCandidates; ++b) w |= (m[b] != 0 ? 1u : 0u) << b;
+                const uint8_t* m = p.src_bytes + src * p.action_count + lane * 32;
+                for (int b = 0; b < 32 && lane * 32 + b < p.action_count; ++b) w |= (m[b] != 0 ? 1u : 0u) << b;
             }
             p.bits[i * kMaskWords + lane] = w;
         }
@@ -348,11 +349,12 @@ __global__ void k_scale(float* v, size_t n, float factor) {
 struct Sample {
     const float* out;  // [n][ld]: q (feature_size), value
     int ld, feature_size;
-    const float* features;  // [tables][368][feature_size]
+    int action_count;       // candidates per sample (at most 368)
+    const float* features;  // [tables][action_count][feature_size]
     int table_count;
     const int32_t* tables;
     const uint32_t* bits;   // [n][12] or null
-    const uint8_t* bytes;   // [n][368] or null
+    const uint8_t* bytes;   // [n][action_count] or null
     size_t count;
     uint64_t seed, step, lane_offset;
     int deterministic;
@@ -363,21 +365,26 @@ struct Sample {
     float* entropies;
 };
 
-__device__ __forceinline__ uint32_t mask_word(const uint32_t* bits, const uint8_t* bytes, size_t i, int word, int lane) {
+__device__ __forceinline__ uint32_t mask_word(const uint32_t* bits, const uint8_t* bytes, size_t i, int word, int lane,
+                                              int actions) {
     if (bits) return bits[i * kMaskWords + word];
     const int c = word * 32 + lane;
-    const bool legal = c < kCandidates && bytes[i * kCandidates + c] != 0;
+    const bool legal = c < actions && bytes[i * actions + c] != 0;
     return __ballot_sync(0xffffffffu, legal);
 }
 
-constexpr int kFeatures = 32;  // kFullMoveFeatureSize (include/t8_v2/full_move_roster.hpp:21)
+// Feature sizes the scorer kernels are built for: the full-move tables' 32
+// (kFullMoveFeatureSize, include/t8_v2/full_move_roster.hpp:21) and 48.
+constexpr int kFeatures = 32;
+constexpr int kMaxFeatures = 48;
 
 // q . F[a] in feature order, then scaled (src/ppo.cu:340-346).
-__device__ __forceinline__ float score_of(const float* q, const float* frow, int, float scale) {
+template <int F>
+__device__ __forceinline__ float score_of(const float* q, const float* frow, float scale) {
     const float4* f4 = reinterpret_cast<const float4*>(frow);
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kFeatures / 4; ++k) {
+    for (int k = 0; k < F / 4; ++k) {
         const float4 f = __ldg(f4 + k);
         s += q[4 * k] * f.x;
         s += q[4 * k + 1] * f.y;
@@ -432,6 +439,7 @@ __device__ __forceinline__ int legal_rank(const uint32_t* words, bool any, int c
     return rank + __popc(words[(c >> 5) % kMaskWords] & ((1u << (c & 31)) - 1u));
 }
 
+template <int F>
 __global__ void k_sample(Sample p) {
     __shared__ float qs[kWarps][64];
     __shared__ int16_t lists[kWarps][kCandidates];
@@ -446,18 +454,18 @@ __global__ void k_sample(Sample p) {
     const float scale = rsqrtf(static_cast<float>(p.feature_size));
     const int table = p.tables ? p.tables[i] : 0;
     const bool bad_table = table < 0 || table >= p.table_count;
-    const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * kCandidates * p.feature_size;
+    const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * p.action_count * F;
     uint32_t words[kMaskWords];
     bool any = false;
 #pragma unroll
     for (int w = 0; w < kMaskWords; ++w) {
-        words[w] = mask_word(p.bits, p.bytes, i, w, lane);
+        words[w] = mask_word(p.bits, p.bytes, i, w, lane, p.action_count);
         any = any || words[w] != 0;
     }
     if (p.logits) {
-        for (int c = lane; c < kCandidates; c += 32) {
-            p.logits[i * kCandidates + c] =
-                bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + c * p.feature_size, p.feature_size, scale);
+        for (int c = lane; c < p.action_count; c += 32) {
+            p.logits[i * p.action_count + c] =
+                bad_table ? __int_as_float(0x7fc00000) : score_of<F>(q, ftab + c * F, scale);
         }
     }
     int16_t* list = lists[warp];
@@ -467,7 +475,7 @@ __global__ void k_sample(Sample p) {
     float best = -3.402823466e38f;
     int best_j = kCandidates;
     for (int j = lane; j < count; j += 32) {
-        const float s = bad_table ? __int_as_float(0x7fc00000) : score_of(q, ftab + list[j] * p.feature_size, p.feature_size, scale);
+        const float s = bad_table ? __int_as_float(0x7fc00000) : score_of<F>(q, ftab + list[j] * F, scale);
         sc[j] = s;
         if (s > best || best_j == kCandidates) {
             best = s;
@@ -650,6 +658,7 @@ __global__ void k_group_scatter(Group p) {
 struct Loss {
     const float* out;  // [n][ld]
     int ld, feature_size;
+    int action_count;  // candidates per sample (at most 368)
     const float* features;
     int table_count;
     const int32_t* tables;
@@ -676,18 +685,26 @@ struct Loss {
 // Rows of one feature table that a k_loss block scores; the block's table sits in shared
 // memory, so each candidate row is read from L2 once per block instead of once per sample.
 constexpr int kLossRows = 256;
-constexpr int kTableBytes = kCandidates * kFeatures * 4;
+constexpr int kMaxTableBytes = kCandidates * kMaxFeatures * 4;
 
 // Chunk k (4 floats) of candidate c's feature row in the staged table: chunks are rotated by
-// c & 7 so that lanes reading different rows at the same chunk hit different banks.
-__device__ __forceinline__ float4 staged_chunk(const float4* table, int c, int k) {
-    return table[c * (kFeatures / 4) + (k ^ (c & 7))];
+// the row (an xor for 8 chunks, a cyclic shift otherwise) so that lanes reading different rows
+// at the same chunk spread over the banks.
+template <int F>
+__device__ __forceinline__ int staged_slot(int c, int k) {
+    constexpr int chunks = F / 4;
+    return c * chunks + (chunks == 8 ? (k ^ (c & 7)) : (k + c) % chunks);
 }
+template <int F>
+__device__ __forceinline__ float4 staged_chunk(const float4* table, int c, int k) {
+    return table[staged_slot<F>(c, k)];
+}
+template <int F>
 __device__ __forceinline__ float staged_score(const float* q, const float4* table, int c, float scale) {
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kFeatures / 4; ++k) {
-        const float4 f = staged_chunk(table, c, k);
+    for (int k = 0; k < F / 4; ++k) {
+        const float4 f = staged_chunk<F>(table, c, k);
         s += q[4 * k] * f.x;
         s += q[4 * k + 1] * f.y;
         s += q[4 * k + 2] * f.z;
@@ -699,8 +716,9 @@ __device__ __forceinline__ float staged_score(const float* q, const float4* tabl
 // The minibatch rows are grouped by feature table (k_group_*); block b takes the b-th run of at
 // most kLossRows rows of one table, counted over the tables in order. Blocks past the last run
 // only write zero partials.
+template <int F>
 __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
-    extern __shared__ float4 table[];  // kCandidates x kFeatures floats, see staged_chunk
+    extern __shared__ float4 table[];  // action_count x F floats, see staged_slot
     __shared__ float qs[kWarps][64];
     __shared__ float grads[kWarps][64];
     __shared__ float colsum[kWarps][64];
@@ -729,10 +747,9 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
     const int bucket = run[0];
     const bool bad_table = bucket < 0 || bucket >= p.table_count;
     if (!bad_table) {
-        const float4* src = reinterpret_cast<const float4*>(p.features + static_cast<size_t>(bucket) * kCandidates * kFeatures);
-        for (int i = threadIdx.x; i < kCandidates * (kFeatures / 4); i += blockDim.x) {
-            const int c = i / (kFeatures / 4), k = i % (kFeatures / 4);
-            table[c * (kFeatures / 4) + (k ^ (c & 7))] = __ldg(src + i);
+        const float4* src = reinterpret_cast<const float4*>(p.features + static_cast<size_t>(bucket) * p.action_count * F);
+        for (int i = threadIdx.x; i < p.action_count * (F / 4); i += blockDim.x) {
+            table[staged_slot<F>(i / (F / 4), i % (F / 4))] = __ldg(src + i);
         }
     }
     float col_lo = 0.0f, col_hi = 0.0f;
@@ -745,9 +762,9 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
         const float* o = p.out + i * p.ld;
         for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
         __syncwarp();
-        float q[kFeatures];
+        float q[F];
 #pragma unroll
-        for (int f = 0; f < kFeatures; ++f) q[f] = qs[warp][f];
+        for (int f = 0; f < F; ++f) q[f] = qs[warp][f];
         uint32_t words[kMaskWords];
         bool any = false;
 #pragma unroll
@@ -760,7 +777,7 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
         const int count = compact_legal(words, any, lane, list);
         float local_max = -3.402823466e38f;
         for (int j = lane; j < count; j += 32) {
-            const float s = bad_table ? __int_as_float(0x7fc00000) : staged_score(q, table, list[j], scale);
+            const float s = bad_table ? __int_as_float(0x7fc00000) : staged_score<F>(q, table, list[j], scale);
             sc[j] = s;
             local_max = fmaxf(local_max, s);
         }
@@ -787,9 +804,9 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
         }
         entropy = warp_sum(entropy);
         // d(objective)/d(score) of each legal candidate folded into d/dq
-        float dq_local[kFeatures];
+        float dq_local[F];
 #pragma unroll
-        for (int f = 0; f < kFeatures; ++f) dq_local[f] = 0.0f;
+        for (int f = 0; f < F; ++f) dq_local[f] = 0.0f;
         if (!bad_table) {
             for (int j = lane; j < count; j += 32) {
                 const int c = list[j];
@@ -798,8 +815,8 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
                 float g = (lp_grad * ((c == selected ? 1.0f : 0.0f) - prob)) * p.inv_batch;
                 g += p.entropy_coef * prob * (lp + entropy) * p.inv_batch;
 #pragma unroll
-                for (int k = 0; k < kFeatures / 4; ++k) {
-                    const float4 f = staged_chunk(table, c, k);
+                for (int k = 0; k < F / 4; ++k) {
+                    const float4 f = staged_chunk<F>(table, c, k);
                     dq_local[4 * k] += g * f.x;
                     dq_local[4 * k + 1] += g * f.y;
                     dq_local[4 * k + 2] += g * f.z;
@@ -809,6 +826,13 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
         }
         const float total = transpose_sum32(dq_local, lane);
         grads[warp][lane] = bad_table ? __int_as_float(0x7fc00000) : total * scale;
+        if constexpr (F > 32) {
+            float high[32];
+#pragma unroll
+            for (int f = 0; f < 32; ++f) high[f] = f + 32 < F ? dq_local[f + 32] : 0.0f;
+            const float upper = transpose_sum32(high, lane);
+            if (lane + 32 < F) grads[warp][32 + lane] = bad_table ? __int_as_float(0x7fc00000) : upper * scale;
+        }
         const float value = qs[warp][p.feature_size];
         const float error = value - p.ret[i];
         float vgrad = error;

@@ -123,21 +123,24 @@ __global__ void k_record_outcome(float* rewards, uint8_t* terminated, uint8_t* t
     next_values[i] = nv[i];
 }
 
-__global__ void k_pack_masks(const uint8_t* bytes, uint32_t* bits, size_t n) {
+// uint8 masks [n][actions] -> 12 packed words per sample (candidates past `actions` are 0)
+__global__ void k_pack_masks(const uint8_t* bytes, int actions, uint32_t* bits, size_t n) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= n * 12) return;
     const size_t sample = i / 12;
     const int word = static_cast<int>(i % 12);
     uint32_t w = 0;
-    for (int b = 0; b < 32 && word * 32 + b < 368; ++b) w |= (bytes[sample * 368 + word * 32 + b] != 0 ? 1u : 0u) << b;
+    for (int b = 0; b < 32 && word * 32 + b < actions; ++b) {
+        w |= (bytes[sample * actions + word * 32 + b] != 0 ? 1u : 0u) << b;
+    }
     bits[i] = w;
 }
 
-__global__ void k_expand(const uint32_t* bits, uint8_t* bytes, size_t n) {
+__global__ void k_expand(const uint32_t* bits, uint8_t* bytes, int actions, size_t n) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (i >= n * 368) return;
-    const size_t sample = i / 368;
-    const int c = static_cast<int>(i % 368);
+    if (i >= n * actions) return;
+    const size_t sample = i / actions;
+    const int c = static_cast<int>(i % actions);
     bytes[i] = (bits[sample * 12 + (c >> 5)] >> (c & 31)) & 1u;
 }
 
@@ -301,6 +304,7 @@ using namespace t8b;
 struct t8b_rollout {
     size_t envs = 0, horizon = 0, samples = 0;
     int width = 0;
+    int action_count = 0;  // candidates per sample (the uint8 mask row)
     Buffer<float> observations, log_probs, values, rewards, next_values, advantages, returns, entropies;
     Buffer<uint8_t> masks, terminated, truncated;
     Buffer<uint32_t> mask_bits;
@@ -319,8 +323,9 @@ struct t8b_rollout {
         bool stale = false;
         for (uint8_t b : bytes_current) stale = stale || b == 0;
         if (!stale) return;
-        if (masks.size() == 0) masks.allocate(samples * 368);
-        launch("k_expand", k_expand, blocks(samples * 368, 256), 256, 0, stream, mask_bits.data(), masks.data(), samples);
+        if (masks.size() == 0) masks.allocate(samples * static_cast<size_t>(action_count));
+        launch("k_expand", k_expand, blocks(samples * static_cast<size_t>(action_count), 256), 256, 0, stream, mask_bits.data(),
+               masks.data(), action_count, samples);
         check(cudaGetLastError(), "expand masks");
         std::fill(bytes_current.begin(), bytes_current.end(), 1);
     }
@@ -360,6 +365,10 @@ int t8b_rollout_create(size_t environments, size_t horizon, const t8b_actor_conf
         r->horizon = horizon;
         r->samples = environments * horizon;
         r->width = config->observation_size;
+        if (config->action_count < 2 || config->action_count > T8B_MAX_CANDIDATES) {
+            raise(T8B_EINVAL, "action_count must be 2-368");
+        }
+        r->action_count = config->action_count;
         const size_t n = r->samples;
         r->observations.allocate(n * static_cast<size_t>(r->width));
         r->mask_bits.allocate(n * 12);
@@ -439,7 +448,7 @@ int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* o
             check(cudaMemcpyAsync(s.mask_bits.data() + at * 12, mask_bits, sizeof(uint32_t) * n * 12,
                                   cudaMemcpyDeviceToDevice, st), "record masks");
         } else {
-            launch("k_pack_masks", k_pack_masks, blocks(n * 12, 256), 256, 0, st, masks, s.mask_bits.data() + at * 12, n);
+            launch("k_pack_masks", k_pack_masks, blocks(n * 12, 256), 256, 0, st, masks, s.action_count, s.mask_bits.data() + at * 12, n);
             check(cudaGetLastError(), "pack masks");
         }
         s.bytes_current[step] = 0;

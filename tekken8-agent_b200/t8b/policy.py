@@ -136,7 +136,7 @@ class GpuActorCritic:
                   "values": view(out.values, (n,), torch.float32, d),
                   "entropies": view(out.entropies, (n,), torch.float32, d)}
         if want_logits:
-            result["logits"] = view(out.logits, (n, 368), torch.float32, d)
+            result["logits"] = view(out.logits, (n, self.config.action_count), torch.float32, d)
         return result
 
     def prepare_shuffle(self, samples: int, epochs: int, seed: int):
@@ -290,7 +290,7 @@ class GpuRolloutBuffer:
         t, n = self.horizon, self.environments
         spec = {
             "observations": ((t, n, self.config.observation_size), torch.float32),
-            "action_masks": ((t, n, 368), torch.uint8),
+            "action_masks": ((t, n, self.config.action_count), torch.uint8),
             "action_mask_bits": ((t, n, 12), torch.int32),
             "actions": ((t, n), torch.int64), "old_log_probabilities": ((t, n), torch.float32),
             "old_values": ((t, n), torch.float32), "rewards": ((t, n), torch.float32),

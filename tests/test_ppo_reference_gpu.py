@@ -40,6 +40,42 @@ def batch(n, tables, rng, width=151):
     return make_batch(n, tables, rng, width)
 
 
+def config3_features(rng, tables=41, slots=256):
+    """Synthetic move properties with the shapes of the config-3 microbench: 48 features per
+    candidate slot, integers stored as floats (startup 10-30, recovery -15..+10, damage 5-40,
+    ...) and a one-hot hit level."""
+    f = np.zeros((tables, slots, 48), np.float32)
+    f[..., 0] = rng.integers(10, 31, (tables, slots))
+    f[..., 1] = rng.integers(-15, 11, (tables, slots))
+    f[..., 2] = rng.integers(5, 41, (tables, slots))
+    f[..., 3:12] = rng.integers(-3, 4, (tables, slots, 9))
+    level = rng.integers(0, 4, (tables, slots))
+    f[..., 12:16] = np.eye(4, dtype=np.float32)[level]
+    f[..., 16:] = rng.normal(size=(tables, slots, 32)).astype(np.float32)
+    return f
+
+
+SHAPES = {
+    # the reference's full-move network: 151 observations, 368 candidates x 32 fixed features
+    "full_move": dict(),
+    # the config-3 shapes: 128 observations, 256 candidate slots x 48 features
+    "config3": dict(observation_size=128, action_count=256, action_feature_size=48),
+}
+
+
+def shaped(name, features, rng, n):
+    """(actor config overrides, feature tables, observations, tables, masks) for a shape."""
+    if name == "full_move":
+        obs, tables, masks = batch(n, features.shape[0], rng)
+        return SHAPES[name], features, obs, tables, masks
+    feats = config3_features(np.random.default_rng(2))
+    obs = rng.normal(size=(n, 128)).astype(np.float32)
+    tables = rng.integers(0, feats.shape[0], n).astype(np.int32)
+    masks = (rng.random((n, 256)) < 0.3).astype(np.uint8)
+    masks[:, 0] = 1
+    return SHAPES[name], feats, obs, tables, masks
+
+
 def test_initial_weights_equal_the_reference(cuda, ref, features, tmp_path):
     """Orthogonal initialisation from the same seed gives the reference's weights bit for bit
     (read back through the reference's own checkpoint file)."""
@@ -104,23 +140,25 @@ def test_checkpoint_rejections(cuda, features, tmp_path):
         GpuActorCritic(256, actor_config(hidden_size=256), seed=1).load_checkpoint(path)
 
 
-def test_forward_matches_the_reference(cuda, ref, features, tmp_path):
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_forward_matches_the_reference(cuda, ref, features, tmp_path, shape):
     import torch
     from t8b.policy import GpuActorCritic, actor_config
-    actor = actor_config()
     n = 8192
-    theirs = ref.RefPolicy(ref.config_from(actor), n, 2027)
-    theirs.set_features(features)
-    ours = GpuActorCritic(n, actor, seed=2027)
-    ours.set_action_feature_tables(features)
     rng = np.random.default_rng(21)
+    overrides, feats, obs, tables, masks = shaped(shape, features, rng, n)
+    actor = actor_config(**overrides)
+    theirs = ref.RefPolicy(ref.config_from(actor), n, 2027)
+    theirs.set_features(feats)
+    ours = GpuActorCritic(n, actor, seed=2027)
+    ours.set_action_feature_tables(feats)
     # larger query weights so the policy is far from uniform
+    outputs = actor.action_feature_size + 1
     p = ours.parameters()
-    p[-(512 * 33 + 33):] *= 40.0
+    p[-(actor.hidden_size * outputs + outputs):] *= 40.0 if shape == "full_move" else 4.0
     ours.set_parameters(p)
     ours.save_checkpoint(tmp_path / "w.t8ppo")
     theirs.load(tmp_path / "w.t8ppo")
-    obs, tables, masks = batch(n, features.shape[0], rng)
     d = lambda a: torch.as_tensor(a, device="cuda")
     for deterministic in (False, True):
         got = ours.forward(d(obs), d(masks), n, seed=7, step=3, deterministic=deterministic, tables=d(tables))
@@ -135,7 +173,8 @@ def test_forward_matches_the_reference(cuda, ref, features, tmp_path):
         assert relative(lp[same], want["log_probabilities"][same]) < 2e-2
 
 
-def test_update_matches_the_reference(cuda, ref, features, tmp_path):
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
     """One update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
     weights on the same rollout agrees with the reference's. The comparison is made well
     conditioned: advantages are all positive and returns sit above the values, so the batch
@@ -144,25 +183,30 @@ def test_update_matches_the_reference(cuda, ref, features, tmp_path):
     the sign of near-zero components is rounding noise in either implementation)."""
     import torch
     from t8b.policy import GpuActorCritic, actor_config, ppo_config
-    from test_ppo_gpu import rollout_inputs, view_of
-    actor = actor_config()
+    from test_ppo_gpu import view_of
     n = 8192
+    rng = np.random.default_rng(31)
+    overrides, feats, obs, tables, masks = shaped(shape, features, rng, n)
+    actor = actor_config(**overrides)
     ours = GpuActorCritic(n, actor, seed=7)
-    ours.set_action_feature_tables(features)
+    ours.set_action_feature_tables(feats)
+    outputs = actor.action_feature_size + 1
     p = ours.parameters()
-    p[-(512 * 33 + 33):] *= 30.0
+    p[-(actor.hidden_size * outputs + outputs):] *= 30.0 if shape == "full_move" else 3.0
     ours.set_parameters(p)
     before = ours.parameters().astype(np.float64)
     ours.save_checkpoint(tmp_path / "start.t8ppo")
     theirs = ref.RefPolicy(ref.config_from(actor), n, 1)
-    theirs.set_features(features)
+    theirs.set_features(feats)
     theirs.load(tmp_path / "start.t8ppo")
-    rng = np.random.default_rng(31)
-    obs, tables, masks, actions, old_lp, old_v, adv, ret = rollout_inputs(ours, features, n, rng)
-    adv = (np.abs(adv) + 0.5).astype(np.float32)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    out = ours.forward(d(obs), d(masks), n, seed=1, step=0, tables=d(tables))
+    actions = out["actions"].cpu().numpy()
+    old_lp = out["log_probabilities"].cpu().numpy() - rng.normal(scale=0.05, size=n).astype(np.float32)
+    old_v = out["values"].cpu().numpy()
+    adv = (np.abs(rng.normal(size=n)) + 0.5).astype(np.float32)
     ret = (old_v + 1.0).astype(np.float32)
-    arrays = (obs, tables, masks, actions, old_lp, old_v, adv, ret)
-    view, keep = view_of(arrays)
+    view, keep = view_of((obs, tables, masks, actions, old_lp, old_v, adv, ret))
     cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3, adam_epsilon=1.0)
     got = ours.update_ppo(view, cfg, shuffle_seed=17)
     zeros_f = torch.zeros(n, device="cuda")
