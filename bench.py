@@ -43,6 +43,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--self-play", action="store_true",
                     help="mirror self-play: a frozen copy of the initial policy plays the other side")
+    ap.add_argument("--workload", choices=("iteration", "mlp"), default="iteration",
+                    help="iteration: the self-play training iteration (the headline); mlp: policy forward + "
+                         "backward on one batch of 32,768 at the config-3 shapes (128 observations, 256 candidates "
+                         "x 48 features, 2 x 512 hidden)")
     return ap.parse_args()
 
 
@@ -336,10 +340,92 @@ def run_ours(args):
         torch.distributed.destroy_process_group()
 
 
+def run_mlp(args):
+    """Policy forward + backward (one PPO minibatch update: forward, objective, backward, Adam)
+    on a batch of 32,768 at the config-3 shapes, with the GEMMs' tensor-core roofline."""
+    import numpy as np
+    import torch
+    from t8b import profile
+    from t8b.policy import GpuActorCritic, actor_config, ppo_config
+    from t8b._lib import RolloutView
+    batch = 32768
+    obs_size, actions, features_size, hidden = 128, 256, 48, 512
+    rng = np.random.default_rng(2)
+    tables = 41
+    feats = np.zeros((tables, actions, features_size), np.float32)
+    feats[..., 0] = rng.integers(10, 31, (tables, actions))
+    feats[..., 1] = rng.integers(-15, 11, (tables, actions))
+    feats[..., 2] = rng.integers(5, 41, (tables, actions))
+    feats[..., 3:12] = rng.integers(-3, 4, (tables, actions, 9))
+    feats[..., 12:16] = np.eye(4, dtype=np.float32)[rng.integers(0, 4, (tables, actions))]
+    feats[..., 16:] = rng.normal(size=(tables, actions, 32)).astype(np.float32)
+    actor = actor_config(observation_size=obs_size, action_count=actions, action_feature_size=features_size,
+                         hidden_size=hidden, orthogonal_initialization=0)
+    policy = GpuActorCritic(batch, actor, seed=2)
+    policy.set_action_feature_tables(feats)
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    obs = d(rng.normal(size=(batch, obs_size)).astype(np.float32))
+    masks = d((rng.random((batch, actions)) < 0.3).astype(np.uint8))
+    masks[:, 0] = 1
+    tab = d(rng.integers(0, tables, batch).astype(np.int32))
+    out = policy.forward(obs, masks, batch, seed=1, step=0, tables=tab)
+    acts = out["actions"].clone()
+    lp = out["log_probabilities"].clone()
+    val = out["values"].clone()
+    adv = d(rng.normal(size=batch).astype(np.float32))
+    ret = val + d(rng.normal(scale=0.5, size=batch).astype(np.float32))
+    view = RolloutView()
+    view.observations, view.action_masks, view.actions = obs.data_ptr(), masks.data_ptr(), acts.data_ptr()
+    view.old_log_probabilities, view.old_values = lp.data_ptr(), val.data_ptr()
+    view.advantages, view.returns, view.feature_tables = adv.data_ptr(), ret.data_ptr(), tab.data_ptr()
+    view.sample_count = view.environment_count = batch
+    view.horizon = 1
+    cfg = ppo_config(epochs=1, minibatch_size=batch, target_kl=0.0)
+    for i in range(args.warmup):
+        policy.update_ppo(view, cfg, shuffle_seed=i)
+    torch.cuda.synchronize()
+    profile.enable(True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        policy.update_ppo(view, cfg, shuffle_seed=100 + i)
+    end.record()
+    end.synchronize()
+    kernels = profile.report()
+    profile.enable(False)
+    ms = start.elapsed_time(end) / args.steps
+    outputs = features_size + 1
+    flops = {"gemm_forward_hidden": 2 * (obs_size * hidden + hidden * hidden),
+             "gemm_forward_output": 2 * hidden * outputs,
+             "gemm_weight_grad": 2 * (obs_size * hidden + hidden * hidden + hidden * outputs),
+             "gemm_input_grad": 2 * (hidden * outputs + hidden * hidden)}
+    gemm_flops = sum(flops.values()) * batch
+    gemm_ms = sum(kernels[k][1] for k in flops if k in kernels) / args.steps
+    _, peak_bf16, peak_sustained, peak_kind = measured_peaks()
+    achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
+    line = {"metric": "policy fwd+bwd samples/s, batch 32,768, config-3 shapes", "value": batch / (ms / 1000.0),
+            "unit": "samples/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 tensor-core products, fp32 accumulation and master weights", "data": "synthetic",
+            "config": {"workload": "config 3 shapes: 128 observations -> 2 x 512 tanh -> 48-d query + value; "
+                                   "256 candidate slots x 48 features per table, 41 tables, ~30% legal; one PPO "
+                                   "minibatch update (forward, objective, backward, global-norm clip, Adam)",
+                       "batch": batch},
+            "roofline": {"kernel": "tcgen05 GEMMs (all labels)", "bound": "tensor", "achieved": achieved,
+                         "peak": peak_bf16, "unit": "TFLOP/s", "frac": achieved / peak_bf16,
+                         "peak_source": f"{peak_kind} burst bf16", "traffic": None,
+                         "gemm_ms_per_step": gemm_ms, "gemm_gflop_per_step": gemm_flops / 1e9},
+            "kernels": [{"kernel": k, "launches_per_step": v[0] / args.steps, "ms_per_step": v[1] / args.steps}
+                        for k, v in sorted(kernels.items(), key=lambda kv: -kv[1][1])[:10]]}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "mlp":
+        run_mlp(args)
     else:
         run_ours(args)
 

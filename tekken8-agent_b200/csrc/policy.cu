@@ -856,7 +856,9 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         }
         // merge the observation normaliser after the update (src/ppo.cu:1663-1667)
         if (s.config.observation_normalization) {
-            const size_t chunk = 8192;
+            // chunks of 1,024-8,192 samples: enough blocks for a single minibatch, few chunks to merge
+            // for a whole rollout (the merge walks the chunks in order)
+            const size_t chunk = std::min<size_t>(8192, std::max<size_t>(1024, (samples / 512 + 7) / 8 * 8));
             const size_t chunks = (samples + chunk - 1) / chunk;
             if (s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
             dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((s.width + 31) / 32));
