@@ -1,14 +1,15 @@
 // tcgen05 GEMM for sm_100a: C[M,N] (+)= A[M,K] . B[N,K]^T in bf16 with fp32 accumulation in
 // tensor memory, fed by TMA, with the epilogue fused by a functor.
 //
-// One persistent CTA per SM, 192 threads:
+// One persistent CTA per SM, 192 or 320 threads:
 //   warp 0     TMA producer: one elected thread loads A and B k-blocks (64 wide) into a ring of
 //              shared-memory stages (128B swizzle), arriving on full[stage];
 //   warp 1     MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide slice and
 //              commits each stage back to empty[stage]; the accumulator of a finished tile is
 //              committed to acc_full[buffer];
-//   warps 2-5  epilogue: tcgen05.ld of their 32 TMEM lanes (lane quarter = warp % 4), 32 columns
-//              at a time, handed to the epilogue functor with an 8 KB warp-private shared-memory
+//   warps 2-5 or 2-9  epilogue: tcgen05.ld of their 32 TMEM lanes (lane quarter = warp % 4), 32
+//              columns at a time (with 8 warps, the two of a quarter take alternate chunks), handed to the
+//              epilogue functor with a 6.5 KB warp-private shared-memory
 //              scratch (for staging a 32 x 32 chunk so global rows are read and written whole);
 //              the functor's prefetch of chunk c + 1 is issued before chunk c is loaded from
 //              tensor memory; then acc_empty[buffer] frees the buffer.
@@ -28,7 +29,10 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+// Epilogue warps: a functor's kEpilogueWarps, 4 (one per lane quarter of the accumulator) or 8
+// (two per quarter, alternating 32-column chunks).
+template <class Epi>
+constexpr int threads_for() { return 64 + 32 * Epi::kEpilogueWarps; }
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -121,7 +125,7 @@ struct EpiCtx {
     int buffer;   // prefetch buffer (0 or 1) holding this chunk's inputs
     bool more;    // the next chunk's prefetch has been issued after this one's
 };
-constexpr int kEpiWarpBytes = 8192;
+constexpr int kEpiWarpBytes = 6656;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(valid ? 16 : 0)
@@ -149,12 +153,12 @@ struct Shape {
     int* error;         // set to 1 on a stalled wait
 };
 
-template <int BN>
+template <int BN, int EW>
 struct Layout {
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kEpiBytes = 4 * kEpiWarpBytes;
+    static constexpr int kEpiBytes = EW * kEpiWarpBytes;
     // stages fill what the 227 KB of a CTA leaves after the epilogue scratch and barriers
     static constexpr int kStageBudget = 232448 - 1024 - 256 - kEpiBytes;
     static constexpr int kStages = kStageBudget / kStageBytes > 8 ? 8 : kStageBudget / kStageBytes;
@@ -163,11 +167,13 @@ struct Layout {
 };
 
 template <int BN, bool A_MN, bool B_MN, class Epi>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_for<Epi>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape s, Epi epi) {
+    constexpr int EW = Epi::kEpilogueWarps;
+    static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
     static_assert(!B_MN || BN % 64 == 0, "MN-major B tiles are whole 64-wide atoms");
-    using L = Layout<BN>;
+    using L = Layout<BN, EW>;
     extern __shared__ __align__(1024) unsigned char raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     unsigned char* stages = base;
@@ -187,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int i = 0; i < 2; ++i) {
             bar_init(acc_full + i, 1);
-            bar_init(acc_empty + i, 4 * 32);
+            bar_init(acc_empty + i, EW * 32);
         }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -296,6 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;  // which alternate 32-column chunks this warp takes (EW = 8)
+        constexpr int stride = EW / 4;
         unsigned char* scratch = epi_scratch + (warp - 2) * kEpiWarpBytes;
         int acc = 0;
         uint32_t acc_phase = 0;
@@ -311,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             x.quarter = quarter;
             x.lane = lane;
             x.scratch = scratch;
-            x.col0 = tn * BN;
+            x.col0 = tn * BN + half * 32;
             x.buffer = 0;
             epi.prefetch(x);
             if (!bar_wait(acc_full + acc, acc_phase, abort)) {
@@ -322,12 +330,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t t = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
             const bool empty_k = kb1 <= kb0;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                x.more = c + 1 < BN / 32;
+            for (int c = half, n = 0; c < BN / 32; c += stride, ++n) {
+                x.more = c + stride < BN / 32;
                 if (x.more) {
                     EpiCtx next = x;
-                    next.col0 = tn * BN + (c + 1) * 32;
-                    next.buffer = (c + 1) & 1;
+                    next.col0 = tn * BN + (c + stride) * 32;
+                    next.buffer = (n + 1) & 1;
                     epi.prefetch(next);
                 }
                 tmem_load32(t + static_cast<uint32_t>(c * 32), v);
@@ -336,7 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int i = 0; i < 32; ++i) v[i] = 0.0f;
                 }
                 x.col0 = tn * BN + c * 32;
-                x.buffer = c & 1;
+                x.buffer = n & 1;
                 epi(x, v);
             }
             fence_before();

@@ -67,7 +67,7 @@ struct Operand {
 // C[m][n] = A . B^T over k, epilogue `epi`; `splits` partitions the k blocks (split-K).
 template <int BN, bool A_MN, bool B_MN, class Epi>
 void gemm(const char* label, const Operand& a, const Operand& b, int splits, int* error, Epi epi, cudaStream_t stream) {
-    using L = tc::Layout<BN>;
+    using L = tc::Layout<BN, Epi::kEpilogueWarps>;
     if (a.k != b.k || a.mn_major != A_MN || b.mn_major != B_MN) raise(T8B_EINVAL, "GEMM operand mismatch");
     tc::Shape s{};
     s.m = a.rows;
@@ -88,7 +88,7 @@ void gemm(const char* label, const Operand& a, const Operand& b, int splits, int
     }
     const int work = s.tiles_m * s.tiles_n * s.splits;
     const int grid = work < sm_count() ? work : sm_count();
-    launch(label, kernel, grid, tc::kThreads, L::kSmemBytes, stream, ma, mb, s, epi);
+    launch(label, kernel, grid, tc::threads_for<Epi>(), L::kSmemBytes, stream, ma, mb, s, epi);
     check(cudaGetLastError(), "GEMM launch");
 }
 

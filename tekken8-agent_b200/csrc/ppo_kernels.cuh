@@ -173,6 +173,7 @@ __device__ __forceinline__ void wait_prefetch(const tc::EpiCtx& x) {
 
 // Hidden layer forward: h = tanh(acc + b) as bf16 [rows][ld].
 struct EpiTanh {
+    static constexpr int kEpilogueWarps = 8;
     const float* bias;
     __nv_bfloat16* out;
     int ld, m, cols;
@@ -195,6 +196,7 @@ struct EpiTanh {
 
 // Output layer: o = acc + b for the valid columns (zero beyond), fp32 [rows][ld].
 struct EpiBias {
+    static constexpr int kEpilogueWarps = 8;
     const float* bias;
     float* out;
     int ld, m, valid;
@@ -226,6 +228,7 @@ struct EpiBias {
 // sums of dz (the bias gradient, reduced later in a fixed order). The h chunk is prefetched
 // with cp.async into one of two 2 KB buffers while the previous chunk is processed.
 struct EpiTanhGrad {
+    static constexpr int kEpilogueWarps = 8;
     const __nv_bfloat16* h;
     __nv_bfloat16* out;
     float* colsum;
@@ -281,6 +284,7 @@ struct EpiTanhGrad {
 
 // Split-K partial of a weight gradient: part[split][row][col] (fp32).
 struct EpiSplit {
+    static constexpr int kEpilogueWarps = 4;
     __device__ void prefetch(const tc::EpiCtx&) const {}
     float* part;
     int m, n;
