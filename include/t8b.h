@@ -250,7 +250,9 @@ int t8b_sim_step(t8b_sim* sim, const int64_t* learner_candidates, const int64_t*
                  uint64_t counter);
 /* Device views  full_move_gpu.hpp:96-112. Masks are uint8 [env][368] as in the
  * reference; t8b_sim_learner_mask_bits gives the packed form the library keeps
- * (12 uint32 words per environment, bit c of word c/32 = candidate c). */
+ * (12 uint32 words per environment, bit c of word c/32 = candidate c). The opponent's masks
+ * are computed on the simulator's stream the first time they are asked for after a state
+ * change (a scripted-opponent trainer never reads them). */
 const float* t8b_sim_learner_observations(const t8b_sim* sim);
 const float* t8b_sim_opponent_observations(const t8b_sim* sim);
 const uint8_t* t8b_sim_learner_masks(t8b_sim* sim);

@@ -273,13 +273,14 @@ __global__ void __launch_bounds__(kStepThreads) k_observe(SimView v) {
 }
 
 // candidate_mask_kernel (src/full_move_gpu.cu:169-186) as one warp per (fight, side).
-__global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t* only) {
+// `sides`: 3 both sides (items = 2 x fights), 1 the learner's, 2 the opponent's (items = fights).
+__global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t* only, int sides) {
     const Staged st = stage_tables(v);
     __shared__ Fight fights[kMaskThreads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t item = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
-    const size_t env = item >> 1;
-    const int side = static_cast<int>(item & 1);
+    const size_t env = sides == 3 ? item >> 1 : item;
+    const int side = sides == 3 ? static_cast<int>(item & 1) : sides - 1;
     const bool active = env < v.count && (only == nullptr || only[env]);
     if (active) {
         const uint32_t* src = reinterpret_cast<const uint32_t*>(v.states + env);
@@ -723,6 +724,7 @@ struct t8b_sim {
     Buffer<float> learner_obs, opponent_obs;
     Buffer<int32_t> learner_tables, opponent_tables;
     Buffer<uint32_t> learner_bits, opponent_bits;
+    bool opponent_bits_stale = true;
     Buffer<uint8_t> learner_bytes, opponent_bytes, legal_bytes;
     Buffer<float> rewards, sparse;
     Buffer<int8_t> outcomes;
@@ -764,10 +766,22 @@ struct t8b_sim {
     }
     void launched(const char* what) const { check(cudaGetLastError(), what); }
 
+    // The learner's masks after every state change; the opponent's are computed when asked for
+    // (opponent_bits_stale), which a scripted-opponent trainer never does.
     void masks(const uint8_t* only) {
         const unsigned warps_per_block = kMaskThreads / 32;
-        launch("k_masks", k_masks, blocks(2 * n, warps_per_block), kMaskThreads, smem(), stream, view(), only);
+        launch("k_masks", k_masks, blocks(n, warps_per_block), kMaskThreads, smem(), stream, view(), only, 1);
         launched("candidate masks");
+        opponent_bits_stale = true;
+    }
+    const uint32_t* opponent_mask_bits() {
+        if (opponent_bits_stale) {
+            const unsigned warps_per_block = kMaskThreads / 32;
+            launch("k_masks", k_masks, blocks(n, warps_per_block), kMaskThreads, smem(), stream, view(), nullptr, 2);
+            launched("opponent masks");
+            opponent_bits_stale = false;
+        }
+        return opponent_bits.data();
     }
     void check_characters(const int32_t* values, bool allow_keep, const char* what) const {
         for (size_t i = 0; i < n; ++i) {
@@ -1075,7 +1089,13 @@ int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, 
 const float* t8b_sim_learner_observations(const t8b_sim* sim) { return sim ? sim->learner_obs.data() : nullptr; }
 const float* t8b_sim_opponent_observations(const t8b_sim* sim) { return sim ? sim->opponent_obs.data() : nullptr; }
 const uint32_t* t8b_sim_learner_mask_bits(const t8b_sim* sim) { return sim ? sim->learner_bits.data() : nullptr; }
-const uint32_t* t8b_sim_opponent_mask_bits(const t8b_sim* sim) { return sim ? sim->opponent_bits.data() : nullptr; }
+const uint32_t* t8b_sim_opponent_mask_bits(const t8b_sim* sim) {
+    if (sim == nullptr) return nullptr;
+    const uint32_t* bits = nullptr;
+    // the view is filled on first use after a state change (the handle is logically const)
+    const int status = with_sim(const_cast<t8b_sim*>(sim), [&](t8b_sim& s) { bits = s.opponent_mask_bits(); });
+    return status == T8B_OK ? bits : nullptr;
+}
 
 static const uint8_t* expand(t8b_sim* sim, bool learner) {
     const uint8_t* result = nullptr;
@@ -1083,7 +1103,7 @@ static const uint8_t* expand(t8b_sim* sim, bool learner) {
         Buffer<uint8_t>& bytes = learner ? s.learner_bytes : s.opponent_bytes;
         if (bytes.size() == 0) bytes.allocate(s.n * kMaxCandidates);
         launch("k_expand_masks", k_expand_masks, blocks(s.n * kMaxCandidates, 256), 256, 0, s.stream, 
-            learner ? s.learner_bits.data() : s.opponent_bits.data(), bytes.data(), s.n);
+            learner ? s.learner_bits.data() : s.opponent_mask_bits(), bytes.data(), s.n);
         s.launched("expand masks");
         result = bytes.data();
     });

@@ -141,11 +141,13 @@ class SelfPlayTrainer:
         the simulator's last step; it overlaps the learner's forward, and the caller makes the
         main stream wait for it before stepping the simulator."""
         side = self.opponent_stream
+        # the views first: the opponent's masks are computed on the simulator's stream when asked for
+        obs, tables, bits = (self.sim.opponent_observations(), self.sim.opponent_feature_tables(),
+                             self.sim.opponent_mask_bits())
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
-            out = self.opponent.forward(self.sim.opponent_observations(), None, self.n, self.seed + 2, counter, False,
-                                        side.cuda_stream, self.sim.opponent_feature_tables(),
-                                        mask_bits=self.sim.opponent_mask_bits())
+            out = self.opponent.forward(obs, None, self.n, self.seed + 2, counter, False, side.cuda_stream, tables,
+                                        mask_bits=bits)
         return out["actions"]
 
     def host_boundary(self):
