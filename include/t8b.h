@@ -270,6 +270,12 @@ const int32_t* t8b_sim_opponent_feature_tables(const t8b_sim* sim);
 int t8b_sim_download_noise_levels(t8b_sim* sim, t8b_noise_levels_t* out);
 /* frames_simulated  full_move_gpu.hpp:120 */
 int t8b_sim_frames_simulated(t8b_sim* sim, uint64_t* out);
+/* Evaluation bookkeeping on the device (no reference counterpart: the reference's evaluate and
+ * head_to_head, src/full_move_train.cpp:921-1044, download terminated and outcomes after every
+ * step). After a step, every fight that has terminated for the first time since the caller
+ * zeroed `finished` gets its outcome in result[env], finished[env] = 1, and *remaining drops by
+ * one. All pointers are device memory ([environments] int8 / uint8, one uint32). */
+int t8b_sim_record_first_outcomes(t8b_sim* sim, int8_t* result, uint8_t* finished, uint32_t* remaining);
 /* download_and_clear_tally and the three tallies cleared with it  full_move_gpu.hpp:124-131.
  * tally: [roster][5][2][3]; scenario: [9][3]; learner: [roster][3]; bot: [331][3]. */
 int t8b_sim_download_and_clear_tally(t8b_sim* sim, uint32_t* tally, uint32_t* scenario_tally,
@@ -298,6 +304,13 @@ int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32
  * (64, 192 or 256) and splits the split-K factor. All pointers are device. */
 int t8b_debug_gemm(const void* a, int a_mn_major, const void* b, int b_mn_major, float* c, int m, int n, int k,
                    int bn, int splits, void* stream);
+
+/* Test hook for the bounded waits (no reference counterpart): one thread waits on a
+ * shared-memory mbarrier with the GEMM's wait loop, giving up after spin_limit polls. With
+ * arrive = 1 the barrier's phase completes first and *timed_out = 0; with arrive = 0 nothing
+ * ever arrives, the wait runs out and *timed_out = 1 (the kernel returns; the context stays
+ * usable). */
+int t8b_debug_bounded_wait(int arrive, uint32_t spin_limit, int* timed_out);
 
 /* Launch accounting (no reference counterpart). t8b_launch_count is the number of kernels the
  * library has launched since it was loaded. t8b_profile_enable(1) clears earlier results and

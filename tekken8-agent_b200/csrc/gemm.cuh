@@ -56,8 +56,9 @@ __device__ __forceinline__ bool bar_try(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 // Waits for the phase with the given parity; false after the spin limit or an abort.
-__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+__device__ __forceinline__ bool bar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                         uint32_t limit = kSpinLimit) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (bar_try(bar, parity)) return true;
         if (*abort) return false;
     }

@@ -70,3 +70,33 @@ extern "C" int t8b_debug_gemm(const void* a, int a_mn_major, const void* b, int 
         }
     });
 }
+
+namespace t8b {
+
+// One thread waits on an mbarrier with the GEMM's bounded wait; with `arrive` the barrier's
+// phase completes first, otherwise nothing ever arrives and the wait runs out after `limit`
+// polls. status[0] = 1 when the wait gave up, 0 when it saw the phase.
+__global__ void k_bounded_wait(int arrive, uint32_t limit, int* status) {
+    __shared__ uint64_t bar;
+    __shared__ int abort;
+    if (threadIdx.x != 0) return;
+    abort = 0;
+    tc::bar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (arrive) tc::bar_arrive(&bar);
+    const bool seen = tc::bar_wait(&bar, 0, &abort, limit);
+    status[0] = seen ? 0 : 1;
+}
+
+}  // namespace t8b
+
+extern "C" int t8b_debug_bounded_wait(int arrive, uint32_t spin_limit, int* timed_out) {
+    using namespace t8b;
+    return guarded([&] {
+        if (!timed_out || spin_limit == 0) raise(T8B_EINVAL, "bounded wait arguments");
+        Buffer<int> status(1);
+        launch("k_bounded_wait", k_bounded_wait, 1, 32, 0, nullptr, arrive, spin_limit, status.data());
+        check(cudaGetLastError(), "bounded wait");
+        status.download(timed_out, 1, nullptr);
+    });
+}

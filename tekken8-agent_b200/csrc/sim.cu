@@ -272,6 +272,20 @@ __global__ void __launch_bounds__(kStepThreads) k_observe(SimView v) {
     write_observations(v, st, match_of(st, p1, p2), s, env, p1, p2, v.learner_is_p1[env] ? 0 : 1);
 }
 
+// The first finished round of every fight during an evaluation: the outcome of a fight that
+// terminates for the first time is kept and `remaining` drops by one; later rounds are ignored.
+__global__ void k_first_outcomes(const uint8_t* terminated, const int8_t* outcomes, size_t count, int8_t* result,
+                                 uint8_t* finished, unsigned* remaining) {
+    const size_t env = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const bool first = env < count && terminated[env] && !finished[env];
+    if (first) {
+        finished[env] = 1;
+        result[env] = outcomes[env];
+    }
+    const uint32_t ballot = __ballot_sync(0xffffffffu, first);
+    if ((threadIdx.x & 31) == 0 && ballot != 0) atomicSub(remaining, static_cast<unsigned>(__popc(ballot)));
+}
+
 // candidate_mask_kernel (src/full_move_gpu.cu:169-186) as one warp per (fight, side).
 // `sides`: 3 both sides (items = 2 x fights), 1 the learner's, 2 the opponent's (items = fights).
 __global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t* only, int sides) {
@@ -1132,6 +1146,15 @@ int t8b_sim_frames_simulated(t8b_sim* sim, uint64_t* out) {
         unsigned long long value = 0;
         s.frames.download(&value, 1, s.stream);
         *out = value;
+    });
+}
+
+int t8b_sim_record_first_outcomes(t8b_sim* sim, int8_t* result, uint8_t* finished, uint32_t* remaining) {
+    return with_sim(sim, [&](t8b_sim& s) {
+        if (!result || !finished || !remaining) raise(T8B_EINVAL, "first-outcome buffers are required");
+        launch("k_first_outcomes", k_first_outcomes, blocks(s.n, 256), 256, 0, s.stream, s.terminated.data(),
+               s.outcomes.data(), s.n, result, finished, remaining);
+        s.launched("first outcomes");
     });
 }
 

@@ -196,6 +196,7 @@ PROTOTYPES = {
     "t8b_sim_opponent_feature_tables": (vp, [vp]),
     "t8b_sim_download_noise_levels": (C.c_int, [vp, vp]),
     "t8b_sim_frames_simulated": (C.c_int, [vp, C.POINTER(u64)]),
+    "t8b_sim_record_first_outcomes": (C.c_int, [vp, vp, vp, vp]),
     "t8b_sim_download_and_clear_tally": (C.c_int, [vp, vp, vp, vp, vp]),
     "t8b_sim_snapshot": (C.c_int, [vp] * 12),
     "t8b_sim_restore": (C.c_int, [vp] * 12),
@@ -300,6 +301,7 @@ for _name, _cls in (("t8b_actor_config_t", ActorConfig), ("t8b_ppo_config_t", Pp
 fp = C.POINTER(C.c_float)
 PROTOTYPES.update({
     "t8b_debug_gemm": (C.c_int, [vp, C.c_int, vp, C.c_int, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+    "t8b_debug_bounded_wait": (C.c_int, [C.c_int, C.c_uint32, C.POINTER(C.c_int)]),
     "t8b_launch_count": (u64, []),
     "t8b_profile_enable": (None, [C.c_int]),
     "t8b_profile_report": (C.c_size_t, [C.c_char_p, C.c_size_t]),

@@ -38,3 +38,18 @@ def test_gemm_matches_torch(cuda, bn, a_mn, b_mn, m, n, k, splits):
     want = a.float() @ b.float().t()
     err = (c - want).abs().max().item() / want.abs().max().item()
     assert err < 1e-3, err
+
+
+def test_bounded_wait_gives_up_and_reports(cuda):
+    """The mbarrier wait the GEMM uses is bounded: a barrier that nothing arrives at makes the
+    wait run out and report it (the kernel returns, the context stays usable); an arrived
+    barrier is seen."""
+    import ctypes as C
+    import torch
+    from t8b import _lib
+    flag = C.c_int(-1)
+    _lib.call("t8b_debug_bounded_wait", 0, 1 << 16, C.byref(flag))
+    assert flag.value == 1
+    _lib.call("t8b_debug_bounded_wait", 1, 1 << 16, C.byref(flag))
+    assert flag.value == 0
+    assert torch.ones(4, device="cuda").sum().item() == 4.0
