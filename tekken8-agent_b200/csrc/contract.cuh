@@ -573,6 +573,113 @@ T8B_HD void start_round(const Match& m, Fight& s, const EnvCfg& ec, uint64_t see
     }
 }
 
+// ------------------------------------------------------------------ memory (--memory)
+// full_move_contract.hpp:611-735: each fighter's last four moves (level, how they ended, age)
+// and decaying traces of its habits, updated after every frame and appended to the observation
+// (the opponent's newest move only once it is perception_delay frames old).
+constexpr int kMemorySlots = 4;
+constexpr int kMemorySlotFeatures = 10;  // level: high, mid, low, throw, no hit; outcome: hit, counter, blocked, missed; age
+constexpr int kMemoryTraces = 5;         // crouching, backing off, sidestepping, guarding, attacking
+constexpr int kMemoryFighterFeatures = kMemorySlots * kMemorySlotFeatures + kMemoryTraces;
+constexpr int kMemoryFeatures = 2 * kMemoryFighterFeatures;
+
+struct MemoryEntry {
+    int16_t move_plus_one;  // 0: empty slot
+    int8_t level;           // 1 high, 2 mid, 3 low, 4 throw, 5 no hit
+    int8_t outcome;         // 0 pending, 1 hit, 2 counter hit, 3 blocked, 4 missed or stopped
+    int32_t age;            // frames since it started
+};
+struct FighterMemory {
+    MemoryEntry slots[kMemorySlots];  // newest first
+    int32_t last_move_plus_one, last_action_frame;
+    float traces[kMemoryTraces];
+};
+struct Memory {
+    FighterMemory f[2];
+};
+static_assert(sizeof(Memory) == 120, "two 60-byte fighter memories");
+
+// memory_level (full_move_contract.hpp:648-660)
+T8B_HD int8_t memory_level(const Match& m, int p, int move) {
+    const DMove& mv = move_at(m, p, move);
+    if (mv.hit_count <= 0) return 5;
+    switch (hit_at(m, p, mv, 0).level) {
+        case kHigh: return 1;
+        case kMid:
+        case kSpecialMid: return 2;
+        case kLow:
+        case kSpecialLow: return 3;
+        case kThrow: return 4;
+        default: return 5;
+    }
+}
+
+// memory_update (full_move_contract.hpp:663-712), after every engine frame with its events.
+T8B_HD void memory_update(const Match& m, const Fight& s, const Events& e, int perception_delay, Memory& memory) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        FighterMemory& fm = memory.f[p];
+        const Fighter& f = s.f[p];
+#pragma unroll
+        for (int slot = 0; slot < kMemorySlots; ++slot) {
+            if (fm.slots[slot].move_plus_one != 0) ++fm.slots[slot].age;
+        }
+        const bool ended = f.move < 0 && fm.last_move_plus_one != 0;
+        const bool started = f.move >= 0 && (f.move + 1 != fm.last_move_plus_one || f.action_frame < fm.last_action_frame);
+        if ((ended || started) && fm.slots[0].move_plus_one != 0 && fm.slots[0].outcome == 0) fm.slots[0].outcome = 4;
+        if (started) {
+#pragma unroll
+            for (int slot = kMemorySlots - 1; slot > 0; --slot) fm.slots[slot] = fm.slots[slot - 1];
+            fm.slots[0] = MemoryEntry{static_cast<int16_t>(f.move + 1), memory_level(m, p, f.move), 0, 0};
+        }
+        if (fm.slots[0].move_plus_one != 0 && fm.slots[0].outcome == 0) {
+            for (int k = 0; k < e.contact_count; ++k) {
+                if (e.contacts[k].attacker != p) continue;
+                switch (e.contacts[k].contact) {
+                    case kHit:
+                    case kThrowHeld: fm.slots[0].outcome = 1; break;
+                    case kCounterHit: fm.slots[0].outcome = 2; break;
+                    case kBlocked: fm.slots[0].outcome = 3; break;
+                    default: fm.slots[0].outcome = 4; break;
+                }
+                break;
+            }
+        }
+        const bool idle = f.move < 0;
+        const float signals[kMemoryTraces] = {
+            f.posture == kCrouching ? 1.0F : 0.0F,
+            idle && (f.universal == kWalkBack || f.universal == kBackdash) ? 1.0F : 0.0F,
+            idle && (f.universal == kSidestepLeft || f.universal == kSidestepRight) ? 1.0F : 0.0F,
+            on(f, fInBlockstun) ? 1.0F : 0.0F,
+            f.move >= 0 && f.action_frame >= perception_delay ? 1.0F : 0.0F,
+        };
+#pragma unroll
+        for (int k = 0; k < kMemoryTraces; ++k) fm.traces[k] += (signals[k] - fm.traces[k]) * (1.0F / 60.0F);
+        fm.last_move_plus_one = f.move + 1;
+        fm.last_action_frame = f.action_frame;
+    }
+}
+
+// encode_fighter_memory / encode_memory (full_move_contract.hpp:714-735); kMemoryFeatures floats.
+T8B_HD void encode_fighter_memory(const FighterMemory& fm, int hide_younger_than, float* out) {
+    for (int k = 0; k < kMemoryFighterFeatures; ++k) out[k] = 0.0F;
+    int written = 0;
+    for (int slot = 0; slot < kMemorySlots && written < kMemorySlots; ++slot) {
+        const MemoryEntry& entry = fm.slots[slot];
+        if (entry.move_plus_one == 0 || entry.age < hide_younger_than) continue;
+        float* at = out + written * kMemorySlotFeatures;
+        if (entry.level >= 1 && entry.level <= 5) at[entry.level - 1] = 1.0F;
+        if (entry.outcome >= 1 && entry.outcome <= 4) at[4 + entry.outcome] = 1.0F;
+        at[9] = c01(entry.age / 180.0);
+        ++written;
+    }
+    for (int k = 0; k < kMemoryTraces; ++k) out[kMemorySlots * kMemorySlotFeatures + k] = fm.traces[k];
+}
+T8B_HD void encode_memory(const Memory& memory, int player, int perception_delay, float* out) {
+    encode_fighter_memory(memory.f[player], 0, out);
+    encode_fighter_memory(memory.f[1 - player], perception_delay, out + kMemoryFighterFeatures);
+}
+
 // ------------------------------------------------------------------ one decision
 struct StepOut {
     float reward, sparse;
@@ -591,7 +698,7 @@ T8B_HD bool is_held(const Input& in) {
 template <int L>
 T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int opponent_candidate, double aggression,
                            const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream, uint64_t counter,
-                           const Noise* noise) {
+                           const Noise* noise, Memory* memory = nullptr) {
     constexpr int learner = L;
     StepOut r{0.0F, 0.0F, 0, 0, 0};
     int lag = 0;
@@ -629,6 +736,7 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
             if (!to_input(*m.side[op], choice, other)) other = Input{-1, kIdle};
         }
         frame_step(m, s, learner == 0 ? own : other, learner == 0 ? other : own, e);
+        if (memory != nullptr) memory_update(m, s, e, ec.perception_delay, *memory);
         ++r.frames;
         distance_frames += mag(s.f[0].x - s.f[1].x);
         for (int k = 0; k < e.contact_count; ++k) {
@@ -660,11 +768,11 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
 
 T8B_HD StepOut decision(const Match& m, Fight& s, int learner, int learner_candidate, int opponent_candidate,
                         double aggression, const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream,
-                        uint64_t counter, const Noise* noise) {
+                        uint64_t counter, const Noise* noise, Memory* memory = nullptr) {
     return learner == 0 ? decision_as<0>(m, s, learner_candidate, opponent_candidate, aggression, ec, profiles, seed,
-                                         stream, counter, noise)
+                                         stream, counter, noise, memory)
                         : decision_as<1>(m, s, learner_candidate, opponent_candidate, aggression, ec, profiles, seed,
-                                         stream, counter, noise);
+                                         stream, counter, noise, memory);
 }
 
 }  // namespace t8b

@@ -62,6 +62,7 @@ struct SimView {
     const int32_t* pending_scenarios;
     const int32_t* pending_learners;
     Noise* noise;  // null without live noise
+    Memory* memories;  // null without --memory
     float* learner_obs;
     float* opponent_obs;
     int32_t* learner_tables;
@@ -125,7 +126,8 @@ __device__ void write_observations(const SimView& v, const Staged& st, const Mat
     const int other = L == 0 ? p2 : p1;
     float* lo = v.learner_obs + env * static_cast<size_t>(v.width);
     float* oo = v.opponent_obs + env * static_cast<size_t>(v.width);
-    float buf[kObservationBase + 3];
+    float buf[kObservationBase + kMemoryFeatures + 3];
+    const int noise_at = kObservationBase + (v.memories != nullptr ? kMemoryFeatures : 0);
 #pragma unroll
     for (int side = 0; side < 2; ++side) {
         const int player = side == 0 ? L : 1 - L;
@@ -133,10 +135,11 @@ __device__ void write_observations(const SimView& v, const Staged& st, const Mat
         const int them = side == 0 ? other : own;
         observe(m, s, player, ec.max_round_frames, st.chars[me].roster_id, st.chars[them].roster_id, buf,
                 ec.perception_delay);
+        if (v.memories != nullptr) encode_memory(v.memories[env], player, ec.perception_delay, buf + kObservationBase);
         if (v.noise != nullptr) {
             const Noise n = v.noise[env];
             perturb(n, s, player, buf);
-            noise_features(n, buf + kObservationBase);
+            noise_features(n, buf + noise_at);
         }
         if (ec.screen_view) screen_view(buf);
         float* out = side == 0 ? lo : oo;
@@ -170,10 +173,17 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
     Fight s = v.states[env];
     const float aggression = v.aggression[env];
     const Noise* noise = v.noise != nullptr ? v.noise + env : nullptr;
+    Memory memory;
+    Memory* remembered = nullptr;
+    if (v.memories != nullptr) {
+        memory = v.memories[env];
+        remembered = &memory;
+    }
     const StepOut r = decision_as<L>(m, s, static_cast<int>(learner_candidates[env]),
                                      opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1,
-                                     aggression, *st.ecfg, v.profiles, seed, env, counter, noise);
+                                     aggression, *st.ecfg, v.profiles, seed, env, counter, noise, remembered);
     v.states[env] = s;
+    if (remembered != nullptr) v.memories[env] = memory;
     v.rewards[env] = r.reward;
     v.sparse[env] = r.sparse;
     v.terminated[env] = r.terminated ? 1 : 0;
@@ -259,6 +269,7 @@ __global__ void __launch_bounds__(kStepThreads) k_reset(SimView v, const uint8_t
     Fight s;
     start_round(m, s, *st.ecfg, seed, env, counter, scenario, learner);
     v.states[env] = s;
+    if (v.memories != nullptr) v.memories[env] = Memory{};
     write_observations(v, st, m, s, env, p1, p2, learner);
 }
 
@@ -735,6 +746,7 @@ struct t8b_sim {
     int sm_count = 1;
     Buffer<float> aggression, pending_aggression;
     Buffer<Noise> noise;
+    Buffer<Memory> memories;  // config.memory only
     Buffer<float> learner_obs, opponent_obs;
     Buffer<int32_t> learner_tables, opponent_tables;
     Buffer<uint32_t> learner_bits, opponent_bits;
@@ -755,6 +767,7 @@ struct t8b_sim {
         v.pending_aggression = pending_aggression.data(); v.scenarios = scenarios.data();
         v.pending_scenarios = pending_scenarios.data(); v.pending_learners = pending_learners.data();
         v.noise = config.live_noise ? noise.data() : nullptr;
+        v.memories = config.memory ? memories.data() : nullptr;
         v.learner_obs = learner_obs.data(); v.opponent_obs = opponent_obs.data();
         v.learner_tables = learner_tables.data(); v.opponent_tables = opponent_tables.data();
         v.learner_bits = learner_bits.data(); v.opponent_bits = opponent_bits.data();
@@ -862,7 +875,6 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
             !(config->start_distance_max >= config->start_distance_min) || !(config->start_distance_min > 0.0)) {
             raise(T8B_EINVAL, "full-move environment configuration is invalid");
         }
-        if (config->memory) raise(T8B_EINVAL, "the --memory observation is not supported by this simulator");
         auto sim = std::make_unique<t8b_sim>();
         sim->n = environments;
         {
@@ -872,7 +884,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         }
         sim->roster = roster_count;
         sim->config = *config;
-        sim->width = kObservationBase + (config->live_noise ? T8B_NOISE_FEATURES : 0);
+        sim->width = kObservationBase + (config->memory ? kMemoryFeatures : 0) + (config->live_noise ? T8B_NOISE_FEATURES : 0);
         const size_t n = environments;
 
         HostRoster host = pack_roster(roster, roster_count);
@@ -927,6 +939,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         sim->pending_learners.allocate(n); sim->scenarios.allocate(n); sim->pending_scenarios.allocate(n);
         sim->learner_is_p1.allocate(n); sim->terminated.allocate(n); sim->truncated.allocate(n);
         sim->aggression.allocate(n); sim->pending_aggression.allocate(n);
+        if (config->memory) sim->memories.allocate(n);
         if (config->live_noise) sim->noise.allocate(n);
         sim->learner_obs.allocate(n * static_cast<size_t>(sim->width));
         sim->opponent_obs.allocate(n * static_cast<size_t>(sim->width));
@@ -1219,6 +1232,7 @@ int t8b_sim_restore(t8b_sim* sim, const t8b_state_t* states, const int32_t* p1, 
             launch("k_draw_noise", k_draw_noise, blocks(s.n, 256), 256, 0, s.stream, s.view(), 0x5eedull);
             s.launched("draw noise levels");
         }
+        if (s.config.memory) s.memories.zero(s.stream);  // memory is not part of a snapshot: it restarts empty
         launch("k_observe", k_observe, blocks(s.n, kStepThreads), kStepThreads, s.smem(), s.stream, s.view());
         s.launched("observe");
         s.masks(nullptr);

@@ -133,14 +133,16 @@ def test_env_matches_golden_digests(cuda, roster):
         sim.reset_done(seed, step)
 
 
-@pytest.mark.parametrize("noise,screen,self_play", [(1, 1, False), (0, 0, False), (1, 0, True)])
-def test_env_matches_reference_contract(cuda, roster, ref_roster, noise, screen, self_play):
-    """Step for step against the reference contract on the host, all outputs compared."""
+@pytest.mark.parametrize("noise,screen,self_play,memory", [(1, 1, False, 0), (0, 0, False, 0), (1, 0, True, 0),
+                                                             (1, 0, False, 1), (0, 0, True, 1)])
+def test_env_matches_reference_contract(cuda, roster, ref_roster, noise, screen, self_play, memory):
+    """Step for step against the reference contract on the host, all outputs compared (with
+    --memory the observation carries each fighter's move history and habit traces)."""
     import torch
     from oracle import ref
     from t8b.sim import GpuFullMoveSimulator
     n, steps, seed = 256, 150, 31
-    config = env_config(live_noise=noise, screen_view=screen, perception_delay=12 if noise else 0,
+    config = env_config(live_noise=noise, screen_view=screen, perception_delay=12 if noise else 0, memory=memory,
                         damage_dealt_weight=0.8, damage_taken_weight=1.2, distance_penalty_per_second=0.002)
     p1, p2, sides, opponents, aggression, scenarios = make_golden.env_case(n)
     sim = GpuFullMoveSimulator(roster, n, config)
@@ -152,6 +154,7 @@ def test_env_matches_reference_contract(cuda, roster, ref_roster, noise, screen,
               learners=np.full(n, -1))
     sim.reset_all(seed, 0)
     cpu.reset_all(seed, 0)
+    assert sim.observation_size() == cpu.width == 148 + 90 * memory + 3 * noise
     rng = np.random.default_rng(3)
     terminations = 0
     for step in range(1, steps + 1):
