@@ -294,6 +294,12 @@ def run_ours(args):
     profile.enable(False)
     frames = trainer.sim.frames_simulated() - frames_before
     total_device = sum(device_ms)
+    per_rank = [total_device / args.steps]
+    if world > 1:
+        gathered = [torch.zeros(1, dtype=torch.float64, device="cuda") for _ in range(world)]
+        torch.distributed.all_gather(gathered, torch.tensor([total_device / args.steps], dtype=torch.float64,
+                                                             device="cuda"))
+        per_rank = [g.item() for g in gathered]
     total_device, wall, rollout_total = max_over_ranks([total_device, wall, sum(rollout_ms)], "cuda")
     units = args.envs * args.horizon * world * args.steps
     value = units / (total_device / 1000.0)
@@ -324,6 +330,7 @@ def run_ours(args):
         "engine_frames_per_s": frames / (total_device / 1000.0) * world,
         "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": bytes_up // args.steps,
                 "d2h_bytes_per_step": bytes_down // args.steps},
+        "rank_ms_per_step": per_rank,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
         "roofline": roofline,
