@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the self-play training hot path (scaled out as config 5).
+"""Benchmark of the self-play training hot path: one training iteration per GPU, scaled out by data parallelism.
 
 One step = one training iteration per GPU: a 128-decision rollout over 32,768 fights (policy
 forward, simulator decision, resets), return normalisation, GAE and the PPO update (4 epochs x 8
@@ -45,7 +45,7 @@ def parse():
                     help="mirror self-play: a frozen copy of the initial policy plays the other side")
     ap.add_argument("--workload", choices=("iteration", "mlp"), default="iteration",
                     help="iteration: the self-play training iteration (the headline); mlp: policy forward + "
-                         "backward on one batch of 32,768 at the config-3 shapes (128 observations, 256 candidates "
+                         "backward on one batch of 32,768 at the microbench shapes (128 observations, 256 candidates "
                          "x 48 features, 2 x 512 hidden)")
     return ap.parse_args()
 
@@ -349,7 +349,7 @@ def run_ours(args):
 
 def run_mlp(args):
     """Policy forward + backward (one PPO minibatch update: forward, objective, backward, Adam)
-    on a batch of 32,768 at the config-3 shapes, with the GEMMs' tensor-core roofline."""
+    on a batch of 32,768 at the microbench shapes, with the GEMMs' tensor-core roofline."""
     import numpy as np
     import torch
     from t8b import profile

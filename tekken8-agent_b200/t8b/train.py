@@ -23,7 +23,7 @@ from .sim import GpuFullMoveSimulator, env_config
 
 
 def config4_env(**overrides):
-    """BASELINE config 4 / training.ini: screen-only observation with live noise (sigma 0.28 m,
+    """The measured self-play configuration (training.ini): screen-only observation with live noise (sigma 0.28 m,
     detection errors 10 %, latency 2-6 frames), perception delay 12, 8-frame holds, and the
     trainer's anti-stalling terms (src/train_launcher.cpp:106-160)."""
     base = dict(screen_view=1, live_noise=1, noise_position_max=0.28, noise_flip_max=0.10, latency_min=2,

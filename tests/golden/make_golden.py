@@ -1,4 +1,4 @@
-"""Regenerates the golden fixtures from the reference itself (run where /root/reference is).
+"""Regenerates the golden fixtures from the reference itself (run where the reference checkout is).
 
   roster41.bin.xz   the 41 fighters with moves, loaded by the reference's own loader
                     (src/full_move_roster.cpp:51, stand-in geometry as the trainer's

@@ -284,7 +284,7 @@ def test_observation_normalizer_merges_like_the_reference(cuda, features):
 
 
 def test_gae_and_advantage_normalization_config2(cuda):
-    """BASELINE config 2 shapes: T = 128, N = 32,768."""
+    """The GAE microbench shapes: T = 128, N = 32,768."""
     import torch
     from t8b.policy import GpuRolloutBuffer
     rng = np.random.default_rng(1)

@@ -41,7 +41,7 @@ def batch(n, tables, rng, width=151):
 
 
 def config3_features(rng, tables=41, slots=256):
-    """Synthetic move properties with the shapes of the config-3 microbench: 48 features per
+    """Synthetic move properties with the shapes of the policy microbench: 48 features per
     candidate slot, integers stored as floats (startup 10-30, recovery -15..+10, damage 5-40,
     ...) and a one-hot hit level."""
     f = np.zeros((tables, slots, 48), np.float32)
@@ -58,7 +58,7 @@ def config3_features(rng, tables=41, slots=256):
 SHAPES = {
     # the reference's full-move network: 151 observations, 368 candidates x 32 fixed features
     "full_move": dict(),
-    # the config-3 shapes: 128 observations, 256 candidate slots x 48 features
+    # the policy microbench shapes: 128 observations, 256 candidate slots x 48 features
     "config3": dict(observation_size=128, action_count=256, action_feature_size=48),
 }
 

@@ -31,7 +31,7 @@ def test_random_play_matches_golden(cuda, roster):
 
 
 def test_random_play_config1_matches_reference(cuda, roster, ref_roster):
-    """1,024 fights over uniform pairs of the 41 fighters, 3,600 frames,
+    """The engine-parity workload: 1,024 fights over uniform pairs of the 41 fighters, 3,600 frames,
     PCG32 seed 0 per fight index; per-frame state hashes equal the reference CPU engine's."""
     from t8b.sim import GpuFullMoveSimulator
     rng = np.random.default_rng(0)
