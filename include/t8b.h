@@ -495,6 +495,17 @@ int t8b_rollout_return_normalizer_state(t8b_rollout* rollout, uint64_t* count, d
 int t8b_rollout_restore_return_normalizer_state(t8b_rollout* rollout, uint64_t count, double mean, double variance,
                                                 const float* discounted_returns);
 int t8b_rollout_set_comm(t8b_rollout* rollout, const t8b_comm_t* comm);
+/* The trainer's rollout loop as one call (no reference counterpart: src/full_move_train.cpp:
+ * 1374-1400 runs it in C++ around the three objects). For each of `horizon` decisions with
+ * counter = update * horizon + step: the learner's forward on its observations, packed masks
+ * and feature tables (seed + 1, sampling), the previous decision's outcome recorded with this
+ * forward's values as its bootstrap, the decision recorded, the simulator stepped (counter + 1;
+ * with `opponent`, a frozen policy's forward with seed + 2 on a second stream chooses the
+ * opponent side's candidates), and finished rounds reset; after the last decision a
+ * deterministic forward (seed + 3) gives the final bootstrap. Everything is queued on `stream`
+ * (the simulator's stream is set to it). */
+int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout* rollout, t8b_policy* opponent, uint64_t seed,
+                        uint64_t update, size_t horizon, float reward_scale, void* stream);
 int t8b_rollout_synchronize(t8b_rollout* rollout, void* stream);
 
 #ifdef __cplusplus

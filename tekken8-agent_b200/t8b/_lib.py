@@ -348,5 +348,6 @@ PROTOTYPES.update({
                                                       C.POINTER(C.c_double), vp]),
     "t8b_rollout_restore_return_normalizer_state": (C.c_int, [vp, u64, C.c_double, C.c_double, vp]),
     "t8b_rollout_set_comm": (C.c_int, [vp, C.POINTER(Comm)]),
+    "t8b_collect_rollout": (C.c_int, [vp, vp, vp, vp, u64, u64, C.c_size_t, C.c_float, vp]),
     "t8b_rollout_synchronize": (C.c_int, [vp, vp]),
 })

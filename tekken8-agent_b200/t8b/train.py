@@ -19,6 +19,7 @@ import numpy as np
 import torch
 
 from .policy import GpuActorCritic, GpuRolloutBuffer, actor_config, ppo_config
+from ._lib import call
 from .sim import GpuFullMoveSimulator, env_config
 
 
@@ -105,11 +106,30 @@ class SelfPlayTrainer:
         self.sim.set_pending_learners(self.learners)
         return 4 * 4 * self.n
 
-    def iterate(self):
-        """One update: rollout + return normalisation + GAE + PPO. Returns the PPO metrics."""
+    def iterate(self, native: bool = True):
+        """One update: rollout + return normalisation + GAE + PPO. Returns the PPO metrics.
+
+        The rollout loop runs natively (t8b_collect_rollout) unless native is False, which
+        runs the same sequence of calls from Python."""
         update = self.update_index = self.update_index + 1
-        t, n = self.horizon, self.n
         self.policy.prepare_shuffle(self.samples, self.epochs, self.seed + update)
+        sim, policy, rollout = self.sim, self.policy, self.rollout
+        if native:
+            call("t8b_collect_rollout", sim.handle, policy._handle, rollout._handle,
+                 self.opponent._handle if self.opponent is not None else None, self.seed, update, self.horizon, 1.0,
+                 None)
+        else:
+            self.rollout_from_python(update)
+        marker = getattr(self, "rollout_event", None)
+        if marker is not None:
+            marker.record()
+        rollout.normalize_rewards(0.99)
+        rollout.compute_gae(0.99, 0.95, True)
+        return policy.update_ppo(rollout.device_view(packed=True), self.ppo, self.seed + update)
+
+    def rollout_from_python(self, update):
+        """The rollout loop of t8b_collect_rollout, call for call, from Python."""
+        t, n = self.horizon, self.n
         sim, policy, rollout = self.sim, self.policy, self.rollout
         tables = sim.learner_feature_tables()
         for step in range(t):
@@ -129,12 +149,6 @@ class SelfPlayTrainer:
                                       mask_bits=sim.learner_mask_bits())
                 rollout.record_outcome_device(step, sim.rewards(), sim.terminated(), sim.truncated(), last["values"])
             sim.reset_done(self.seed, counter + 1)
-        marker = getattr(self, "rollout_event", None)
-        if marker is not None:
-            marker.record()
-        rollout.normalize_rewards(0.99)
-        rollout.compute_gae(0.99, 0.95, True)
-        return policy.update_ppo(rollout.device_view(packed=True), self.ppo, self.seed + update)
 
     def opponent_launch(self, counter):
         """Enqueues the frozen policy's forward for this decision on the opponent stream, after

@@ -259,3 +259,26 @@ def test_self_play_iteration_with_a_checkpoint_opponent(cuda, roster, tmp_path):
         results.append((trainer.policy.parameters(), trainer.sim.download_state_bytes()))
     assert np.array_equal(results[0][0], results[1][0])
     assert np.array_equal(results[0][1], results[1][1])
+
+
+@pytest.mark.parametrize("self_play", [False, True])
+def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self_play):
+    """t8b_collect_rollout issues the same calls as the trainer's Python loop: one iteration
+    from the same seeds gives bit-identical weights, simulator states and advantages."""
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config
+    from t8b.train import SelfPlayTrainer
+    opponent = None
+    if self_play:
+        GpuActorCritic(1024, actor_config(), 8).save_checkpoint(tmp_path / "frozen.t8ppo")
+        opponent = tmp_path / "frozen.t8ppo"
+    results = []
+    for native in (True, False):
+        trainer = SelfPlayTrainer(roster, environments=1024, horizon=8, epochs=1, minibatches=2, seed=11,
+                                  opponent=opponent)
+        trainer.iterate(native=native)
+        torch.cuda.synchronize()
+        results.append((trainer.policy.parameters(), trainer.sim.download_state_bytes(),
+                        trainer.rollout.tensor("advantages").cpu().numpy().copy()))
+    for a, b in zip(*results):
+        assert np.array_equal(a, b)
