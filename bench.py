@@ -55,22 +55,26 @@ def roster_raw():
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region. One process
+    samples every GPU of the job (local rank 0 passes them all), so N ranks do not start N
+    pollers of the driver."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
-        self.index = index
+    def __init__(self, indices):
+        self.indices = list(indices)
         self.rows = []
         self.proc = None
 
     def __enter__(self):
+        if not self.indices:
+            return self
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", ",".join(map(str, self.indices)),
+                                          f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -80,7 +84,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) == 8:
+            if len(parts) == 9:
                 self.rows.append(parts)
 
     def __exit__(self, *exc):
@@ -94,13 +98,21 @@ class ClockSampler:
     def summary(self):
         if not self.rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
-        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        number = lambda v: v.replace(".", "").isdigit()
+        sm = [float(r[1]) for r in self.rows if number(r[1])]
+        mx = [float(r[2]) for r in self.rows if number(r[2])]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower() == "active"})
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower() == "active"})
         loaded = [s for s in sm if s > 0]
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+        out = {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+               "reasons": reasons, "samples": len(self.rows)}
+        if len(self.indices) > 1:
+            per = {}
+            for r in self.rows:
+                if number(r[1]) and float(r[1]) > 0:
+                    per.setdefault(r[0], []).append(float(r[1]))
+            out["sm_mhz_per_gpu"] = {k: statistics.median(v) for k, v in sorted(per.items())}
+        return out
 
 
 def distributed():
@@ -267,11 +279,18 @@ def run_ours(args):
     torch.cuda.synchronize()
     device_ms = []
     rollout_ms = []
+    host_queue_ms = []
     bytes_up = bytes_down = 0
     frames_before = trainer.sim.frames_simulated()
     launches_before = profile.launch_count()
     profile.enable(True)
-    with ClockSampler(local) as clocks:
+    # local rank 0 samples every GPU of this node's ranks (device i for local rank i, named as
+    # nvidia-smi counts them when CUDA_VISIBLE_DEVICES renumbers the devices)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", str(world)))
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    physical = [v.strip() for v in visible.split(",")] if visible and all(
+        v.strip().isdigit() for v in visible.split(",")) else [str(i) for i in range(local_world)]
+    with ClockSampler(physical[:local_world] if local == 0 else []) as clocks:
         wall0 = time.perf_counter()
         for _ in range(args.steps):
             up, down = trainer.host_boundary()
@@ -281,6 +300,7 @@ def run_ours(args):
             start.record()
             trainer.rollout_event = mid
             metrics = trainer.iterate()
+            host_queue_ms.append(trainer.rollout_host_ms)
             end.record()
             end.synchronize()
             device_ms.append(start.elapsed_time(end))
@@ -331,6 +351,8 @@ def run_ours(args):
         "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": bytes_up // args.steps,
                 "d2h_bytes_per_step": bytes_down // args.steps},
         "rank_ms_per_step": per_rank,
+        "host": {"cpus_usable": len(os.sched_getaffinity(0)), "rollout_queue_ms_per_step":
+                 sum(host_queue_ms) / len(host_queue_ms)},
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / args.steps,
         "roofline": roofline,

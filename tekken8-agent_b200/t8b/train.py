@@ -15,6 +15,8 @@ Two changes of schedule, neither of which changes what is learned:
 """
 from __future__ import annotations
 
+import time
+
 import numpy as np
 import torch
 
@@ -114,12 +116,14 @@ class SelfPlayTrainer:
         update = self.update_index = self.update_index + 1
         self.policy.prepare_shuffle(self.samples, self.epochs, self.seed + update)
         sim, policy, rollout = self.sim, self.policy, self.rollout
+        started = time.perf_counter()
         if native:
             call("t8b_collect_rollout", sim.handle, policy._handle, rollout._handle,
                  self.opponent._handle if self.opponent is not None else None, self.seed, update, self.horizon, 1.0,
                  None)
         else:
             self.rollout_from_python(update)
+        self.rollout_host_ms = 1000.0 * (time.perf_counter() - started)  # time to queue the rollout
         marker = getattr(self, "rollout_event", None)
         if marker is not None:
             marker.record()
