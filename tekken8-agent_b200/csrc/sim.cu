@@ -37,11 +37,12 @@ static_assert(sizeof(DMove) == 304, "compact move record");
 
 constexpr int kMaskWords = 12;  // 368 candidates in 32-bit words
 constexpr unsigned kStepThreads = 128;
-// Fights per warp in k_step. The decision loop is one dependent chain per fight and its
-// lanes diverge; fewer fights per warp (more warps, narrower path unions) measured slower on
-// B200 at 32,768 fights (16 lanes +8 %, 8 lanes +35 % per step), so every lane carries a fight.
-constexpr unsigned kStepLanes = 32;
-constexpr unsigned kStepFightsPerBlock = kStepThreads / 32 * kStepLanes;
+// k_step runs one fight per lane: the decision loop is one dependent chain per fight and its
+// lanes diverge, and fewer fights per warp (more warps, narrower path unions) measured slower
+// on B200 at 32,768 fights (16 lanes +8 %, 8 lanes +35 % per step). Its blocks hold up to 8
+// warps (210 registers per thread, no spills; 9 warps spill) and it runs one block per SM;
+// step_grid picks the block size.
+constexpr unsigned kStepMaxWarps = 8;
 constexpr unsigned kMaskThreads = 256;
 
 // Pointers every kernel needs, passed by value.
@@ -205,11 +206,11 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
 // env_step_kernel (src/full_move_gpu.cu:188-229) with the observation pass fused in.
 //
 // The frame loop is compiled once per learner side (step_fight<0>, step_fight<1>), and an SM
-// that runs both copies at once thrashes its instruction cache. So the grid is two blocks per
+// that runs both copies at once thrashes its instruction cache. So the grid is one block per
 // SM, each block takes the side its SM serves (SMs below the P1 share of the fights serve P1)
-// and pulls 128-fight chunks of that side (side_order lists P1-learner fights first) from a
-// per-side ticket; when its side runs out it helps with the other side.
-__global__ void __launch_bounds__(kStepThreads, 1) k_step(SimView v, const int64_t* learner_candidates,
+// and pulls chunks of that side, one fight per thread (side_order lists P1-learner fights
+// first), from a per-side ticket; when its side runs out it helps with the other side.
+__global__ void __launch_bounds__(kStepMaxWarps * 32, 1) k_step(SimView v, const int64_t* learner_candidates,
                                                             const int64_t* opponent_candidates, uint64_t seed,
                                                             uint64_t counter, unsigned* tickets, uint32_t p1_fights) {
     const Staged st = stage_tables(v);
@@ -218,28 +219,49 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(SimView v, const int64
     asm("mov.u32 %0, %%smid;" : "=r"(smid));
     asm("mov.u32 %0, %%nsmid;" : "=r"(nsmid));
     int side = static_cast<uint64_t>(smid) * v.count < static_cast<uint64_t>(p1_fights) * nsmid ? 0 : 1;
-    const unsigned lane = threadIdx.x & 31u;
-    const unsigned offset = (threadIdx.x >> 5) * kStepLanes + lane;
     unsigned long long frames = 0;
     for (int sides_done = 0; sides_done < 2;) {
         __syncthreads();
         if (threadIdx.x == 0) chunk = atomicAdd(tickets + side, 1u);
         __syncthreads();
-        const size_t first = static_cast<size_t>(chunk) * kStepFightsPerBlock;
+        const size_t first = static_cast<size_t>(chunk) * blockDim.x;
         const size_t count = side == 0 ? p1_fights : v.count - p1_fights;
         if (first >= count) {
             side ^= 1;
             ++sides_done;
             continue;
         }
-        const size_t in_side = first + offset;
-        if (lane < kStepLanes && in_side < count) {
+        const size_t in_side = first + threadIdx.x;
+        if (in_side < count) {
             const size_t env = v.side_order[(side == 0 ? 0 : p1_fights) + in_side];
             frames += side == 0 ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter)
                                 : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter);
         }
     }
     add_frames(v, frames);
+}
+
+// k_step's launch shape: the fewest waves of one block per SM, then the fewest warps per block
+// whose chunks (counted per side, as the blocks take them) fit in those waves, so every SM
+// carries about the same number of warps (32,768 fights on 148 SMs: 148 blocks of 7 warps).
+// One block of 7 warps per SM measured 9 % faster than two blocks of 4 per SM (108 SMs with 8
+// warps, 40 with 4) at 32,768 fights.
+struct StepGrid {
+    unsigned blocks, threads;
+};
+inline StepGrid step_grid(size_t fights, size_t p1_fights, int sm_count) {
+    const size_t sms = static_cast<size_t>(std::max(sm_count, 1));
+    const auto chunks = [&](size_t threads) {
+        return (p1_fights + threads - 1) / threads + (fights - p1_fights + threads - 1) / threads;
+    };
+    for (size_t waves = 1;; ++waves) {
+        for (size_t warps = 1; warps <= kStepMaxWarps; ++warps) {
+            const size_t c = chunks(warps * 32);
+            if (c <= waves * sms) {
+                return {static_cast<unsigned>(std::max<size_t>(std::min(c, sms), 1)), static_cast<unsigned>(warps * 32)};
+            }
+        }
+    }
 }
 
 // env_reset_kernel (src/full_move_gpu.cu:231-255) with the observation pass fused in.
@@ -1105,8 +1127,8 @@ int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, 
         if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
         if (s.step_tickets.size() == 0) s.step_tickets.allocate(2);
         s.step_tickets.zero(s.stream);
-        const unsigned grid = std::min<unsigned>(blocks(s.n, kStepFightsPerBlock), 2u * static_cast<unsigned>(s.sm_count));
-        launch("k_step", k_step, grid, kStepThreads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter,
+        const StepGrid g = step_grid(s.n, s.p1_fights, s.sm_count);
+        launch("k_step", k_step, g.blocks, g.threads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter,
                s.step_tickets.data(), s.p1_fights);
         s.launched("step");
         s.masks(nullptr);
