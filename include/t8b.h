@@ -248,6 +248,14 @@ int t8b_sim_reset_all(t8b_sim* sim, uint64_t seed, uint64_t counter);
 int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter);
 int t8b_sim_step(t8b_sim* sim, const int64_t* learner_candidates, const int64_t* opponent_candidates, uint64_t seed,
                  uint64_t counter);
+/* No reference counterpart: t8b_sim_step followed by t8b_sim_reset_done with the same seed and
+ * counter, in one launch sequence. A fight whose round ends is reset inside the step, so its
+ * terminal observations are never written; states, matchups, noise levels, rewards,
+ * terminations, outcomes, tallies, and the observations and masks after the call equal those
+ * after the two calls. (The trainer reads no terminal observation except at the last decision
+ * of a rollout, where it bootstraps from them before resetting.) */
+int t8b_sim_step_and_reset(t8b_sim* sim, const int64_t* learner_candidates, const int64_t* opponent_candidates,
+                           uint64_t seed, uint64_t counter);
 /* Device views  full_move_gpu.hpp:96-112. Masks are uint8 [env][368] as in the
  * reference; t8b_sim_learner_mask_bits gives the packed form the library keeps
  * (12 uint32 words per environment, bit c of word c/32 = candidate c). The opponent's masks

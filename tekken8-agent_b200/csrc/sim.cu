@@ -162,13 +162,41 @@ __device__ __forceinline__ void add_frames(const SimView& v, unsigned long long 
     if ((threadIdx.x & 31) == 0 && frames != 0) atomicAdd(v.frames, frames);
 }
 
+// One fight's round reset (env_reset_kernel, src/full_move_gpu.cu:231-255): fresh live-noise
+// levels, the pending matchup, aggression and scenario, and a new round's state, stored; p1 and
+// p2 come back as the new matchup.
+__device__ __forceinline__ Fight reset_fight(const SimView& v, const Staged& st, size_t env, uint64_t seed,
+                                             uint64_t counter, int& p1, int& p2) {
+    if (v.noise != nullptr) v.noise[env] = draw_noise(*st.ecfg, seed, env, counter);
+    const bool learner_p1 = v.learner_is_p1[env] != 0;
+    if (learner_p1) {
+        p2 = v.pending_opponents[env];
+        if (v.pending_learners[env] >= 0) p1 = v.pending_learners[env];
+    } else {
+        p1 = v.pending_opponents[env];
+        if (v.pending_learners[env] >= 0) p2 = v.pending_learners[env];
+    }
+    v.p1[env] = p1;
+    v.p2[env] = p2;
+    v.aggression[env] = v.pending_aggression[env];
+    const int scenario = v.pending_scenarios[env];
+    v.scenarios[env] = scenario;
+    Fight s;
+    start_round(match_of(st, p1, p2), s, *st.ecfg, seed, env, counter, scenario, learner_p1 ? 0 : 1);
+    v.states[env] = s;
+    if (v.memories != nullptr) v.memories[env] = Memory{};
+    return s;
+}
+
 // One fight's decision with the learner on side L: the state stays in registers through the
 // frame loop (every fighter index is a constant), then the outcome, tallies and observations.
+// With `reset`, a fight whose round ended is reset at once (reset_fight with the step's seed
+// and counter, as reset_done would do next) and only the new round's observations are written.
 template <int L>
 __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const Staged& st, size_t env,
                                                          const int64_t* learner_candidates,
                                                          const int64_t* opponent_candidates, uint64_t seed,
-                                                         uint64_t counter) {
+                                                         uint64_t counter, bool reset) {
     const int p1 = v.p1[env], p2 = v.p2[env];
     const Match m = match_of(st, p1, p2);
     Fight s = v.states[env];
@@ -183,8 +211,6 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
     const StepOut r = decision_as<L>(m, s, static_cast<int>(learner_candidates[env]),
                                      opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1,
                                      aggression, *st.ecfg, v.profiles, seed, env, counter, noise, remembered);
-    v.states[env] = s;
-    if (remembered != nullptr) v.memories[env] = memory;
     v.rewards[env] = r.reward;
     v.sparse[env] = r.sparse;
     v.terminated[env] = r.terminated ? 1 : 0;
@@ -199,7 +225,14 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
         const int bot = bot_id(aggression);
         if (bot >= 0 && bot < T8B_SCRIPTED_PROFILES) atomicAdd(&v.bot_tally[bot * 3 + column], 1u);
     }
-    write_observations<L>(v, st, m, s, env, p1, p2);
+    int q1 = p1, q2 = p2;
+    if (reset && r.terminated) {
+        s = reset_fight(v, st, env, seed, counter, q1, q2);
+    } else {
+        v.states[env] = s;
+        if (remembered != nullptr) v.memories[env] = memory;
+    }
+    write_observations<L>(v, st, match_of(st, q1, q2), s, env, q1, q2);
     return static_cast<unsigned long long>(r.frames);
 }
 
@@ -212,7 +245,8 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
 // first), from a per-side ticket; when its side runs out it helps with the other side.
 __global__ void __launch_bounds__(kStepMaxWarps * 32, 1) k_step(SimView v, const int64_t* learner_candidates,
                                                             const int64_t* opponent_candidates, uint64_t seed,
-                                                            uint64_t counter, unsigned* tickets, uint32_t p1_fights) {
+                                                            uint64_t counter, unsigned* tickets, uint32_t p1_fights,
+                                                            int reset) {
     const Staged st = stage_tables(v);
     __shared__ unsigned chunk;
     unsigned smid, nsmid;
@@ -234,8 +268,9 @@ __global__ void __launch_bounds__(kStepMaxWarps * 32, 1) k_step(SimView v, const
         const size_t in_side = first + threadIdx.x;
         if (in_side < count) {
             const size_t env = v.side_order[(side == 0 ? 0 : p1_fights) + in_side];
-            frames += side == 0 ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter)
-                                : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter);
+            frames += side == 0
+                ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0)
+                : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0);
         }
     }
     add_frames(v, frames);
@@ -271,28 +306,9 @@ __global__ void __launch_bounds__(kStepThreads) k_reset(SimView v, const uint8_t
     const size_t env = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (env >= v.count) return;
     if (only_done != nullptr && !only_done[env]) return;
-    if (v.noise != nullptr) v.noise[env] = draw_noise(*st.ecfg, seed, env, counter);
     int p1 = v.p1[env], p2 = v.p2[env];
-    const bool learner_p1 = v.learner_is_p1[env] != 0;
-    if (learner_p1) {
-        p2 = v.pending_opponents[env];
-        if (v.pending_learners[env] >= 0) p1 = v.pending_learners[env];
-    } else {
-        p1 = v.pending_opponents[env];
-        if (v.pending_learners[env] >= 0) p2 = v.pending_learners[env];
-    }
-    v.p1[env] = p1;
-    v.p2[env] = p2;
-    v.aggression[env] = v.pending_aggression[env];
-    const int scenario = v.pending_scenarios[env];
-    v.scenarios[env] = scenario;
-    const Match m = match_of(st, p1, p2);
-    const int learner = learner_p1 ? 0 : 1;
-    Fight s;
-    start_round(m, s, *st.ecfg, seed, env, counter, scenario, learner);
-    v.states[env] = s;
-    if (v.memories != nullptr) v.memories[env] = Memory{};
-    write_observations(v, st, m, s, env, p1, p2, learner);
+    const Fight s = reset_fight(v, st, env, seed, counter, p1, p2);
+    write_observations(v, st, match_of(st, p1, p2), s, env, p1, p2, v.learner_is_p1[env] != 0 ? 0 : 1);
 }
 
 // Observations of every fight from its stored state (restore).
@@ -1122,17 +1138,29 @@ int t8b_sim_reset_done(t8b_sim* sim, uint64_t seed, uint64_t counter) {
     });
 }
 
-int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter) {
+namespace t8b {
+static int step_launch(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter,
+                bool reset) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
         if (s.step_tickets.size() == 0) s.step_tickets.allocate(2);
         s.step_tickets.zero(s.stream);
         const StepGrid g = step_grid(s.n, s.p1_fights, s.sm_count);
         launch("k_step", k_step, g.blocks, g.threads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter,
-               s.step_tickets.data(), s.p1_fights);
+               s.step_tickets.data(), s.p1_fights, reset ? 1 : 0);
         s.launched("step");
         s.masks(nullptr);
     });
+}
+}  // namespace t8b
+
+int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter) {
+    return t8b::step_launch(sim, learner, opponent, seed, counter, false);
+}
+
+int t8b_sim_step_and_reset(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed,
+                           uint64_t counter) {
+    return t8b::step_launch(sim, learner, opponent, seed, counter, true);
 }
 
 const float* t8b_sim_learner_observations(const t8b_sim* sim) { return sim ? sim->learner_obs.data() : nullptr; }

@@ -9,6 +9,8 @@
 // decision itself, the simulator step, and the reset of finished rounds. After the last
 // decision one deterministic forward (seed + 3) gives the final bootstrap. With a frozen
 // opponent policy its forward (seed + 2) runs on a second stream that overlaps the learner's.
+// Every decision but the last steps and resets in one call (t8b_sim_step_and_reset): nothing
+// reads the terminal observations there, while the last decision's bootstrap forward does.
 #include "common.cuh"
 
 extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout* rollout, t8b_policy* opponent,
@@ -66,13 +68,15 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
             ok(t8b_rollout_record_policy_device(rollout, step, obs, nullptr, bits, out.actions, out.log_probabilities,
                                                 out.values, stream, tables, out.entropies));
             if (opponent) check(cudaStreamWaitEvent(main, opponent_done, 0), "wait");
-            ok(t8b_sim_step(sim, out.actions, opponent_actions, seed, counter + 1));
-            if (step + 1 == horizon) {
-                ok(t8b_policy_forward(policy, t8b_sim_learner_observations(sim), nullptr, t8b_sim_learner_mask_bits(sim),
-                                      n, seed + 3, counter, 1, stream, tables, 0, &last));
-                ok(t8b_rollout_record_outcome_device(rollout, step, t8b_sim_rewards(sim), t8b_sim_terminated(sim),
-                                                     t8b_sim_truncated(sim), last.values, reward_scale, stream));
+            if (step + 1 < horizon) {
+                ok(t8b_sim_step_and_reset(sim, out.actions, opponent_actions, seed, counter + 1));
+                continue;
             }
+            ok(t8b_sim_step(sim, out.actions, opponent_actions, seed, counter + 1));
+            ok(t8b_policy_forward(policy, t8b_sim_learner_observations(sim), nullptr, t8b_sim_learner_mask_bits(sim), n,
+                                  seed + 3, counter, 1, stream, tables, 0, &last));
+            ok(t8b_rollout_record_outcome_device(rollout, step, t8b_sim_rewards(sim), t8b_sim_terminated(sim),
+                                                 t8b_sim_truncated(sim), last.values, reward_scale, stream));
             ok(t8b_sim_reset_done(sim, seed, counter + 1));
         }
         if (opponent) check(cudaStreamSynchronize(side), "opponent stream");

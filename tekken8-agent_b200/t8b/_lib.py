@@ -181,6 +181,7 @@ PROTOTYPES = {
     "t8b_sim_reset_all": (C.c_int, [vp, u64, u64]),
     "t8b_sim_reset_done": (C.c_int, [vp, u64, u64]),
     "t8b_sim_step": (C.c_int, [vp, vp, vp, u64, u64]),
+    "t8b_sim_step_and_reset": (C.c_int, [vp, vp, vp, u64, u64]),
     "t8b_sim_learner_observations": (vp, [vp]),
     "t8b_sim_opponent_observations": (vp, [vp]),
     "t8b_sim_learner_masks": (vp, [vp]),

@@ -153,6 +153,14 @@ class GpuFullMoveSimulator:
         call("t8b_sim_step", self._handle, ptr(learner_candidates),
              ptr(opponent_candidates) if opponent_candidates is not None else None, seed, counter)
 
+    def step_and_reset(self, learner_candidates: torch.Tensor, opponent_candidates: torch.Tensor | None, seed: int,
+                       counter: int):
+        """step then reset_done with the same seed and counter; finished fights' terminal
+        observations are never written."""
+        assert learner_candidates.dtype == torch.int64
+        call("t8b_sim_step_and_reset", self._handle, ptr(learner_candidates),
+             ptr(opponent_candidates) if opponent_candidates is not None else None, seed, counter)
+
     def _view(self, name, shape, dtype):
         return view(getattr(_lib.lib(), name)(self._handle), shape, dtype, self.device)
 

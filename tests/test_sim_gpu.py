@@ -182,6 +182,65 @@ def test_env_matches_reference_contract(cuda, roster, ref_roster, noise, screen,
     assert sim.frames_simulated() == cpu.read()["frames"]
 
 
+@pytest.mark.parametrize("noise,screen,self_play,memory", [(1, 1, False, 0), (1, 0, True, 1)])
+def test_step_and_reset_equals_step_then_reset_done(cuda, roster, ref_roster, noise, screen, self_play, memory):
+    """t8b_sim_step_and_reset against t8b_sim_step + t8b_sim_reset_done on a second simulator and
+    against the reference contract's step + reset_done: after every call the states, matchups,
+    noise levels, rewards, terminations, outcomes, both sides' observations and masks, and at
+    the end the tallies and frame counts are identical. Short rounds and pending learners make
+    the in-step reset run on many fights."""
+    import torch
+    from oracle import ref
+    from t8b.sim import GpuFullMoveSimulator
+    n, steps, seed = 256, 120, 17
+    config = env_config(live_noise=noise, screen_view=screen, perception_delay=12 if noise else 0, memory=memory,
+                        max_round_frames=300)
+    p1, p2, sides, opponents, aggression, scenarios = make_golden.env_case(n)
+    learners = np.where(np.arange(n) % 3 == 0, (np.arange(n) * 7) % 41, -1).astype(np.int32)
+    sims = []
+    for _ in range(2):
+        sim = GpuFullMoveSimulator(roster, n, config)
+        sim.set_matchups(p1, p2)
+        sim.set_learner_sides(sides)
+        sim.set_pending_opponents(opponents, aggression, scenarios)
+        sim.set_pending_learners(learners)
+        sim.reset_all(seed, 0)
+        sims.append(sim)
+    fused, split = sims
+    cpu = ref.RefEnv(ref_roster, n, config, threads=16)
+    cpu.setup(p1=p1, p2=p2, learner_is_p1=sides, opponents=opponents, aggression=aggression, scenarios=scenarios,
+              learners=learners)
+    cpu.reset_all(seed, 0)
+    rng = np.random.default_rng(8)
+    terminations = 0
+    for step in range(1, steps + 1):
+        a = gpu_read(fused)
+        act = np.array([np.nonzero(m)[0][rng.integers(m.sum())] for m in a["learner_masks"]], np.int64)
+        opp = None
+        if self_play:
+            opp = np.array([np.nonzero(m)[0][rng.integers(m.sum())] for m in a["opponent_masks"]], np.int64)
+        la = torch.as_tensor(act, device="cuda")
+        oa = None if opp is None else torch.as_tensor(opp, device="cuda")
+        fused.step_and_reset(la, oa, seed, step)
+        split.step(la, oa, seed, step)
+        split.reset_done(seed, step)
+        cpu.step(act, opp, seed, step)
+        cpu.reset_done(seed, step)
+        a, b, c = gpu_read(fused), gpu_read(split), cpu.read()
+        for key in ("rewards", "terminated", "outcomes", "states", "learner_obs", "opponent_obs", "learner_masks",
+                    "opponent_masks"):
+            assert np.array_equal(a[key].view(np.uint8), b[key].view(np.uint8)), (key, step, first_mismatch(a[key], b[key]))
+            assert np.array_equal(a[key].view(np.uint8), c[key].view(np.uint8)), (key, step, first_mismatch(a[key], c[key]))
+        if noise:
+            assert bytes(fused.download_noise_levels()) == bytes(split.download_noise_levels())
+        assert np.array_equal(fused.learner_feature_tables().cpu().numpy(), split.learner_feature_tables().cpu().numpy())
+        terminations += int(a["terminated"].sum())
+    assert terminations > 100
+    assert fused.frames_simulated() == split.frames_simulated() == cpu.read()["frames"]
+    for x, y in zip(fused.download_and_clear_tally(), split.download_and_clear_tally()):
+        assert np.array_equal(x, y)
+
+
 def test_engine_legal_mask_and_tallies(cuda, roster, ref_roster):
     import torch
     from t8b.sim import GpuFullMoveSimulator
