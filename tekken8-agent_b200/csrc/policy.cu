@@ -513,6 +513,10 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
               "objective shared memory");
         check(cudaFuncSetAttribute(ppo::k_loss<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kMaxTableBytes),
               "objective shared memory");
+        check(cudaFuncSetAttribute(ppo::k_sample<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(ppo::sample_smem(32))), "sampler shared memory");
+        check(cudaFuncSetAttribute(ppo::k_sample<48>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   static_cast<int>(ppo::sample_smem(48))), "sampler shared memory");
         const size_t sms = static_cast<size_t>(sm_count());
         const size_t part = std::max({sms * p->hidden * kOutPad, sms * static_cast<size_t>(p->hidden) * p->hidden,
                                       sms * static_cast<size_t>(p->hidden) * p->padded});
@@ -637,10 +641,16 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         smp.log_probs = s.log_probs.data();
         smp.values = s.values.data();
         smp.entropies = s.entropies.data();
+        // one group per feature table (plus one for out-of-range table indices), about 64 samples
+        // per block
+        const size_t groups = tables ? static_cast<size_t>(s.tables) + 1 : 1;
+        smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>((n + groups * 64 - 1) / (groups * 64), 1), 4096));
+        const unsigned sample_grid = static_cast<unsigned>(groups * smp.parts);
+        const size_t sample_bytes = ppo::sample_smem(s.feature_size);
         if (s.feature_size == 48) {
-            launch("k_sample", ppo::k_sample<48>, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
+            launch("k_sample", ppo::k_sample<48>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
         } else {
-            launch("k_sample", ppo::k_sample<32>, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, smp);
+            launch("k_sample", ppo::k_sample<32>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
         }
         check(cudaGetLastError(), "sample actions");
         if (out) {

@@ -362,6 +362,7 @@ struct Sample {
     size_t count;
     uint64_t seed, step, lane_offset;
     int deterministic;
+    unsigned parts;  // blocks per table group (k_sample's grid is groups x parts)
     float* logits;  // [n][368] or null
     int64_t* actions;
     float* log_probs;
@@ -382,19 +383,14 @@ __device__ __forceinline__ uint32_t mask_word(const uint32_t* bits, const uint8_
 constexpr int kFeatures = 32;
 constexpr int kMaxFeatures = 48;
 
-// q . F[a] in feature order, then scaled (src/ppo.cu:340-346).
+// q . F[a] in feature order, then scaled (src/ppo.cu:340-346), with the table staged in shared
+// memory transposed ([feature][candidate]: lanes scoring consecutive candidates read
+// consecutive words).
 template <int F>
-__device__ __forceinline__ float score_of(const float* q, const float* frow, float scale) {
-    const float4* f4 = reinterpret_cast<const float4*>(frow);
+__device__ __forceinline__ float score_staged(const float* q, const float* ft, int c, float scale) {
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < F / 4; ++k) {
-        const float4 f = __ldg(f4 + k);
-        s += q[4 * k] * f.x;
-        s += q[4 * k + 1] * f.y;
-        s += q[4 * k + 2] * f.z;
-        s += q[4 * k + 3] * f.w;
-    }
+    for (int k = 0; k < F; ++k) s += q[k] * ft[k * kCandidates + c];
     return s * scale;
 }
 
@@ -443,22 +439,26 @@ __device__ __forceinline__ int legal_rank(const uint32_t* words, bool any, int c
     return rank + __popc(words[(c >> 5) % kMaskWords] & ((1u << (c & 31)) - 1u));
 }
 
+// k_sample's shape: 16 warps per block; a block gathers up to kSampleFound of its samples before
+// scoring them, checking kSampleUnroll table indices per thread per gathering round.
+constexpr int kSampleWarps = 16;
+constexpr int kSampleFound = 4096;
+constexpr int kSampleUnroll = 4;
+
+// Dynamic shared memory of k_sample: the block's feature table, then the gathered sample indices.
+inline size_t sample_smem(int features) {
+    return static_cast<size_t>(features) * kCandidates * sizeof(float) + kSampleFound * sizeof(uint32_t);
+}
+
+// One sample, one warp: the scores of the legal candidates, the masked softmax, the
+// inverse-CDF draw (argmax when deterministic), log-probability, value and entropy.
 template <int F>
-__global__ void k_sample(Sample p) {
-    __shared__ float qs[kWarps][64];
-    __shared__ int16_t lists[kWarps][kCandidates];
-    __shared__ float scores[kWarps][kCandidates];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t i = static_cast<size_t>(blockIdx.x) * kWarps + warp;
-    if (i >= p.count) return;
+__device__ __forceinline__ void sample_one(const Sample& p, size_t i, int lane, float* q, int16_t* list, float* sc,
+                                           const float* ft, bool bad_table) {
     const float* o = p.out + i * p.ld;
-    for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
+    for (int f = lane; f <= p.feature_size; f += 32) q[f] = o[f];
     __syncwarp();
-    const float* q = qs[warp];
     const float scale = rsqrtf(static_cast<float>(p.feature_size));
-    const int table = p.tables ? p.tables[i] : 0;
-    const bool bad_table = table < 0 || table >= p.table_count;
-    const float* ftab = p.features + static_cast<size_t>(bad_table ? 0 : table) * p.action_count * F;
     uint32_t words[kMaskWords];
     bool any = false;
 #pragma unroll
@@ -469,17 +469,15 @@ __global__ void k_sample(Sample p) {
     if (p.logits) {
         for (int c = lane; c < p.action_count; c += 32) {
             p.logits[i * p.action_count + c] =
-                bad_table ? __int_as_float(0x7fc00000) : score_of<F>(q, ftab + c * F, scale);
+                bad_table ? __int_as_float(0x7fc00000) : score_staged<F>(q, ft, c, scale);
         }
     }
-    int16_t* list = lists[warp];
-    float* sc = scores[warp];
     const int count = compact_legal(words, any, lane, list);
     // scores of the legal candidates; argmax = largest score, then the lowest candidate
     float best = -3.402823466e38f;
     int best_j = kCandidates;
     for (int j = lane; j < count; j += 32) {
-        const float s = bad_table ? __int_as_float(0x7fc00000) : score_of<F>(q, ftab + list[j] * F, scale);
+        const float s = bad_table ? __int_as_float(0x7fc00000) : score_staged<F>(q, ft, list[j], scale);
         sc[j] = s;
         if (s > best || best_j == kCandidates) {
             best = s;
@@ -533,6 +531,70 @@ __global__ void k_sample(Sample p) {
         p.log_probs[i] = sc[selected_j] - log_sum;
         p.values[i] = bad_table ? __int_as_float(0x7fc00000) : q[p.feature_size];
         p.entropies[i] = entropy;
+    }
+    __syncwarp();
+}
+
+// The forward's sampler (src/ppo.cu:238-300), one warp per sample. Each block owns one feature
+// table (p.parts blocks per table, sample i going to part i % p.parts; with tables given, one
+// more group takes the samples whose table index is out of range and gives them NaN scores):
+// it stages the table in shared memory once and gathers its samples by scanning the table
+// indices, so scoring reads shared memory instead of streaming every sample's feature rows
+// from L2.
+template <int F>
+__global__ void __launch_bounds__(32 * kSampleWarps) k_sample(Sample p) {
+    extern __shared__ __align__(16) unsigned char dynamic_smem[];
+    float* ft = reinterpret_cast<float*>(dynamic_smem);
+    uint32_t* found = reinterpret_cast<uint32_t*>(ft + F * kCandidates);
+    __shared__ float qs[kSampleWarps][64];
+    __shared__ int16_t lists[kSampleWarps][kCandidates];
+    __shared__ float scores[kSampleWarps][kCandidates];
+    __shared__ unsigned found_count;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int group = static_cast<int>(blockIdx.x / p.parts);
+    const size_t part = blockIdx.x % p.parts;
+    const bool bad_group = p.tables != nullptr && group == p.table_count;
+    if (!bad_group) {
+        const float* src = p.features + static_cast<size_t>(group) * p.action_count * F;
+        for (int idx = threadIdx.x; idx < p.action_count * F; idx += blockDim.x) {
+            ft[(idx % F) * kCandidates + idx / F] = src[idx];
+        }
+    }
+    if (threadIdx.x == 0) found_count = 0;
+    __syncthreads();
+    // this part's samples are i = part + t * parts, t < per_part
+    const size_t per_part = p.count > part ? (p.count - part + p.parts - 1) / p.parts : 0;
+    const size_t round = static_cast<size_t>(blockDim.x) * kSampleUnroll;
+    size_t t0 = 0;
+    for (;;) {
+        while (t0 < per_part && found_count + round <= kSampleFound) {
+            size_t index[kSampleUnroll];
+            int key[kSampleUnroll];
+#pragma unroll
+            for (int u = 0; u < kSampleUnroll; ++u) {
+                const size_t t = t0 + threadIdx.x + static_cast<size_t>(u) * blockDim.x;
+                index[u] = part + t * p.parts;
+                key[u] = -1;
+                if (t < per_part) {
+                    const int table = p.tables ? p.tables[index[u]] : 0;
+                    key[u] = p.tables && (table < 0 || table >= p.table_count) ? p.table_count : table;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kSampleUnroll; ++u) {
+                if (key[u] == group) found[atomicAdd(&found_count, 1u)] = static_cast<uint32_t>(index[u]);
+            }
+            t0 += round;
+            __syncthreads();
+        }
+        const unsigned count = found_count;
+        for (unsigned j = warp; j < count; j += kSampleWarps) {
+            sample_one<F>(p, found[j], lane, qs[warp], lists[warp], scores[warp], ft, bad_group);
+        }
+        __syncthreads();
+        if (t0 >= per_part) break;
+        if (threadIdx.x == 0) found_count = 0;
+        __syncthreads();
     }
 }
 
