@@ -51,11 +51,18 @@ T8B_HD bool to_input(const DCharacter& ch, int candidate, Input& in) {
     return true;
 }
 
-// candidate_legal (full_move_contract.hpp:42-49)
+// candidate_legal (full_move_contract.hpp:42-49). A move candidate's legality reads its gate
+// record (the same fields input_ok reads of the move; candidates name existing moves).
 T8B_HD bool candidate_ok(const Match& m, const Fight& s, int p, int candidate) {
     if (candidate == 0) return true;
+    const DCharacter& ch = *m.side[p];
+    if (candidate >= kUniversalCount && candidate < ch.candidate_count) {
+        const DGate g = ch.gates[candidate];
+        if (g.move < 0 || s.winner >= 0) return false;
+        return move_allowed(m, s, p, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
+    }
     Input in{-1, kIdle};
-    if (!to_input(*m.side[p], candidate, in)) return false;
+    if (!to_input(ch, candidate, in)) return false;
     if (candidate == 6 && s.f[p].posture != kCrouching) return false;
     return input_ok(m, s, p, in);
 }

@@ -126,6 +126,17 @@ struct DFacts {
     uint32_t bits;  // 1 valid, 2 safe, 4 launcher, 8 low, 16 throw
 };
 
+// What legal's move branch reads of a move candidate's move (flags, required posture, stance
+// and heat cost), per candidate: one 16-byte record instead of three 32-byte sectors of the
+// move record behind the candidate's move index. move is -1 for candidates without a move.
+struct alignas(16) DGate {
+    uint64_t flags;
+    int32_t required_stance;
+    uint8_t required_posture;
+    uint8_t heat_cost;  // heat_cost_frames != 0
+    int16_t move;
+};
+
 // One roster character on the device.
 struct DCharacter {
     const DMove* moves;
@@ -134,6 +145,7 @@ struct DCharacter {
     const int2* spans;
     const int32_t* candidate_moves;
     const DFacts* facts;
+    const DGate* gates;  // [candidate_count]
     int32_t move_count, stance_count, candidate_count, roster_id;
     DRules rules;
 };
@@ -349,6 +361,43 @@ T8B_HD bool can_act(const Match& m, const Fight& s, int p) {
     return f.action_frame >= action_length(f.universal, *m.cfg);
 }
 
+// The move branch of legal (full_combat_core.hpp:380-441) for a move with these flags,
+// required posture and stance, and heat cost; the round is still running.
+T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, uint8_t required_posture,
+                         int32_t required_stance, bool heat_cost) {
+    const Fighter& f = s.f[p];
+    const Cfg& c = *m.cfg;
+    const auto need = [flags](uint64_t bit) { return (flags & bit) != 0ull; };
+    if (need(kReactive)) return false;
+    if (need(kRequiresSidestep)) {
+        const bool stepping = f.move < 0 && f.action_frame >= 1 && f.stun == 0 && !on(f, fCrumpled) &&
+            f.break_frames == 0 && f.pending_throw_hit < 0 &&
+            (f.universal == kSidestepLeft || f.universal == kSidestepRight);
+        if (!stepping) return false;
+    } else if (!can_act(m, s, p)) {
+        return false;
+    }
+    const Fighter& o = s.f[1 - p];
+    if (need(kRequiresBackTurned) != on(f, fBackTurned)) return false;
+    if (need(kRequiresOpponentBackTurned) && !on(o, fBackTurned)) return false;
+    if (need(kRequiresBackToWall)) {
+        const double wall = o.x >= f.x ? s.left_wall : s.right_wall;
+        if (mag(f.x - wall) > c.back_to_wall_distance) return false;
+    }
+    if (need(kRequiresOpponentLeft) || need(kRequiresOpponentRight)) {
+        const double toward = f.x >= o.x ? 1.0 : -1.0;
+        const double gap = hi(mag(f.x - o.x), 1e-9);
+        const double side = (f.axis - o.axis) * toward / gap;
+        if (need(kRequiresOpponentLeft) && side > -c.side_exposure_ratio) return false;
+        if (need(kRequiresOpponentRight) && side < c.side_exposure_ratio) return false;
+    }
+    const bool heat = on(f, fHeat);
+    return required_posture == f.posture && (required_stance < 0 || required_stance == f.stance) &&
+        (!need(kRequiresHeat) || heat) && (!need(kConsumesHeat) || heat) && (!heat_cost || heat) &&
+        (!need(kEngagesHeat) || (on(f, fHeatAvailable) && !heat)) &&
+        (!(need(kRequiresRage) || need(kConsumesRage)) || on(f, fRage));
+}
+
 // legal (full_combat_core.hpp:380-441)
 T8B_HD bool input_ok(const Match& m, const Fight& s, int p, const Input& in) {
     if (s.winner >= 0) return false;
@@ -357,34 +406,7 @@ T8B_HD bool input_ok(const Match& m, const Fight& s, int p, const Input& in) {
     if (in.move >= 0) {
         if (in.move >= m.side[p]->move_count) return false;
         const DMove& mv = move_at(m, p, in.move);
-        if (has(mv, kReactive)) return false;
-        if (has(mv, kRequiresSidestep)) {
-            const bool stepping = f.move < 0 && f.action_frame >= 1 && f.stun == 0 && !on(f, fCrumpled) &&
-                f.break_frames == 0 && f.pending_throw_hit < 0 &&
-                (f.universal == kSidestepLeft || f.universal == kSidestepRight);
-            if (!stepping) return false;
-        } else if (!can_act(m, s, p)) {
-            return false;
-        }
-        const Fighter& o = s.f[1 - p];
-        if (has(mv, kRequiresBackTurned) != on(f, fBackTurned)) return false;
-        if (has(mv, kRequiresOpponentBackTurned) && !on(o, fBackTurned)) return false;
-        if (has(mv, kRequiresBackToWall)) {
-            const double wall = o.x >= f.x ? s.left_wall : s.right_wall;
-            if (mag(f.x - wall) > c.back_to_wall_distance) return false;
-        }
-        if (has(mv, kRequiresOpponentLeft) || has(mv, kRequiresOpponentRight)) {
-            const double toward = f.x >= o.x ? 1.0 : -1.0;
-            const double gap = hi(mag(f.x - o.x), 1e-9);
-            const double side = (f.axis - o.axis) * toward / gap;
-            if (has(mv, kRequiresOpponentLeft) && side > -c.side_exposure_ratio) return false;
-            if (has(mv, kRequiresOpponentRight) && side < c.side_exposure_ratio) return false;
-        }
-        const bool heat = on(f, fHeat);
-        return mv.required_posture == f.posture && (mv.required_stance < 0 || mv.required_stance == f.stance) &&
-            (!has(mv, kRequiresHeat) || heat) && (!has(mv, kConsumesHeat) || heat) &&
-            (mv.heat_cost_frames == 0 || heat) && (!has(mv, kEngagesHeat) || (on(f, fHeatAvailable) && !heat)) &&
-            (!(has(mv, kRequiresRage) || has(mv, kConsumesRage)) || on(f, fRage));
+        return move_allowed(m, s, p, mv.flags, mv.required_posture, mv.required_stance, mv.heat_cost_frames != 0);
     }
     switch (in.universal) {
         case kWakeupStand:

@@ -637,6 +637,7 @@ struct HostRoster {
     std::vector<int2> spans;
     std::vector<int32_t> candidate_moves;
     std::vector<DFacts> facts;
+    std::vector<DGate> gates;
     struct Offsets { size_t move, hit, stance, candidate; };
     std::vector<Offsets> offsets;
     std::vector<int32_t> roster_ids;
@@ -707,6 +708,23 @@ DFacts candidate_facts(const t8b_character_t& ch, int candidate) {
     return out;
 }
 
+// The legality inputs of a move candidate (DGate); universal candidates and gaps get move -1.
+DGate candidate_gate(const t8b_character_t& ch, int candidate) {
+    DGate g;
+    std::memset(&g, 0, sizeof g);
+    g.move = -1;
+    const int move = candidate >= kUniversalCount ? ch.candidate_moves[candidate] : -1;
+    if (move < 0) return g;
+    if (move > 32767) raise(T8B_EINVAL, "a candidate's move index exceeds 32767");
+    const t8b_move_t& m = ch.moves[move];
+    g.flags = m.flags;
+    g.required_stance = m.required_stance;
+    g.required_posture = m.required_posture;
+    g.heat_cost = m.heat_cost_frames != 0 ? 1 : 0;
+    g.move = static_cast<int16_t>(move);
+    return g;
+}
+
 // Repacks the boundary tables into the device layout (host vectors; the caller uploads).
 HostRoster pack_roster(const t8b_character_t* roster, int roster_count) {
     HostRoster host;
@@ -745,6 +763,7 @@ HostRoster pack_roster(const t8b_character_t* roster, int roster_count) {
             if (ch.candidate_moves[k] >= ch.move_count) raise(T8B_EINVAL, "a candidate names a missing move");
             host.candidate_moves.push_back(ch.candidate_moves[k]);
             host.facts.push_back(candidate_facts(ch, k));
+            host.gates.push_back(candidate_gate(ch, k));
         }
         host.roster_ids.push_back(ch.roster_id);
     }
@@ -767,6 +786,7 @@ struct t8b_sim {
     Buffer<int2> spans;
     Buffer<int32_t> candidate_moves;
     Buffer<DFacts> facts;
+    Buffer<DGate> gates;
     Buffer<DCharacter> chars;
     Buffer<Cfg> cfg;
     Buffer<EnvCfg> ecfg;
@@ -932,6 +952,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         if (host.stances.empty()) host.stances.push_back(DStance{});
         if (host.candidate_moves.empty()) host.candidate_moves.push_back(-1);
         if (host.facts.empty()) host.facts.push_back(DFacts{});
+        if (host.gates.empty()) host.gates.push_back(DGate{});
         cudaStream_t s = sim->stream;
         sim->moves.allocate(host.moves.size()); sim->moves.upload(host.moves.data(), host.moves.size(), s);
         sim->hits.allocate(host.hits.size()); sim->hits.upload(host.hits.data(), host.hits.size(), s);
@@ -940,6 +961,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
         sim->candidate_moves.allocate(host.candidate_moves.size());
         sim->candidate_moves.upload(host.candidate_moves.data(), host.candidate_moves.size(), s);
         sim->facts.allocate(host.facts.size()); sim->facts.upload(host.facts.data(), host.facts.size(), s);
+        sim->gates.allocate(host.gates.size()); sim->gates.upload(host.gates.data(), host.gates.size(), s);
         std::vector<DCharacter> chars;
         for (int c = 0; c < roster_count; ++c) {
             const auto& off = host.offsets[static_cast<size_t>(c)];
@@ -950,6 +972,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
             d.spans = sim->spans.data();
             d.candidate_moves = sim->candidate_moves.data() + off.candidate;
             d.facts = sim->facts.data() + off.candidate;
+            d.gates = sim->gates.data() + off.candidate;
             d.move_count = roster[c].move_count;
             d.stance_count = roster[c].stance_count;
             d.candidate_count = roster[c].candidate_count;
