@@ -370,27 +370,36 @@ struct Sample {
     float* entropies;
 };
 
-__device__ __forceinline__ uint32_t mask_word(const uint32_t* bits, const uint8_t* bytes, size_t i, int word, int lane,
-                                              int actions) {
-    if (bits) return bits[i * kMaskWords + word];
-    const int c = word * 32 + lane;
-    const bool legal = c < actions && bytes[i * actions + c] != 0;
-    return __ballot_sync(0xffffffffu, legal);
-}
-
 // Feature sizes the scorer kernels are built for: the full-move tables' 32
 // (kFullMoveFeatureSize, include/t8_v2/full_move_roster.hpp:21) and 48.
 constexpr int kFeatures = 32;
 constexpr int kMaxFeatures = 48;
+constexpr int kMaxTableBytes = kCandidates * kMaxFeatures * 4;
 
-// q . F[a] in feature order, then scaled (src/ppo.cu:340-346), with the table staged in shared
-// memory transposed ([feature][candidate]: lanes scoring consecutive candidates read
-// consecutive words).
+// Chunk k (4 floats) of candidate c's feature row in the staged table: chunks are rotated by
+// the row (an xor for 8 chunks, a cyclic shift otherwise) so that lanes reading different rows
+// at the same chunk spread over the banks.
 template <int F>
-__device__ __forceinline__ float score_staged(const float* q, const float* ft, int c, float scale) {
+__device__ __forceinline__ int staged_slot(int c, int k) {
+    constexpr int chunks = F / 4;
+    return c * chunks + (chunks == 8 ? (k ^ (c & 7)) : (k + c) % chunks);
+}
+template <int F>
+__device__ __forceinline__ float4 staged_chunk(const float4* table, int c, int k) {
+    return table[staged_slot<F>(c, k)];
+}
+// q . F[a] in feature order, then scaled (src/ppo.cu:340-346).
+template <int F>
+__device__ __forceinline__ float staged_score(const float* q, const float4* table, int c, float scale) {
     float s = 0.0f;
 #pragma unroll
-    for (int k = 0; k < F; ++k) s += q[k] * ft[k * kCandidates + c];
+    for (int k = 0; k < F / 4; ++k) {
+        const float4 f = staged_chunk<F>(table, c, k);
+        s += q[4 * k] * f.x;
+        s += q[4 * k + 1] * f.y;
+        s += q[4 * k + 2] * f.z;
+        s += q[4 * k + 3] * f.w;
+    }
     return s * scale;
 }
 
@@ -450,26 +459,49 @@ inline size_t sample_smem(int features) {
     return static_cast<size_t>(features) * kCandidates * sizeof(float) + kSampleFound * sizeof(uint32_t);
 }
 
+// One sample's global inputs, loaded a sample ahead: lane w < 12 holds packed mask word w
+// (bits) or each lane its candidate's mask byte per word (bytes), and the output row's q and
+// value (lane f: elements f and 32 + f).
+struct SampleInputs {
+    uint32_t raw[kMaskWords];
+    float q_lo, q_hi;
+};
+
+__device__ __forceinline__ void load_sample(const Sample& p, size_t i, int lane, SampleInputs& in) {
+    const float* o = p.out + i * p.ld;
+    in.q_lo = lane <= p.feature_size ? o[lane] : 0.0f;
+    in.q_hi = lane + 32 <= p.feature_size ? o[lane + 32] : 0.0f;
+    if (p.bits) {
+        in.raw[0] = lane < kMaskWords ? p.bits[i * kMaskWords + lane] : 0u;
+    } else {
+#pragma unroll
+        for (int w = 0; w < kMaskWords; ++w) {
+            const int c = w * 32 + lane;
+            in.raw[w] = c < p.action_count ? p.bytes[i * p.action_count + c] : 0u;
+        }
+    }
+}
+
 // One sample, one warp: the scores of the legal candidates, the masked softmax, the
 // inverse-CDF draw (argmax when deterministic), log-probability, value and entropy.
 template <int F>
-__device__ __forceinline__ void sample_one(const Sample& p, size_t i, int lane, float* q, int16_t* list, float* sc,
-                                           const float* ft, bool bad_table) {
-    const float* o = p.out + i * p.ld;
-    for (int f = lane; f <= p.feature_size; f += 32) q[f] = o[f];
+__device__ __forceinline__ void sample_one(const Sample& p, size_t i, int lane, const SampleInputs& in, float* q,
+                                           int16_t* list, float* sc, const float4* table, bool bad_table) {
+    q[lane] = in.q_lo;
+    if (lane + 32 <= p.feature_size) q[lane + 32] = in.q_hi;
     __syncwarp();
     const float scale = rsqrtf(static_cast<float>(p.feature_size));
     uint32_t words[kMaskWords];
     bool any = false;
 #pragma unroll
     for (int w = 0; w < kMaskWords; ++w) {
-        words[w] = mask_word(p.bits, p.bytes, i, w, lane, p.action_count);
+        words[w] = p.bits ? __shfl_sync(0xffffffffu, in.raw[0], w) : __ballot_sync(0xffffffffu, in.raw[w] != 0u);
         any = any || words[w] != 0;
     }
     if (p.logits) {
         for (int c = lane; c < p.action_count; c += 32) {
             p.logits[i * p.action_count + c] =
-                bad_table ? __int_as_float(0x7fc00000) : score_staged<F>(q, ft, c, scale);
+                bad_table ? __int_as_float(0x7fc00000) : staged_score<F>(q, table, c, scale);
         }
     }
     const int count = compact_legal(words, any, lane, list);
@@ -477,7 +509,7 @@ __device__ __forceinline__ void sample_one(const Sample& p, size_t i, int lane, 
     float best = -3.402823466e38f;
     int best_j = kCandidates;
     for (int j = lane; j < count; j += 32) {
-        const float s = bad_table ? __int_as_float(0x7fc00000) : score_staged<F>(q, ft, list[j], scale);
+        const float s = bad_table ? __int_as_float(0x7fc00000) : staged_score<F>(q, table, list[j], scale);
         sc[j] = s;
         if (s > best || best_j == kCandidates) {
             best = s;
@@ -538,14 +570,15 @@ __device__ __forceinline__ void sample_one(const Sample& p, size_t i, int lane, 
 // The forward's sampler (src/ppo.cu:238-300), one warp per sample. Each block owns one feature
 // table (p.parts blocks per table, sample i going to part i % p.parts; with tables given, one
 // more group takes the samples whose table index is out of range and gives them NaN scores):
-// it stages the table in shared memory once and gathers its samples by scanning the table
-// indices, so scoring reads shared memory instead of streaming every sample's feature rows
-// from L2.
+// it stages the table in shared memory once (staged_slot layout) and gathers its samples by
+// scanning the table indices, so scoring reads shared memory instead of streaming every
+// sample's feature rows from L2. A warp loads its next sample's inputs while it scores the
+// current one.
 template <int F>
 __global__ void __launch_bounds__(32 * kSampleWarps) k_sample(Sample p) {
     extern __shared__ __align__(16) unsigned char dynamic_smem[];
-    float* ft = reinterpret_cast<float*>(dynamic_smem);
-    uint32_t* found = reinterpret_cast<uint32_t*>(ft + F * kCandidates);
+    float4* table = reinterpret_cast<float4*>(dynamic_smem);
+    uint32_t* found = reinterpret_cast<uint32_t*>(table + kCandidates * (F / 4));
     __shared__ float qs[kSampleWarps][64];
     __shared__ int16_t lists[kSampleWarps][kCandidates];
     __shared__ float scores[kSampleWarps][kCandidates];
@@ -555,9 +588,9 @@ __global__ void __launch_bounds__(32 * kSampleWarps) k_sample(Sample p) {
     const size_t part = blockIdx.x % p.parts;
     const bool bad_group = p.tables != nullptr && group == p.table_count;
     if (!bad_group) {
-        const float* src = p.features + static_cast<size_t>(group) * p.action_count * F;
-        for (int idx = threadIdx.x; idx < p.action_count * F; idx += blockDim.x) {
-            ft[(idx % F) * kCandidates + idx / F] = src[idx];
+        const float4* src = reinterpret_cast<const float4*>(p.features + static_cast<size_t>(group) * p.action_count * F);
+        for (int idx = threadIdx.x; idx < p.action_count * (F / 4); idx += blockDim.x) {
+            table[staged_slot<F>(idx / (F / 4), idx % (F / 4))] = __ldg(src + idx);
         }
     }
     if (threadIdx.x == 0) found_count = 0;
@@ -576,8 +609,8 @@ __global__ void __launch_bounds__(32 * kSampleWarps) k_sample(Sample p) {
                 index[u] = part + t * p.parts;
                 key[u] = -1;
                 if (t < per_part) {
-                    const int table = p.tables ? p.tables[index[u]] : 0;
-                    key[u] = p.tables && (table < 0 || table >= p.table_count) ? p.table_count : table;
+                    const int table_index = p.tables ? p.tables[index[u]] : 0;
+                    key[u] = p.tables && (table_index < 0 || table_index >= p.table_count) ? p.table_count : table_index;
                 }
             }
 #pragma unroll
@@ -588,8 +621,12 @@ __global__ void __launch_bounds__(32 * kSampleWarps) k_sample(Sample p) {
             __syncthreads();
         }
         const unsigned count = found_count;
+        SampleInputs next;
+        if (static_cast<unsigned>(warp) < count) load_sample(p, found[warp], lane, next);
         for (unsigned j = warp; j < count; j += kSampleWarps) {
-            sample_one<F>(p, found[j], lane, qs[warp], lists[warp], scores[warp], ft, bad_group);
+            const SampleInputs current = next;
+            if (j + kSampleWarps < count) load_sample(p, found[j + kSampleWarps], lane, next);
+            sample_one<F>(p, found[j], lane, current, qs[warp], lists[warp], scores[warp], table, bad_group);
         }
         __syncthreads();
         if (t0 >= per_part) break;
@@ -751,33 +788,6 @@ struct Loss {
 // Rows of one feature table that a k_loss block scores; the block's table sits in shared
 // memory, so each candidate row is read from L2 once per block instead of once per sample.
 constexpr int kLossRows = 256;
-constexpr int kMaxTableBytes = kCandidates * kMaxFeatures * 4;
-
-// Chunk k (4 floats) of candidate c's feature row in the staged table: chunks are rotated by
-// the row (an xor for 8 chunks, a cyclic shift otherwise) so that lanes reading different rows
-// at the same chunk spread over the banks.
-template <int F>
-__device__ __forceinline__ int staged_slot(int c, int k) {
-    constexpr int chunks = F / 4;
-    return c * chunks + (chunks == 8 ? (k ^ (c & 7)) : (k + c) % chunks);
-}
-template <int F>
-__device__ __forceinline__ float4 staged_chunk(const float4* table, int c, int k) {
-    return table[staged_slot<F>(c, k)];
-}
-template <int F>
-__device__ __forceinline__ float staged_score(const float* q, const float4* table, int c, float scale) {
-    float s = 0.0f;
-#pragma unroll
-    for (int k = 0; k < F / 4; ++k) {
-        const float4 f = staged_chunk<F>(table, c, k);
-        s += q[4 * k] * f.x;
-        s += q[4 * k + 1] * f.y;
-        s += q[4 * k + 2] * f.z;
-        s += q[4 * k + 3] * f.w;
-    }
-    return s * scale;
-}
 
 // The minibatch rows are grouped by feature table (k_group_*); block b takes the b-th run of at
 // most kLossRows rows of one table, counted over the tables in order. Blocks past the last run
