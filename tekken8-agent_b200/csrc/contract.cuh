@@ -89,18 +89,21 @@ T8B_HD uint64_t mix64(uint64_t v) {
     v = (v ^ (v >> 27)) * 0x94D049BB133111EBull;
     return v ^ (v >> 31);
 }
-T8B_HD uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t counter) { return mix64(mix64(seed ^ mix64(stream)) ^ counter); }
+// hash3(seed, stream, counter) = draw(prefix_of(seed, stream), counter): a caller making many
+// draws from one (seed, stream) takes the prefix once.
+T8B_HD uint64_t prefix_of(uint64_t seed, uint64_t stream) { return mix64(seed ^ mix64(stream)); }
+T8B_HD uint64_t draw(uint64_t prefix, uint64_t counter) { return mix64(prefix ^ counter); }
+T8B_HD uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t counter) { return draw(prefix_of(seed, stream), counter); }
 T8B_HD int below(uint64_t bits, int bound) { return static_cast<int>(bits % static_cast<uint64_t>(bound)); }
 T8B_HD double unit(uint64_t bits) { return static_cast<double>(bits >> 11) * (1.0 / 9007199254740992.0); }
 
 // ------------------------------------------------------------------ scripted opponents
 // scripted_candidate (full_move_contract.hpp:90-119): the legacy random opponent.
-T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggression, uint64_t seed, uint64_t stream,
-                           uint64_t counter) {
+T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggression, uint64_t prefix, uint64_t counter) {
     const DCharacter& ch = *m.side[p];
     const bool close = mag(s.f[p].x - s.f[1 - p].x) < 1.6;
-    uint64_t draw = 0;
-    const int roll = below(hash3(seed, stream, counter * 64u + draw++), 100);
+    uint64_t draw_index = 0;
+    const int roll = below(draw(prefix, counter * 64u + draw_index++), 100);
     if (!close && roll < 55) {
         const int approach = roll < 30 ? 3 : 1;
         if (candidate_ok(m, s, p, approach)) return approach;
@@ -110,14 +113,14 @@ T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggress
         if (candidate_ok(m, s, p, guard)) return guard;
     }
     const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
-    if (ch.candidate_count > kUniversalCount && below(hash3(seed, stream, counter * 64u + draw++), 100) < share) {
+    if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
         for (int k = 0; k < 24; ++k) {
-            const int c = kUniversalCount + below(hash3(seed, stream, counter * 64u + draw++), ch.candidate_count - kUniversalCount);
+            const int c = kUniversalCount + below(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount);
             if (candidate_ok(m, s, p, c)) return c;
         }
     }
     for (int k = 0; k < 24; ++k) {
-        const int c = below(hash3(seed, stream, counter * 64u + draw++), kUniversalCount);
+        const int c = below(draw(prefix, counter * 64u + draw_index++), kUniversalCount);
         if (candidate_ok(m, s, p, c)) return c;
     }
     return 0;
@@ -136,7 +139,7 @@ T8B_HD int bot_id(double behaviour) { return behaviour < 0.0 ? static_cast<int>(
 
 // scripted_bot_candidate (full_move_contract.hpp:319-502)
 T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, uint64_t seed, uint64_t stream,
-                      uint64_t counter) {
+                      uint64_t prefix, uint64_t counter) {
     constexpr int cNeutral = 0, cWalkForward = 1, cWalkBack = 2, cDash = 3, cBackdash = 4, cCrouch = 5;
     constexpr int cStepLeft = 8, cStepRight = 9, cBreak1 = 15, cBreak2 = 16, cBreak12 = 17;
     constexpr int cWakeStand = 19, cWakeRoll = 20, cTechRoll = 21;
@@ -145,10 +148,10 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     const Fighter& own = s.f[p];
     const Fighter& other = s.f[1 - p];
     const double distance = mag(own.x - other.x);
-    uint64_t draw = 0;
+    uint64_t draw_index = 0;
     const uint64_t attack_key = static_cast<uint64_t>(s.frame - other.action_frame) * 4096u +
         static_cast<uint64_t>(other.move + 1);
-#define T8B_ROLL() unit(hash3(seed, stream, counter * 64u + draw++))
+#define T8B_ROLL() unit(draw(prefix, counter * 64u + draw_index++))
 #define T8B_ATTACK_ROLL(purpose) unit(hash3(seed, stream ^ (0x9e3779b97f4a7c15ull * ((purpose) + 1ull)), attack_key))
     const int spread = ihi(1, ch.candidate_count - kUniversalCount);
 
@@ -166,7 +169,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     // getting up
     if (own.posture == kGrounded) {
         const int options[3] = {cWakeStand, cWakeRoll, cTechRoll};
-        const int first = below(hash3(seed, stream, counter * 64u + 63u), 3);
+        const int first = below(draw(prefix, counter * 64u + 63u), 3);
         for (int k = 0; k < 3; ++k) {
             if (candidate_ok(m, s, p, options[(first + k) % 3])) return options[(first + k) % 3];
         }
@@ -211,7 +214,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
             int best = -1;
             double best_score = -1.0;
             for (int k = 0; k < 24; ++k) {
-                const int c = kUniversalCount + below(hash3(seed, stream, counter * 64u + 32u + static_cast<uint64_t>(k)), spread);
+                const int c = kUniversalCount + below(draw(prefix, counter * 64u + 32u + static_cast<uint64_t>(k)), spread);
                 if (c >= ch.candidate_count) continue;
                 const DFacts& fx = ch.facts[c];
                 if (!(fx.bits & 1u) || (fx.bits & 16u) || fx.startup > window || fx.reach + 0.1 < distance) continue;
@@ -239,7 +242,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     // pressure
     if (pr.pressure > 0.0F && on(other, fInBlockstun) && can_act(m, s, p) && T8B_ROLL() < pr.pressure) {
         for (int k = 0; k < 16; ++k) {
-            const int c = kUniversalCount + below(hash3(seed, stream, counter * 64u + 40u + static_cast<uint64_t>(k)), spread);
+            const int c = kUniversalCount + below(draw(prefix, counter * 64u + 40u + static_cast<uint64_t>(k)), spread);
             if (c >= ch.candidate_count) continue;
             const DFacts& fx = ch.facts[c];
             if ((fx.bits & 1u) && !(fx.bits & 16u) && fx.startup <= 14 && fx.reach + 0.05 >= distance &&
@@ -272,7 +275,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
         int best = -1;
         double best_score = -1e9;
         for (int k = 0; k < 12; ++k) {
-            const int c = kUniversalCount + below(hash3(seed, stream, counter * 64u + 8u + static_cast<uint64_t>(k)), spread);
+            const int c = kUniversalCount + below(draw(prefix, counter * 64u + 8u + static_cast<uint64_t>(k)), spread);
             if (c >= ch.candidate_count) continue;
             const DFacts& fx = ch.facts[c];
             if (!(fx.bits & 1u) || !candidate_ok(m, s, p, c)) continue;
@@ -726,6 +729,7 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
     const bool learner_held = is_held(li);
     const bool opponent_held = policy_opponent && is_held(oi);
     const int bot = bot_id(aggression);
+    const uint64_t opponent_prefix = prefix_of(seed, stream);
     Events e;
     int broken = 0;
     double distance_frames = 0.0;
@@ -738,8 +742,8 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
             if (landing || (opponent_held && holding)) other = oi;
         } else if (decides(m, s, op)) {
             const uint64_t at = counter * 256u + static_cast<uint64_t>(frame);
-            const int choice = bot >= 0 ? bot_choice(m, s, op, profiles[bot], seed, stream, at)
-                                        : random_opponent(m, s, op, aggression, seed, stream, at);
+            const int choice = bot >= 0 ? bot_choice(m, s, op, profiles[bot], seed, stream, opponent_prefix, at)
+                                        : random_opponent(m, s, op, aggression, opponent_prefix, at);
             if (!to_input(*m.side[op], choice, other)) other = Input{-1, kIdle};
         }
         frame_step(m, s, learner == 0 ? own : other, learner == 0 ? other : own, e);
