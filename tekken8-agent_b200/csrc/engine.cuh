@@ -398,6 +398,55 @@ T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, 
         (!(need(kRequiresRage) || need(kConsumesRage)) || on(f, fRage));
 }
 
+// What move_allowed derives from the fight rather than from the move, computed once for a
+// fighter whose candidates are all checked against the same state (the legal-move masks).
+struct MoveContext {
+    bool can, stepping, back_turned, opponent_back_turned, near_wall, left_ok, right_ok, heat, heat_available, rage;
+    uint8_t posture;
+    int32_t stance;
+};
+T8B_HD MoveContext move_context(const Match& m, const Fight& s, int p) {
+    const Fighter& f = s.f[p];
+    const Fighter& o = s.f[1 - p];
+    const Cfg& c = *m.cfg;
+    MoveContext x;
+    x.stepping = f.move < 0 && f.action_frame >= 1 && f.stun == 0 && !on(f, fCrumpled) && f.break_frames == 0 &&
+        f.pending_throw_hit < 0 && (f.universal == kSidestepLeft || f.universal == kSidestepRight);
+    x.can = can_act(m, s, p);
+    x.back_turned = on(f, fBackTurned);
+    x.opponent_back_turned = on(o, fBackTurned);
+    const double wall = o.x >= f.x ? s.left_wall : s.right_wall;
+    x.near_wall = !(mag(f.x - wall) > c.back_to_wall_distance);
+    const double toward = f.x >= o.x ? 1.0 : -1.0;
+    const double gap = hi(mag(f.x - o.x), 1e-9);
+    const double side = (f.axis - o.axis) * toward / gap;
+    x.left_ok = !(side > -c.side_exposure_ratio);
+    x.right_ok = !(side < c.side_exposure_ratio);
+    x.heat = on(f, fHeat);
+    x.heat_available = on(f, fHeatAvailable);
+    x.rage = on(f, fRage);
+    x.posture = f.posture;
+    x.stance = f.stance;
+    return x;
+}
+// move_allowed with the fight's side taken from a MoveContext (the same decisions in the same
+// order; the round is still running).
+T8B_HD bool context_allows(const MoveContext& x, uint64_t flags, uint8_t required_posture, int32_t required_stance,
+                           bool heat_cost) {
+    const auto need = [flags](uint64_t bit) { return (flags & bit) != 0ull; };
+    if (need(kReactive)) return false;
+    if (need(kRequiresSidestep) ? !x.stepping : !x.can) return false;
+    if (need(kRequiresBackTurned) != x.back_turned) return false;
+    if (need(kRequiresOpponentBackTurned) && !x.opponent_back_turned) return false;
+    if (need(kRequiresBackToWall) && !x.near_wall) return false;
+    if (need(kRequiresOpponentLeft) && !x.left_ok) return false;
+    if (need(kRequiresOpponentRight) && !x.right_ok) return false;
+    return required_posture == x.posture && (required_stance < 0 || required_stance == x.stance) &&
+        (!need(kRequiresHeat) || x.heat) && (!need(kConsumesHeat) || x.heat) && (!heat_cost || x.heat) &&
+        (!need(kEngagesHeat) || (x.heat_available && !x.heat)) &&
+        (!(need(kRequiresRage) || need(kConsumesRage)) || x.rage);
+}
+
 // legal (full_combat_core.hpp:380-441)
 T8B_HD bool input_ok(const Match& m, const Fight& s, int p, const Input& in) {
     if (s.winner >= 0) return false;

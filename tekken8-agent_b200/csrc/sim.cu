@@ -358,10 +358,20 @@ __global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t
     const int player = side == 0 ? learner : 1 - learner;
     const int count = m.side[player]->candidate_count;
     const Fight& s = fights[warp];
+    // move candidates: the gate record against the fighter's side of move_allowed, derived once
+    const MoveContext context = move_context(m, s, player);
+    const DGate* gates = m.side[player]->gates;
     uint32_t mine = 0;
     for (int word = 0; word < kMaskWords; ++word) {
         const int c = word * 32 + lane;
-        const bool legal = c < count && candidate_ok(m, s, player, c);
+        bool legal = false;
+        if (c >= kUniversalCount && c < count) {
+            const DGate g = gates[c];
+            legal = g.move >= 0 && s.winner < 0 &&
+                context_allows(context, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
+        } else if (c < count) {
+            legal = candidate_ok(m, s, player, c);
+        }
         const uint32_t bits = __ballot_sync(0xffffffffu, legal);
         if (lane == word) mine = bits;
     }
