@@ -778,7 +778,8 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 prep.ret = s.mb_ret.data();
                 prep.src_tables = r.feature_tables;
                 prep.tables = s.mb_tables.data();
-                launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
+                launch("k_gather", ppo::k_gather, blocks((n + ppo::kGatherRows - 1) / ppo::kGatherRows, ppo::kWarps),
+                       32 * ppo::kWarps, 0, st, prep);
                 check(cudaGetLastError(), "gather minibatch");
                 s.network(n, st);
                 ppo::Loss loss{};

@@ -137,6 +137,96 @@ __global__ void k_prep(Prep p) {
     }
 }
 
+// The minibatch gather of update_ppo: k_prep's work for kGatherRows consecutive minibatch rows
+// per warp. The rows' source indices come from one load per lane, and every row's loads are
+// issued before any is used, so a warp keeps several random rows in flight; lane r carries row
+// r's per-sample scalars. The same arithmetic as k_prep, element for element.
+constexpr int kGatherRows = 4;
+constexpr int kGatherHeld = 8;  // columns a lane holds per row (the first 256 of the row)
+
+__global__ void __launch_bounds__(32 * kWarps) k_gather(Prep p) {
+    const int lane = threadIdx.x & 31;
+    const size_t first = (static_cast<size_t>(blockIdx.x) * kWarps + (threadIdx.x >> 5)) * kGatherRows;
+    if (first >= p.count) return;
+    size_t mine = 0;
+    if (lane < kGatherRows && first + lane < p.count) mine = p.perm ? p.perm[p.offset + first + lane] : p.offset + first + lane;
+    size_t src[kGatherRows];
+    bool live[kGatherRows];
+#pragma unroll
+    for (int r = 0; r < kGatherRows; ++r) {
+        src[r] = __shfl_sync(0xffffffffu, mine, r);
+        live[r] = first + r < p.count;
+    }
+    float held[kGatherRows][kGatherHeld];
+#pragma unroll
+    for (int r = 0; r < kGatherRows; ++r) {
+        const float* row = p.obs + src[r] * static_cast<size_t>(p.width);
+#pragma unroll
+        for (int k = 0; k < kGatherHeld; ++k) {
+            const int j = lane + 32 * k;
+            held[r][k] = live[r] && j < p.width ? row[j] : 0.0f;
+        }
+    }
+    uint32_t words[kGatherRows];
+#pragma unroll
+    for (int r = 0; r < kGatherRows; ++r) {
+        words[r] = 0;
+        if (live[r] && lane < kMaskWords) {
+            if (p.src_bits) {
+                words[r] = p.src_bits[src[r] * kMaskWords + lane];
+            } else {
+                const uint8_t* m = p.src_bytes + src[r] * p.action_count + lane * 32;
+                for (int b = 0; b < 32 && lane * 32 + b < p.action_count; ++b) words[r] |= (m[b] != 0 ? 1u : 0u) << b;
+            }
+        }
+    }
+    const bool carries = lane < kGatherRows && first + lane < p.count;
+    int32_t action = 0, table = 0;
+    float old_lp = 0.0f, old_v = 0.0f, advantage = 0.0f, ret = 0.0f;
+    if (carries) {
+        action = static_cast<int32_t>(p.src_actions[mine]);
+        old_lp = p.src_old_lp[mine];
+        old_v = p.src_old_v[mine];
+        advantage = p.src_adv[mine];
+        ret = p.src_ret[mine];
+        table = p.src_tables ? p.src_tables[mine] : 0;
+    }
+#pragma unroll
+    for (int r = 0; r < kGatherRows; ++r) {
+        if (!live[r]) break;
+        __nv_bfloat16* out = p.x + (first + r) * static_cast<size_t>(p.padded);
+#pragma unroll
+        for (int k = 0; k < kGatherHeld; ++k) {
+            const int j = lane + 32 * k;
+            if (j >= p.padded) break;
+            float v = held[r][k];
+            if (j < p.width && p.normalize) v = fminf(p.clip, fmaxf(-p.clip, (v - p.mean[j]) * p.istd[j]));
+            out[j] = __float2bfloat16_rn(v);
+        }
+        const float* row = p.obs + src[r] * static_cast<size_t>(p.width);
+        for (int j = lane + 32 * kGatherHeld; j < p.padded; j += 32) {
+            float v = 0.0f;
+            if (j < p.width) {
+                v = row[j];
+                if (p.normalize) v = fminf(p.clip, fmaxf(-p.clip, (v - p.mean[j]) * p.istd[j]));
+            }
+            out[j] = __float2bfloat16_rn(v);
+        }
+        if (lane < kMaskWords) p.bits[(first + r) * kMaskWords + lane] = words[r];
+    }
+    if (carries) {
+        const size_t i = first + lane;
+        p.actions[i] = action;
+        p.old_lp[i] = old_lp;
+        p.old_v[i] = old_v;
+        float a = advantage;
+        if (p.adv_stats) a = static_cast<float>((static_cast<double>(a) - p.adv_stats[0]) * p.adv_stats[1]);
+        p.adv[i] = a;
+        p.ret[i] = ret;
+        p.tables[i] = table;
+    }
+}
+
 // ------------------------------------------------------------------ GEMM epilogues
 // Epilogue stores go through the warp's scratch: each lane writes its own row's 32 values,
 // then the warp writes 8 (bf16) or 4 (fp32) whole 64/128-byte row segments per instruction.
