@@ -274,33 +274,6 @@ std::vector<std::vector<uint32_t>> make_permutations(size_t count, int epochs, u
     return out;
 }
 
-__global__ void k_validate(const float* obs, int width, const uint8_t* bytes, const uint32_t* bits,
-                           int actions_per_sample, const int64_t* actions, const float* lp, const float* v,
-                           const float* adv, const float* ret, size_t n, int* invalid) {
-    const size_t s = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (s >= n) return;
-    bool finite = isfinite(lp[s]) && isfinite(v[s]) && isfinite(adv[s]) && isfinite(ret[s]);
-    for (int f = 0; f < width && finite; ++f) finite = isfinite(obs[s * width + f]);
-    bool any = false;
-    bool chosen = false;
-    const int64_t a = actions[s];
-    for (int w = 0; w < 12; ++w) {
-        uint32_t word;
-        if (bits) {
-            word = bits[s * 12 + w];
-        } else {
-            word = 0;
-            for (int b = 0; b < 32 && w * 32 + b < actions_per_sample; ++b) {
-                word |= (bytes[s * actions_per_sample + w * 32 + b] != 0 ? 1u : 0u) << b;
-            }
-        }
-        any = any || word != 0;
-        if (a >= w * 32 && a < w * 32 + 32) chosen = (word >> (a - w * 32)) & 1u;
-    }
-    const bool valid = a >= 0 && a < actions_per_sample && ((any && chosen) || (!any && a == 0));
-    if (!finite || !valid) atomicExch(invalid, 1);
-}
-
 // decision_flags_kernel + deterministic_decision_entropy_kernel (src/ppo.cu:570-610), multi-block:
 // per-block fp64 (entropy sum, decision count) in index order, then a fixed-order total.
 __global__ void k_decision_partials(const float* entropy, const uint8_t* decision, const uint8_t* bytes,
@@ -709,11 +682,32 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         if (r.sample_count > 0xffffffffull) raise(T8B_EINVAL, "rollout too large for 32-bit sample indices");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         const size_t samples = r.sample_count;
-        // validate_rollout_kernel (src/ppo.cu:423-451, 1545-1559)
+        // validate_rollout_kernel (src/ppo.cu:423-451, 1545-1559), with the batch moments of the
+        // observations for the normaliser taken in the same pass (merged after the update)
+        // chunks of 1,024-8,192 samples: enough blocks for a single minibatch, few chunks to merge
+        // for a whole rollout (the merge walks the chunks in order)
+        const size_t chunk = std::min<size_t>(8192, std::max<size_t>(1024, (samples / 512 + 7) / 8 * 8));
+        const size_t chunks = (samples + chunk - 1) / chunk;
+        const bool normalizing = s.config.observation_normalization;
+        if (normalizing && s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
         s.invalid.zero(st);
-        launch("k_validate", k_validate, blocks(samples, 256), 256, 0, st, r.observations, s.width, r.action_masks, r.action_mask_bits,
-                                                         s.config.action_count, r.actions, r.old_log_probabilities, r.old_values, r.advantages,
-                                                         r.returns, samples, s.invalid.data());
+        ppo::Scan scan{};
+        scan.obs = r.observations;
+        scan.width = s.width;
+        scan.samples = samples;
+        scan.chunk = chunk;
+        scan.moments = normalizing ? s.obs_chunks.data() : nullptr;
+        scan.bytes = r.action_masks;
+        scan.bits = r.action_mask_bits;
+        scan.actions_per_sample = s.config.action_count;
+        scan.actions = r.actions;
+        scan.lp = r.old_log_probabilities;
+        scan.v = r.old_values;
+        scan.adv = r.advantages;
+        scan.ret = r.returns;
+        scan.invalid = s.invalid.data();
+        launch("k_scan", ppo::k_scan, dim3(static_cast<unsigned>((s.width + 31) / 32 + 1), static_cast<unsigned>(chunks)), 256,
+               0, st, scan);
         check(cudaGetLastError(), "validate rollout");
         int invalid = 0;
         s.invalid.download(&invalid, 1, st);
@@ -866,14 +860,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
             }
         }
         // merge the observation normaliser after the update (src/ppo.cu:1663-1667)
-        if (s.config.observation_normalization) {
-            // chunks of 1,024-8,192 samples: enough blocks for a single minibatch, few chunks to merge
-            // for a whole rollout (the merge walks the chunks in order)
-            const size_t chunk = std::min<size_t>(8192, std::max<size_t>(1024, (samples / 512 + 7) / 8 * 8));
-            const size_t chunks = (samples + chunk - 1) / chunk;
-            if (s.obs_chunks.size() < chunks * s.width * 3) s.obs_chunks.allocate(chunks * s.width * 3);
-            dim3 grid(static_cast<unsigned>(chunks), static_cast<unsigned>((s.width + 31) / 32));
-            launch("k_obs_moments", ppo::k_obs_moments, grid, 256, 0, st, r.observations, samples, s.width, chunk, s.obs_chunks.data());
+        if (normalizing) {
             if (s.comm.active() && s.comm.hooks.allreduce_sum_f64) {
                 // data parallel: every rank's batch moments land in its own slot of a zeroed
                 // [world][width][3] buffer, a sum all-reduce gathers them, and each rank merges

@@ -1138,51 +1138,117 @@ __global__ void k_adam(float* params, const float* grads, float* m1, float* m2, 
     if (ts.copy_t) ts.copy_t[static_cast<size_t>(c) * ts.copy_t_ld + r] = b;
 }
 
-// ------------------------------------------------------------------ observation normaliser
-// Per-feature moments of a block of observations (fp64), merged by Chan's formula in a fixed
-// order (src/ppo.cu:150-215 computes them in two passes over the rollout; one pass of
-// per-chunk (count, mean, M2) merged in chunk order gives the same statistics).
-__global__ void k_obs_moments(const float* obs, size_t samples, int width, size_t chunk, double* out) {
-    // grid: (chunks, ceil(width / 32)); each thread owns one feature over one chunk
-    const int feature = blockIdx.y * 32 + (threadIdx.x & 31);
-    const int sub = threadIdx.x >> 5;  // 8 sub-chunks per block, merged in order
-    __shared__ double sm_mean[8][32], sm_m2[8][32];
-    __shared__ double sm_n[8];
-    const size_t begin = static_cast<size_t>(blockIdx.x) * chunk;
-    const size_t end = begin + chunk < samples ? begin + chunk : samples;
-    const size_t span = (end > begin ? end - begin : 0);
-    const size_t per = (span + 7) / 8;
-    const size_t b = begin + sub * per;
-    const size_t e = b + per < end ? b + per : end;
-    double mean = 0.0, m2 = 0.0, count = 0.0;
-    if (feature < width) {
-        for (size_t s = b; s < e; ++s) {
-            const double x = obs[s * width + feature];
-            count += 1.0;
-            const double d = x - mean;
-            mean += d / count;
-            m2 += d * (x - mean);
+// ------------------------------------------------------------------ rollout scan, observation normaliser
+// One pass over the rollout before update_ppo: validate_rollout_kernel's checks (src/ppo.cu:423-451:
+// finite observations, log-probabilities, values, advantages and returns; each action legal in its
+// mask, or 0 with no legal candidate) and, when `moments` is non-null, the batch moments of every
+// observation feature per chunk of samples ([chunks][width][3]: count, mean, M2), which the
+// normaliser merges after the update (src/ppo.cu:1663-1667). Grid x: the feature groups of 32,
+// then one group checking the chunk's samples; grid y: the chunks. A thread owns one feature
+// over an eighth of a chunk and sums (x - K) and (x - K)^2 in double, K the first value it reads
+// (shifted sums, no division per element); the eighths merge in order (Chan et al.).
+struct Scan {
+    const float* obs;
+    int width;
+    size_t samples, chunk;
+    double* moments;
+    const uint8_t* bytes;
+    const uint32_t* bits;
+    int actions_per_sample;
+    const int64_t* actions;
+    const float* lp;
+    const float* v;
+    const float* adv;
+    const float* ret;
+    int* invalid;
+};
+
+__global__ void __launch_bounds__(256) k_scan(Scan p) {
+    const int groups = (p.width + 31) / 32;
+    const size_t begin = static_cast<size_t>(blockIdx.y) * p.chunk;
+    const size_t end = begin + p.chunk < p.samples ? begin + p.chunk : p.samples;
+    if (static_cast<int>(blockIdx.x) == groups) {
+        bool ok = true;
+        for (size_t s = begin + threadIdx.x; s < end; s += blockDim.x) {
+            bool finite = isfinite(p.lp[s]) && isfinite(p.v[s]) && isfinite(p.adv[s]) && isfinite(p.ret[s]);
+            bool any = false, chosen = false;
+            const int64_t a = p.actions[s];
+            for (int w = 0; w < kMaskWords; ++w) {
+                uint32_t word = 0;
+                if (p.bits) {
+                    word = p.bits[s * kMaskWords + w];
+                } else {
+                    for (int b = 0; b < 32 && w * 32 + b < p.actions_per_sample; ++b) {
+                        word |= (p.bytes[s * p.actions_per_sample + w * 32 + b] != 0 ? 1u : 0u) << b;
+                    }
+                }
+                any = any || word != 0;
+                if (a >= w * 32 && a < w * 32 + 32) chosen = (word >> (a - w * 32)) & 1u;
+            }
+            const bool valid = a >= 0 && a < p.actions_per_sample && ((any && chosen) || (!any && a == 0));
+            ok = ok && finite && valid;
         }
-    } else {
-        count = e > b ? static_cast<double>(e - b) : 0.0;
+        if (!ok) atomicExch(p.invalid, 1);
+        return;
     }
-    sm_mean[sub][threadIdx.x & 31] = mean;
-    sm_m2[sub][threadIdx.x & 31] = m2;
-    if ((threadIdx.x & 31) == 0) sm_n[sub] = e > b ? static_cast<double>(e - b) : 0.0;
+    const int lane = threadIdx.x & 31;
+    const int sub = threadIdx.x >> 5;  // 8 eighths of the chunk per block
+    const int feature = static_cast<int>(blockIdx.x) * 32 + lane;
+    __shared__ double sm_mean[8][32], sm_m2[8][32], sm_n[8];
+    const size_t span = end > begin ? end - begin : 0;
+    const size_t per = (span + 7) / 8;
+    const size_t b = begin + sub * per < end ? begin + sub * per : end;
+    const size_t e = b + per < end ? b + per : end;
+    bool finite = true;
+    double shift = 0.0, s1 = 0.0, s2 = 0.0, t1 = 0.0, t2 = 0.0;
+    if (feature < p.width && e > b) {
+        const float* col = p.obs + feature;
+        const size_t w = static_cast<size_t>(p.width);
+        shift = col[b * w];
+        size_t s = b;
+        for (; s + 2 <= e; s += 2) {
+            const float x0 = col[s * w], x1 = col[(s + 1) * w];
+            finite = finite && isfinite(x0) && isfinite(x1);
+            const double d0 = static_cast<double>(x0) - shift, d1 = static_cast<double>(x1) - shift;
+            s1 += d0;
+            s2 += d0 * d0;
+            t1 += d1;
+            t2 += d1 * d1;
+        }
+        if (s < e) {
+            const float x = col[s * w];
+            finite = finite && isfinite(x);
+            const double d = static_cast<double>(x) - shift;
+            s1 += d;
+            s2 += d * d;
+        }
+    }
+    if (!finite) atomicExch(p.invalid, 1);
+    if (p.moments == nullptr) return;
+    const double n = e > b ? static_cast<double>(e - b) : 0.0;
+    double mean = 0.0, m2 = 0.0;
+    if (n > 0.0) {
+        const double sum = s1 + t1;
+        mean = shift + sum / n;
+        m2 = fmax((s2 + t2) - sum * sum / n, 0.0);
+    }
+    sm_mean[sub][lane] = mean;
+    sm_m2[sub][lane] = m2;
+    if (lane == 0) sm_n[sub] = n;
     __syncthreads();
-    if (sub == 0 && feature < width) {
-        double n = 0.0, mu = 0.0, q = 0.0;
+    if (sub == 0 && feature < p.width) {
+        double count = 0.0, mu = 0.0, q = 0.0;
         for (int k = 0; k < 8; ++k) {
             const double nk = sm_n[k];
             if (nk == 0.0) continue;
-            const double total = n + nk;
-            const double delta = sm_mean[k][threadIdx.x & 31] - mu;
-            q += sm_m2[k][threadIdx.x & 31] + delta * delta * n * nk / total;
+            const double total = count + nk;
+            const double delta = sm_mean[k][lane] - mu;
+            q += sm_m2[k][lane] + delta * delta * count * nk / total;
             mu += delta * nk / total;
-            n = total;
+            count = total;
         }
-        double* slot = out + (static_cast<size_t>(blockIdx.x) * width + feature) * 3;
-        slot[0] = n;
+        double* slot = p.moments + (static_cast<size_t>(blockIdx.y) * p.width + feature) * 3;
+        slot[0] = count;
         slot[1] = mu;
         slot[2] = q;
     }
