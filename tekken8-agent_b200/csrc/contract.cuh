@@ -95,6 +95,22 @@ T8B_HD uint64_t prefix_of(uint64_t seed, uint64_t stream) { return mix64(seed ^ 
 T8B_HD uint64_t draw(uint64_t prefix, uint64_t counter) { return mix64(prefix ^ counter); }
 T8B_HD uint64_t hash3(uint64_t seed, uint64_t stream, uint64_t counter) { return draw(prefix_of(seed, stream), counter); }
 T8B_HD int below(uint64_t bits, int bound) { return static_cast<int>(bits % static_cast<uint64_t>(bound)); }
+// x mod b for x < 2^53 and b < 2^20, given inverse = 1.0 / b: the double quotient estimate is off
+// by at most one, so one correction gives the exact remainder.
+T8B_HD uint32_t reduce_by(uint64_t x, uint32_t b, double inverse) {
+    int64_t r = static_cast<int64_t>(x) -
+        static_cast<int64_t>(static_cast<double>(x) * inverse) * static_cast<int64_t>(b);
+    if (r < 0) r += b;
+    else if (r >= static_cast<int64_t>(b)) r -= b;
+    return static_cast<uint32_t>(r);
+}
+// below(bits, bound) for a bound below 2^20 with its reciprocal at hand: the high word reduced
+// first, then the 52-bit rest.
+T8B_HD int below_with(uint64_t bits, int bound, double inverse) {
+    const uint32_t b = static_cast<uint32_t>(bound);
+    const uint64_t r = reduce_by(bits >> 32, b, inverse);
+    return static_cast<int>(reduce_by((r << 32) | (bits & 0xffffffffull), b, inverse));
+}
 T8B_HD double unit(uint64_t bits) { return static_cast<double>(bits >> 11) * (1.0 / 9007199254740992.0); }
 
 // ------------------------------------------------------------------ scripted opponents
@@ -115,7 +131,7 @@ T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggress
     const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
     if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
         for (int k = 0; k < 24; ++k) {
-            const int c = kUniversalCount + below(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount);
+            const int c = kUniversalCount + below_with(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount, ch.move_candidate_inverse);
             if (candidate_ok(m, s, p, c)) return c;
         }
     }

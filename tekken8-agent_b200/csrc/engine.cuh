@@ -146,6 +146,7 @@ struct DCharacter {
     const int32_t* candidate_moves;
     const DFacts* facts;
     const DGate* gates;  // [candidate_count]
+    double move_candidate_inverse;  // 1 / (candidate_count - kUniversalCount), 0 without move candidates
     int32_t move_count, stance_count, candidate_count, roster_id;
     DRules rules;
 };

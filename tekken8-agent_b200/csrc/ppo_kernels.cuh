@@ -883,7 +883,7 @@ constexpr int kLossRows = 256;
 // most kLossRows rows of one table, counted over the tables in order. Blocks past the last run
 // only write zero partials.
 template <int F>
-__global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
+__global__ void __launch_bounds__(32 * kWarps, 3) k_loss(Loss p) {
     extern __shared__ float4 table[];  // action_count x F floats, see staged_slot
     __shared__ float qs[kWarps][64];
     __shared__ float grads[kWarps][64];
@@ -925,6 +925,9 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
     const float scale = rsqrtf(static_cast<float>(p.feature_size));
     for (int row = run[1] + warp; bucket >= 0 && row < run[2]; row += kWarps) {
         const size_t i = static_cast<size_t>(row);
+        // the sample's scalars load with its output row, one exposed latency per sample
+        const int32_t action_in = p.actions[i];
+        const float old_lp_in = p.old_lp[i], advantage_in = p.adv[i], ret_in = p.ret[i], old_v_in = p.old_v[i];
         const float* o = p.out + i * p.ld;
         for (int f = lane; f <= p.feature_size; f += 32) qs[warp][f] = o[f];
         __syncwarp();
@@ -953,11 +956,11 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
         for (int j = lane; j < count; j += 32) local += expf(sc[j] - maximum);
         const float sum = fmaxf(warp_sum(local), 1e-20f);
         const float log_sum = logf(sum) + maximum;
-        const int selected = any ? p.actions[i] : 0;
+        const int selected = any ? action_in : 0;
         const float new_lp = sc[legal_rank(words, any, selected)] - log_sum;
-        const float log_ratio = new_lp - p.old_lp[i];
+        const float log_ratio = new_lp - old_lp_in;
         const float ratio = expf(log_ratio);
-        const float advantage = p.adv[i];
+        const float advantage = advantage_in;
         const float unclipped = ratio * advantage;
         const float clipped = fminf(1.0f + p.clip, fmaxf(1.0f - p.clip, ratio)) * advantage;
         const bool use_unclipped = unclipped <= clipped;
@@ -1000,13 +1003,13 @@ __global__ void __launch_bounds__(32 * kWarps) k_loss(Loss p) {
             if (lane + 32 < F) grads[warp][32 + lane] = bad_table ? __int_as_float(0x7fc00000) : upper * scale;
         }
         const float value = qs[warp][p.feature_size];
-        const float error = value - p.ret[i];
+        const float error = value - ret_in;
         float vgrad = error;
         float vloss = 0.5f * error * error;
         if (p.value_clip > 0.0f) {
-            const float delta = value - p.old_v[i];
-            const float clipped_value = p.old_v[i] + fminf(p.value_clip, fmaxf(-p.value_clip, delta));
-            const float cerr = clipped_value - p.ret[i];
+            const float delta = value - old_v_in;
+            const float clipped_value = old_v_in + fminf(p.value_clip, fmaxf(-p.value_clip, delta));
+            const float cerr = clipped_value - ret_in;
             const float closs = 0.5f * cerr * cerr;
             if (closs > vloss) {
                 vloss = closs;

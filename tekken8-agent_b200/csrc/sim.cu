@@ -986,6 +986,7 @@ int t8b_sim_create(const t8b_character_t* roster, int roster_count, const t8b_en
             d.move_count = roster[c].move_count;
             d.stance_count = roster[c].stance_count;
             d.candidate_count = roster[c].candidate_count;
+            d.move_candidate_inverse = roster[c].candidate_count > kUniversalCount ? 1.0 / (roster[c].candidate_count - kUniversalCount) : 0.0;
             d.roster_id = roster[c].roster_id;
             d.rules.resource_max = roster[c].rules.resource_max;
             d.rules.install_threshold = roster[c].rules.install_threshold;
