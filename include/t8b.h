@@ -329,6 +329,9 @@ int t8b_debug_bounded_wait(int arrive, uint32_t spin_limit, int* timed_out);
 uint64_t t8b_launch_count(void);
 void t8b_profile_enable(int on);
 size_t t8b_profile_report(char* text, size_t capacity);
+/* Restricts the event bracketing to launches labelled `label` (copied; NULL brackets every
+ * launch again), so one kernel can be timed inside a run without events around the others. */
+void t8b_profile_only(const char* label);
 
 /* ------------------------------------------------------------------ policy and PPO
  * class GpuActorCritic (include/t8_v2/ppo.hpp:112-193). Every matrix product runs bf16 x bf16

@@ -20,7 +20,9 @@ struct Timing {
 
 std::atomic<uint64_t> g_launches{0};
 std::atomic<bool> g_profiling{false};
+std::atomic<bool> g_filtered{false};
 std::mutex g_lock;
+std::string g_only;  // the one label bracketed while g_filtered
 std::map<std::string, Timing> g_timings;
 std::vector<cudaEvent_t> g_pool;
 
@@ -41,6 +43,7 @@ LaunchScope::LaunchScope(const char* n, cudaStream_t s) : name(n), stream(s) {
     g_launches.fetch_add(1, std::memory_order_relaxed);
     if (g_profiling.load(std::memory_order_relaxed)) {
         std::lock_guard<std::mutex> guard(g_lock);
+        if (g_filtered.load(std::memory_order_relaxed) && g_only != name) return;
         start = take_event();
         cudaEventRecord(start, stream);
     }
@@ -66,6 +69,13 @@ void t8b_profile_enable(int on) {
     std::lock_guard<std::mutex> guard(t8b::g_lock);
     if (on) t8b::g_timings.clear();
     t8b::g_profiling.store(on != 0);
+}
+
+/* Event bracketing for launches labelled `label` only (NULL: every launch). */
+void t8b_profile_only(const char* label) {
+    std::lock_guard<std::mutex> guard(t8b::g_lock);
+    t8b::g_only = label != nullptr ? label : "";
+    t8b::g_filtered.store(label != nullptr);
 }
 
 /* Synchronises the device, folds the recorded events into totals and writes one line per

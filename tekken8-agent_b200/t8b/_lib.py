@@ -306,6 +306,7 @@ PROTOTYPES.update({
     "t8b_launch_count": (u64, []),
     "t8b_profile_enable": (None, [C.c_int]),
     "t8b_profile_report": (C.c_size_t, [C.c_char_p, C.c_size_t]),
+    "t8b_profile_only": (None, [C.c_char_p]),
     "t8b_actor_config_default": (None, [C.POINTER(ActorConfig)]),
     "t8b_ppo_config_default": (None, [C.POINTER(PpoConfig)]),
     "t8b_policy_create": (C.c_int, [C.c_size_t, C.POINTER(ActorConfig), u64, C.POINTER(vp)]),

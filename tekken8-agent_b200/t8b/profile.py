@@ -18,6 +18,11 @@ def enable(on: bool = True) -> None:
     lib().t8b_profile_enable(1 if on else 0)
 
 
+def only(label: str | None) -> None:
+    """Brackets only the launches labelled `label` (None: every launch)."""
+    lib().t8b_profile_only(None if label is None else label.encode())
+
+
 def report() -> dict[str, tuple[int, float]]:
     """Synchronises the device and returns {label: (launches, total device ms)}."""
     need = lib().t8b_profile_report(None, 0)
