@@ -614,10 +614,13 @@ int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, co
         smp.log_probs = s.log_probs.data();
         smp.values = s.values.data();
         smp.entropies = s.entropies.data();
-        // one group per feature table (plus one for out-of-range table indices), about 64 samples
-        // per block
+        // one group per feature table (plus one for out-of-range table indices), each split into
+        // parts so that the grid fills one wave of two blocks per SM (at most 256 samples a block
+        // beyond that): at 32,768 samples over 42 groups, 7 parts (294 blocks) measured 12 %
+        // faster than 13 parts of about 64 samples (546 blocks, 1.8 waves)
         const size_t groups = tables ? static_cast<size_t>(s.tables) + 1 : 1;
-        smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>((n + groups * 64 - 1) / (groups * 64), 1), 4096));
+        const size_t wave = static_cast<size_t>(2 * sm_count()) / groups;
+        smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>({(n + groups * 256 - 1) / (groups * 256), wave, 1}), 4096));
         const unsigned sample_grid = static_cast<unsigned>(groups * smp.parts);
         const size_t sample_bytes = ppo::sample_smem(s.feature_size);
         if (s.feature_size == 48) {
