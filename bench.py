@@ -43,10 +43,12 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--self-play", action="store_true",
                     help="mirror self-play: a frozen copy of the initial policy plays the other side")
-    ap.add_argument("--workload", choices=("iteration", "mlp"), default="iteration",
-                    help="iteration: the self-play training iteration (the headline); mlp: policy forward + "
-                         "backward on one batch of 32,768 at the microbench shapes (128 observations, 256 candidates "
-                         "x 48 features, 2 x 512 hidden)")
+    ap.add_argument("--workload", choices=("iteration", "mlp", "gae_loss", "engine"), default="iteration",
+                    help="iteration: the self-play training iteration (config 4, the headline); mlp: policy forward "
+                         "+ backward on one batch of 32,768 at the microbench shapes (config 3: 128 observations, 256 "
+                         "candidates x 48 features, 2 x 512 hidden); gae_loss: GAE + advantage normalisation + the "
+                         "clipped PPO objective over a T=128 x N=32,768 rollout with 256 slots (config 2); engine: "
+                         "1,024 fights x 3,600 frames of random legal play (config 1)")
     return ap.parse_args()
 
 
@@ -172,6 +174,9 @@ GEMM_FLOPS_PER_SAMPLE = {
 # GAE: read reward, value, next value (4 B each), terminated, truncated (1 B each); write
 # advantage and return (4 B each) = 22 B per sample.
 GAE_BYTES_PER_SAMPLE = 22
+# Config 2 objective on raw logits (K = 256): read K + 1 outputs, K mask bytes, the action and four
+# scalars (old log-prob, old value, advantage, return); write K + 1 gradients = 2,336 B per sample.
+LOGIT_LOSS_BYTES_PER_SAMPLE = 257 * 4 + 256 + 8 + 4 * 4 + 257 * 4
 # PPO loss with on-chip scores: read the 33 output floats, 12 mask words, action, table id, old
 # log-prob, advantage, return, old value; write the 33 output gradients = 364 B per sample.
 LOSS_BYTES_PER_SAMPLE = 33 * 4 + 12 * 4 + 8 + 4 + 4 * 4 + 33 * 4 + 24
@@ -214,13 +219,11 @@ def run_reference(args):
     world, rank, local = distributed()
     if rank != 0:
         return
-    import numpy as np
-    from t8b import roster as roster_module
-    from t8b.train import config4_env
-    roster = roster_module.parse(roster_raw())
-    features = roster.feature_tables()
-    env = config4_env()
+    # the reference arm loads only the oracle's libraries (the reference's own CPU code), no product code
+    from oracle import ref
     from oracle.cpu_iteration import CpuIteration
+    features = ref.RefRoster(roster_raw()).feature_tables()
+    env = ref.config4_env()
     threads = os.cpu_count() or 1
     sample_envs, sample_horizon = 2048, 16
     it = CpuIteration(roster_raw(), features, env, sample_envs, sample_horizon, args.epochs, args.minibatches,
@@ -461,12 +464,245 @@ def run_mlp(args):
     print(json.dumps(line), flush=True)
 
 
+def clock_indices():
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    if visible and all(v.strip().isdigit() for v in visible.split(",")):
+        return [visible.split(",")[0].strip()]
+    return ["0"]
+
+
+def run_gae_loss(args):
+    """Config 2: GAE with advantage normalisation and the clipped PPO objective (raw logits over
+    K = 256 slots) over one rollout of T = 128 decisions x N = 32,768 fights (4,194,304 samples),
+    seeded synthetic inputs (t8b.workloads.config2_rollout). A step is compute_gae(normalize) +
+    t8b_ppo_output_gradient over the whole rollout; inputs (9.8 GB) are larger than L2."""
+    import numpy as np
+    import torch
+    from t8b import profile
+    from t8b.policy import GpuRolloutBuffer, ppo_config, ppo_output_gradient
+    from t8b.workloads import config2_rollout
+    t, n, k = 128, 32768, 256
+    w = config2_rollout(t, n, k, seed=1)
+    buf = GpuRolloutBuffer(n, t)
+    fields = (("rewards", w.rewards), ("old_values", w.values), ("next_values", w.next_values),
+              ("terminated", w.terminated), ("truncated", w.truncated))
+    for name, src in fields:
+        buf.tensor(name).copy_(src)
+    adv = buf.tensor("advantages").reshape(-1)
+    ret = buf.tensor("returns").reshape(-1)
+    old_v = w.values.reshape(-1)
+    cfg = ppo_config(entropy_coefficient=0.01)
+    grads = torch.empty_like(w.outputs)
+    sums = torch.zeros(8, dtype=torch.float64, device="cuda")
+    from t8b._lib import call
+    from t8b.device import ptr
+    import ctypes as C
+
+    def step():
+        buf.compute_gae(0.99, 0.95, True)
+        call("t8b_ppo_output_gradient", ptr(w.outputs), ptr(w.masks), ptr(w.actions), ptr(w.old_log_probabilities),
+             ptr(old_v), ptr(adv), ptr(ret), w.samples, k, C.byref(cfg), ptr(grads), ptr(sums), None)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches_before = profile.launch_count()
+    profile.enable(True)
+    profile.only("k_logit_objective")
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(clock_indices()) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        end.synchronize()
+    launches = profile.launch_count() - launches_before
+    timed = profile.report()
+    profile.enable(False)
+    profile.only(None)
+    ms = start.elapsed_time(end) / args.steps
+    # per-kernel table from one more, untimed step with events around every launch
+    profile.enable(True)
+    step()
+    kernels = profile.report()
+    profile.enable(False)
+    # end to end: this step's inputs copied from pinned host memory, the metric sums read back
+    host_inputs = [(src, torch.empty(src.shape, dtype=src.dtype, pin_memory=True)) for src in
+                   (w.rewards, w.values, w.next_values, w.terminated, w.truncated, w.outputs, w.masks, w.actions,
+                    w.old_log_probabilities)]
+    for src, pinned in host_inputs:
+        pinned.copy_(src)
+    dests = [buf.tensor("rewards"), buf.tensor("old_values"), buf.tensor("next_values"), buf.tensor("terminated"),
+             buf.tensor("truncated"), w.outputs, w.masks, w.actions, w.old_log_probabilities]
+    sums_host = torch.empty(8, dtype=torch.float64, pin_memory=True)
+    bytes_up = sum(p.numel() * p.element_size() for _, p in host_inputs)
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for _ in range(args.steps):
+        for (_, pinned), dest in zip(host_inputs, dests):
+            dest.copy_(pinned.view(dest.shape), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        step()
+        sums_host.copy_(sums, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - wall0) / args.steps
+    samples = w.samples
+    peak_hbm, _, _, peak_kind = measured_peaks()
+    loss_launches, loss_ms = timed.get("k_logit_objective", (1, float("nan")))
+    loss_avg_ms = loss_ms / max(loss_launches, 1)
+    loss_gbs = LOGIT_LOSS_BYTES_PER_SAMPLE * samples / (loss_avg_ms / 1000.0) / 1e9
+    rows = []
+    for label, (count, total) in sorted(kernels.items(), key=lambda kv: -kv[1][1]):
+        row = {"kernel": label, "launches_per_step": count, "ms_per_step": total}
+        per = {"k_logit_objective": LOGIT_LOSS_BYTES_PER_SAMPLE, "k_gae": GAE_BYTES_PER_SAMPLE,
+               "k_normalize": 8}.get(label)
+        if per is not None:
+            gbs = per * samples * count / (total / 1000.0) / 1e9
+            row.update(bound="hbm", achieved=gbs, unit="GB/s", frac=gbs / peak_hbm)
+        rows.append(row)
+    cpu = cpu_gae_loss(w, adv, ret, cfg) if not args.no_cpu_baseline else None
+    line = {"metric": "GAE + clipped PPO loss samples/s (T=128 x N=32,768, K=256), 1 B200", "value": samples / (ms / 1000.0),
+            "unit": "samples/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp64 statistics)",
+            "data": "synthetic (seeded, t8b.workloads.config2_rollout)",
+            "config": {"workload": "config 2: GAE + advantage normalisation + clipped PPO/value/entropy objective on "
+                                   "raw logits, T=128 x N=32,768, K=256 slots ~30% legal, seed 1",
+                       "samples": samples, "slots": k, "l2": "inputs larger than L2 (9.8 GB per step)"},
+            "e2e": {"value": samples / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": bytes_up,
+                    "d2h_bytes_per_step": 64},
+            "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
+            "roofline": {"kernel": "k_logit_objective", "bound": "hbm", "achieved": loss_gbs, "peak": peak_hbm,
+                         "unit": "GB/s", "frac": loss_gbs / peak_hbm, "traffic": None,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)", "avg_launch_ms": loss_avg_ms,
+                         "algorithmic_bytes_per_sample": LOGIT_LOSS_BYTES_PER_SAMPLE},
+            "kernels": rows, "kernels_source": "one untimed step after the timed ones, CUDA events around every launch",
+            "clocks": clocks.summary()}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def cpu_gae_loss(w, adv, ret, cfg, sample_rows=262144):
+    """CPU leg of config 2: the float64 numpy GAE restatement over the whole rollout and the
+    float64 C restatement of the objective (oracle/objective.c, all host threads) over a bounded
+    sample of its rows; the rate is samples / (GAE time per sample + objective time per sample)."""
+    from oracle import objective
+    from oracle import ppo_ref as R
+    host = lambda x: x.cpu().numpy()
+    rewards, values, term, trunc, nv = (host(x) for x in (w.rewards, w.values, w.terminated, w.truncated, w.next_values))
+    t0 = time.perf_counter()
+    a, _ = R.gae(rewards, values, term, trunc, nv, 0.99, 0.95)
+    R.normalize_advantages(a)
+    gae_s = (time.perf_counter() - t0) / w.samples
+    rows = slice(0, sample_rows)
+    inputs = [host(x[rows]) for x in (w.outputs, w.masks, w.actions, w.old_log_probabilities,
+                                      w.values.reshape(-1), adv, ret)]
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    objective.objective(*inputs, w.samples, cfg.clip_range, cfg.value_clip_range, cfg.value_coefficient,
+                        cfg.entropy_coefficient, threads=threads)
+    loss_s = (time.perf_counter() - t0) / sample_rows
+    return {"value": 1.0 / (gae_s + loss_s), "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"GAE + normalisation over all {w.samples} samples (numpy float64, one thread) and the objective "
+                      f"over {sample_rows} of them (oracle/objective.c float64, {threads} threads)"}
+
+
+def run_engine(args):
+    """Config 1: 1,024 fights x 3,600 frames of the engine, every fighter picking a uniformly random
+    legal candidate at each decision (PCG32 per fight), one FNV-1a state hash per fight-frame
+    written to HBM. A step is one t8b_sim_random_play over the whole workload."""
+    import numpy as np
+    import torch
+    from t8b import profile
+    from t8b import roster as roster_module
+    from t8b.sim import GpuFullMoveSimulator
+    from t8b._lib import call
+    from t8b.device import ptr
+    fights, frames = 1024, 3600
+    raw = roster_raw()
+    roster = roster_module.parse(raw)
+    rng = np.random.default_rng(0)
+    p1 = rng.integers(0, len(roster), fights).astype(np.int32)
+    p2 = rng.integers(0, len(roster), fights).astype(np.int32)
+    x1 = np.full(fights, -0.45)
+    x2 = np.full(fights, 0.45)
+    sim = GpuFullMoveSimulator(roster, fights)
+    dev = lambda a: torch.as_tensor(a, device="cuda")
+    tp1, tp2, tx1, tx2 = dev(p1), dev(p2), dev(x1), dev(x2)
+    hashes = torch.empty((fights, frames), dtype=torch.int64, device="cuda")
+
+    def step(a=tp1, b=tp2, c=tx1, d=tx2, out=hashes):
+        call("t8b_sim_random_play", sim._handle, fights, ptr(a), ptr(b), ptr(c), ptr(d), frames, 0, ptr(out), None)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches_before = profile.launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(clock_indices()) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        end.synchronize()
+    launches = profile.launch_count() - launches_before
+    ms = start.elapsed_time(end) / args.steps
+    units = fights * frames
+    # end to end: the matchups and start positions uploaded from pinned memory, the hashes read back
+    pins = [torch.as_tensor(a).pin_memory() for a in (p1, p2, x1, x2)]
+    hashes_host = torch.empty((fights, frames), dtype=torch.int64, pin_memory=True)
+    torch.cuda.synchronize()
+    wall0 = time.perf_counter()
+    for _ in range(args.steps):
+        ins = [p.to("cuda", non_blocking=True) for p in pins]
+        step(*ins)
+        hashes_host.copy_(hashes, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = (time.perf_counter() - wall0) / args.steps
+    got = hashes.cpu().numpy().view(np.uint64)
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import ref
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        want, _, _ = ref.RefRoster(raw).random_play(p1, p2, x1, x2, frames, 0, threads=threads)
+        cpu_s = time.perf_counter() - t0
+        cpu = {"value": units / cpu_s, "unit": "fight-frames/s", "cores": threads, "kind": "reference",
+               "sample": f"the whole workload ({fights} fights x {frames} frames) on the reference's own CPU engine "
+                         f"(full_core::step, oracle/_ref), one fight per thread over {threads} threads",
+               "hashes_equal": bool(np.array_equal(got, want))}
+    line = {"metric": "engine fight-frames/s (random legal play, 1,024 fights x 3,600 frames), 1 B200",
+            "value": units / (ms / 1000.0), "unit": "fight-frames/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64 engine (no FMA contraction)",
+            "data": "synthetic (41-fighter roster tables from the reference loader; PCG32 seed 0 per fight)",
+            "config": {"workload": "config 1: engine parity run, 1,024 fights x 3,600 frames, per-frame state hash",
+                       "fights": fights, "frames": frames,
+                       "l2": "not flushed: 240 B of state per fight stays in registers; the 29 MB hash trace is "
+                             "written once per step"},
+            "e2e": {"value": units / e2e_s, "unit": "fight-frames/s", "h2d_bytes_per_step": fights * 24,
+                    "d2h_bytes_per_step": fights * frames * 8},
+            "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
+            "roofline": {"kernel": "k_random_play", "bound": "issue/latency (fp64 + integer branching)",
+                         "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
+                         "note": "1,024 fights are 32 warps on 148 SMs: one warp on most SMs; the figure of merit "
+                                 "is fight-frames/s against the CPU engine"},
+            "clocks": clocks.summary()}
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.workload == "mlp":
         run_mlp(args)
+    elif args.workload == "gae_loss":
+        run_gae_loss(args)
+    elif args.workload == "engine":
+        run_engine(args)
     else:
         run_ours(args)
 

@@ -459,7 +459,8 @@ int t8b_policy_synchronize(t8b_policy* policy, void* stream);
 /* debug_ppo_objective_gradient (include/t8_v2/ppo.hpp:100-108), batched: d(objective)/d(logits,
  * value) of the clipped PPO objective for raw [n][k + 1] outputs. Device pointers. metric_sums
  * (8 doubles: policy loss, value loss, entropy, KL, clip fraction, -, decisions, decision
- * entropy) may be NULL. */
+ * entropy) may be NULL. The call returns once the work is queued on `stream` (its metric
+ * partials come from the library's stream-ordered pool on the current device). */
 int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const int64_t* actions,
                             const float* old_log_probabilities, const float* old_values, const float* advantages,
                             const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
@@ -470,7 +471,11 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
  * loop that must not pay cudaMalloc/cudaFree's implicit device synchronisation mid-step). The
  * metric partials use a static 4 MiB device array instead of a per-call buffer: at most 524,288
  * samples per call (T8B_EINVAL beyond); the first call on a device looks the array up and should
- * come before any stream capture; calls overlapping on the GPU race on the shared array. */
+ * come before any stream capture; calls overlapping on the GPU race on the shared array.
+ * The call returns once the work is queued: gradients and metric_sums are ordered on `stream`
+ * only, so synchronise it (or record an event on it) before the host or another stream reads them.
+ * `stream` must belong to the current device, and the device's primary context (the runtime
+ * API's) must be current: the array's address is kept per device index. */
 int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, const int64_t* actions,
                                    const float* old_log_probabilities, const float* old_values, const float* advantages,
                                    const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,
@@ -481,7 +486,10 @@ int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, c
 typedef struct t8b_rollout t8b_rollout;
 int t8b_rollout_create(size_t environments, size_t horizon, const t8b_actor_config_t* config, t8b_rollout** out);
 int t8b_rollout_destroy(t8b_rollout* rollout);
-int t8b_rollout_device_view(const t8b_rollout* rollout, t8b_rollout_view_t* out); /* ppo.hpp:239 */
+/* device_view  ppo.hpp:239. When steps were recorded with packed masks since the last view, the
+ * uint8 masks are expanded first; the expansion waits for those recordings on whatever stream
+ * they were queued and is complete when the call returns. */
+int t8b_rollout_device_view(const t8b_rollout* rollout, t8b_rollout_view_t* out);
 /* The same view with packed masks only (action_masks NULL): no uint8 expansion (no reference
  * counterpart; update_ppo reads action_mask_bits). */
 int t8b_rollout_packed_view(const t8b_rollout* rollout, t8b_rollout_view_t* out);

@@ -4,6 +4,7 @@ oracle/Makefile. Used only by tests/, __graft_entry__.smoke() and bench.py's CPU
 from __future__ import annotations
 
 import ctypes as C
+import os
 import subprocess
 from pathlib import Path
 
@@ -11,7 +12,41 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "_ref" / "libt8ref.so"
-REFERENCE = Path("/root/reference")
+# The reference checkout: $T8B_REFERENCE when set, else ../reference beside this repository.
+REFERENCE = Path(os.environ.get("T8B_REFERENCE", HERE.parent.parent / "reference"))
+
+
+class EnvConfig(C.Structure):
+    """t8b_env_config_t of include/t8b.h, the struct the harness converts to full_core::EnvConfig."""
+    _fields_ = [("max_round_frames", C.c_int32), ("hold_frames", C.c_int32), ("max_frames_per_decision", C.c_int32)] + \
+               [(n, C.c_float) for n in ("damage_reward", "win_reward", "draw_penalty", "throw_break_penalty",
+                                          "time_penalty_per_second", "damage_dealt_weight", "damage_taken_weight",
+                                          "distance_penalty_per_second")] + \
+               [("perception_delay", C.c_int32), ("memory", C.c_uint8), ("live_noise", C.c_uint8),
+                ("screen_view", C.c_uint8), ("pad", C.c_uint8), ("noise_position_max", C.c_float),
+                ("noise_flip_max", C.c_float), ("latency_min", C.c_int32), ("latency_max", C.c_int32),
+                ("pad2", C.c_int32), ("start_center_range", C.c_double), ("start_distance_min", C.c_double),
+                ("start_distance_max", C.c_double)]
+
+
+def env_config(**overrides) -> EnvConfig:
+    """full_core::EnvConfig with the reference's own defaults, then the given fields."""
+    config = EnvConfig()
+    lib().t8ref_env_config_default(C.byref(config))
+    for key, value in overrides.items():
+        setattr(config, key, value)
+    return config
+
+
+def config4_env(**overrides) -> EnvConfig:
+    """The trainer's measured self-play environment (training.ini through src/train_launcher.cpp:
+    106-160): screen-only observation with live noise (sigma 0.28 m, 10 % flips, latency 2-6),
+    perception delay 12, 8-frame holds and the anti-stalling reward terms."""
+    base = dict(screen_view=1, live_noise=1, noise_position_max=0.28, noise_flip_max=0.10, latency_min=2,
+                latency_max=6, perception_delay=12, hold_frames=8, draw_penalty=0.5, throw_break_penalty=0.03,
+                time_penalty_per_second=0.01, max_round_frames=3600)
+    base.update(overrides)
+    return env_config(**base)
 
 
 def build() -> Path:
@@ -54,6 +89,9 @@ def lib():
         h.t8ref_env_step.argtypes = [vp, vp, vp, C.c_uint64, C.c_uint64, C.c_int]
         h.t8ref_env_read.argtypes = [vp] * 14
         h.t8ref_env_upload_states.argtypes = [vp, vp]
+        h.t8ref_env_config_default.restype = None
+        h.t8ref_env_config_default.argtypes = [vp]
+        h.t8ref_roster_features.argtypes = [vp, vp, C.c_int]
         _lib = h
     return _lib
 
@@ -82,6 +120,13 @@ class RefRoster:
         if getattr(self, "handle", None):
             lib().t8ref_roster_free(self.handle)
             self.handle = None
+
+    def feature_tables(self, stride: int = 368) -> np.ndarray:
+        """[characters, stride, 32] float32 candidate features, zero past each character's candidates."""
+        count = lib().t8ref_roster_count(self.handle)
+        out = np.zeros((count, stride, 32), np.float32)
+        _check(lib().t8ref_roster_features(self.handle, _p(out), stride))
+        return out
 
     def random_play(self, p1, p2, x1, x2, frames: int, seed: int, threads: int = 8, states=False, inputs=False):
         p1 = np.ascontiguousarray(p1, np.int32)

@@ -247,6 +247,22 @@ fc::EnvConfig from_env_config(const t8b_env_config_t& o) {
     return c;
 }
 
+t8b_env_config_t to_env_config(const fc::EnvConfig& c) {
+    t8b_env_config_t o;
+    std::memset(&o, 0, sizeof o);
+    o.max_round_frames = c.max_round_frames; o.hold_frames = c.hold_frames;
+    o.max_frames_per_decision = c.max_frames_per_decision; o.damage_reward = c.damage_reward;
+    o.win_reward = c.win_reward; o.draw_penalty = c.draw_penalty; o.throw_break_penalty = c.throw_break_penalty;
+    o.time_penalty_per_second = c.time_penalty_per_second; o.damage_dealt_weight = c.damage_dealt_weight;
+    o.damage_taken_weight = c.damage_taken_weight; o.distance_penalty_per_second = c.distance_penalty_per_second;
+    o.perception_delay = c.perception_delay; o.memory = c.memory ? 1 : 0; o.live_noise = c.live_noise ? 1 : 0;
+    o.noise_position_max = c.noise_position_max; o.noise_flip_max = c.noise_flip_max;
+    o.latency_min = c.latency_min; o.latency_max = c.latency_max; o.screen_view = c.screen_view ? 1 : 0;
+    o.start_center_range = c.start_center_range; o.start_distance_min = c.start_distance_min;
+    o.start_distance_max = c.start_distance_max;
+    return o;
+}
+
 t8b_state_t to_state(const fc::State& s) {
     t8b_state_t o;
     std::memset(&o, 0, sizeof o);
@@ -633,6 +649,22 @@ void* t8ref_roster_parse(const void* data, size_t size) {
 }
 
 void t8ref_roster_free(void* roster) { delete static_cast<Roster*>(roster); }
+// full_core::EnvConfig's default member initialisers (include/t8_v2/full_move_contract.hpp:737-773).
+void t8ref_env_config_default(t8b_env_config_t* out) { *out = to_env_config(fc::EnvConfig{}); }
+
+// Candidate feature tables of a parsed roster: out[character][stride][32], zero past each
+// character's candidates (the trainer's table layout, src/full_move_train.cpp:1176-1184).
+int t8ref_roster_features(void* roster_handle, float* out, int stride) {
+    const Roster& roster = *static_cast<Roster*>(roster_handle);
+    for (std::size_t c = 0; c < roster.characters.size(); ++c) {
+        float* table = out + c * static_cast<std::size_t>(stride) * 32;
+        std::fill(table, table + static_cast<std::size_t>(stride) * 32, 0.0F);
+        const auto& f = roster.characters[c].features;
+        std::copy(f.begin(), f.begin() + std::min<std::size_t>(f.size(), static_cast<std::size_t>(stride) * 32), table);
+    }
+    return 0;
+}
+
 int t8ref_roster_count(void* roster) { return static_cast<int>(static_cast<Roster*>(roster)->characters.size()); }
 
 // The engine-parity workload (include/t8b.h t8b_sim_random_play) on full_core::step.

@@ -77,7 +77,10 @@ public:
         count_ = count;
         if (count > 0) {
             check(cudaMalloc(reinterpret_cast<void**>(&data_), sizeof(T) * count), "cudaMalloc");
-            check(cudaMemset(data_, 0, sizeof(T) * count), "cudaMemset");
+            // The clear runs on the legacy stream, which a caller's non-blocking stream does not
+            // wait for: it is complete before the buffer is handed out.
+            check(cudaMemsetAsync(data_, 0, sizeof(T) * count, cudaStreamLegacy), "cudaMemset");
+            check(cudaStreamSynchronize(cudaStreamLegacy), "cudaMemset");
         }
     }
     void upload(const T* host, std::size_t count, cudaStream_t stream) {

@@ -17,58 +17,119 @@
 
 namespace t8b {
 
-constexpr unsigned kGaeThreads = 128;
+// GAE block: 32 fights x chunks of 64 steps staged in shared memory (28 KB), 256 threads.
+constexpr int kGaeFights = 32;
+constexpr int kGaeChunk = 64;
+constexpr unsigned kGaeThreads = 256;
 
 // gae_kernel (src/ppo.cu:2003-2029) fused with advantage_stats_kernel (src/ppo.cu:2031-2063).
-__global__ void k_gae(const float* rewards, const float* values, const uint8_t* terminated, const uint8_t* truncated,
-                      const float* next_values, size_t envs, size_t horizon, float gamma, float lambda, float* adv,
-                      float* ret, double* partial) {
-    __shared__ double s1[kGaeThreads], s2[kGaeThreads];
-    const size_t env = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+// The [step][fight] records of one block's 32 fights are staged a chunk of 64 steps at a time,
+// latest chunk first: all 256 threads load the chunk's rows (each warp a 32-fight row of every
+// array, every load issued before any is used), warp 0 runs the recurrence of the reference for
+// its 32 fights, one lane each, over the chunk in reverse (the same fp32 operations in the same
+// order, so advantages and returns are the reference's bit for bit), and all threads store the
+// advantages and returns rows. The fp64 moments of each fight's advantages are summed in reverse
+// step order and reduced over the warp into one partial per block.
+__global__ void __launch_bounds__(kGaeThreads) k_gae(const float* rewards, const float* values, const uint8_t* terminated,
+                                                     const uint8_t* truncated, const float* next_values, size_t envs,
+                                                     size_t horizon, float gamma, float lambda, float* adv, float* ret,
+                                                     double* partial) {
+    __shared__ float s_reward[kGaeChunk][kGaeFights], s_value[kGaeChunk][kGaeFights], s_next[kGaeChunk][kGaeFights];
+    __shared__ uint8_t s_term[kGaeChunk][kGaeFights], s_trunc[kGaeChunk][kGaeFights];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const size_t fight0 = static_cast<size_t>(blockIdx.x) * kGaeFights;
+    const size_t fight = fight0 + static_cast<size_t>(lane);
+    const bool live = fight < envs;
+    float next = 0.0f;
     double sum = 0.0, square = 0.0;
-    if (env < envs) {
-        float next = 0.0f;
-        for (size_t back = 0; back < horizon; ++back) {
-            const size_t at = (horizon - 1 - back) * envs + env;
-            const bool time_limit = truncated[at] != 0;
-            const bool ended = terminated[at] != 0;
-            const float bootstrap = ended && !time_limit ? 0.0f : 1.0f;
-            const float trace = ended || time_limit ? 0.0f : 1.0f;
-            const float value = values[at];
-            const float delta = rewards[at] + gamma * next_values[at] * bootstrap - value;
-            next = delta + gamma * lambda * trace * next;
-            adv[at] = next;
-            ret[at] = next + value;
-            sum += static_cast<double>(next);
-            square += static_cast<double>(next) * static_cast<double>(next);
+    for (size_t chunk_end = horizon; chunk_end > 0;) {
+        const size_t first = chunk_end > static_cast<size_t>(kGaeChunk) ? chunk_end - kGaeChunk : 0;
+        const int rows = static_cast<int>(chunk_end - first);
+        constexpr int kRowsPerWarp = kGaeChunk / (kGaeThreads / 32);
+        float r[kRowsPerWarp], v[kRowsPerWarp], nv[kRowsPerWarp];
+        uint8_t te[kRowsPerWarp], tr[kRowsPerWarp];
+#pragma unroll
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            const int row = warp + k * (kGaeThreads / 32);
+            const size_t at = (first + static_cast<size_t>(row)) * envs + fight;
+            const bool in = live && row < rows;
+            r[k] = in ? rewards[at] : 0.0f;
+            v[k] = in ? values[at] : 0.0f;
+            nv[k] = in ? next_values[at] : 0.0f;
+            te[k] = in ? terminated[at] : 0;
+            tr[k] = in ? truncated[at] : 0;
         }
-    }
-    s1[threadIdx.x] = sum;
-    s2[threadIdx.x] = square;
-    __syncthreads();
-    for (int w = blockDim.x / 2; w > 0; w >>= 1) {
-        if (threadIdx.x < w) {
-            s1[threadIdx.x] += s1[threadIdx.x + w];
-            s2[threadIdx.x] += s2[threadIdx.x + w];
+#pragma unroll
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            const int row = warp + k * (kGaeThreads / 32);
+            s_reward[row][lane] = r[k];
+            s_value[row][lane] = v[k];
+            s_next[row][lane] = nv[k];
+            s_term[row][lane] = te[k];
+            s_trunc[row][lane] = tr[k];
         }
         __syncthreads();
+        if (warp == 0) {
+            for (int row = rows - 1; row >= 0; --row) {
+                const bool time_limit = s_trunc[row][lane] != 0;
+                const bool ended = s_term[row][lane] != 0;
+                const float bootstrap = ended && !time_limit ? 0.0f : 1.0f;
+                const float trace = ended || time_limit ? 0.0f : 1.0f;
+                const float value = s_value[row][lane];
+                const float delta = s_reward[row][lane] + gamma * s_next[row][lane] * bootstrap - value;
+                next = delta + gamma * lambda * trace * next;
+                s_reward[row][lane] = next;
+                s_next[row][lane] = next + value;
+                if (live) {
+                    sum += static_cast<double>(next);
+                    square += static_cast<double>(next) * static_cast<double>(next);
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kRowsPerWarp; ++k) {
+            const int row = warp + k * (kGaeThreads / 32);
+            if (live && row < rows) {
+                const size_t at = (first + static_cast<size_t>(row)) * envs + fight;
+                adv[at] = s_reward[row][lane];
+                ret[at] = s_next[row][lane];
+            }
+        }
+        __syncthreads();
+        chunk_end = first;
     }
-    if (threadIdx.x == 0) {
-        partial[2 * blockIdx.x] = s1[0];
-        partial[2 * blockIdx.x + 1] = s2[0];
+    if (warp == 0) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, off);
+            square += __shfl_xor_sync(0xffffffffu, square, off);
+        }
+        if (lane == 0) {
+            partial[2 * blockIdx.x] = sum;
+            partial[2 * blockIdx.x + 1] = square;
+        }
     }
 }
 
-// Fixed-order total of [blocks][2] partial sums -> out[0..1].
+// Fixed-order total of [blocks][2] partial sums -> out[0..1]: each lane of one warp sums a
+// strided share in index order, then a fixed butterfly adds the lanes.
 __global__ void k_pair_total(const double* partial, int blocks, double* out) {
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    if (blockIdx.x != 0 || threadIdx.x >= 32) return;
     double a = 0.0, b = 0.0;
-    for (int i = 0; i < blocks; ++i) {
+    for (int i = static_cast<int>(threadIdx.x); i < blocks; i += 32) {
         a += partial[2 * i];
         b += partial[2 * i + 1];
     }
-    out[0] = a;
-    out[1] = b;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        a += __shfl_xor_sync(0xffffffffu, a, off);
+        b += __shfl_xor_sync(0xffffffffu, b, off);
+    }
+    if (threadIdx.x == 0) {
+        out[0] = a;
+        out[1] = b;
+    }
 }
 
 // Per-block fp64 (sum, sum of squares) of a float array, grid-stride in index order.
@@ -279,6 +340,29 @@ constexpr size_t kStaticObjectiveSamples = 524288;
 constexpr size_t kStaticObjectiveBlocks = kStaticObjectiveSamples / ppo::kWarps;
 static __device__ __align__(256) double g_objective_scratch[kStaticObjectiveBlocks * ppo::kMetrics];  // 4 MiB
 
+// The library's stream-ordered memory pool on the current device (created once per device and
+// kept until exit), for per-call scratch whose lifetime is one call's stream order. Its release
+// threshold is unbounded, so freed blocks stay in the pool for the next call instead of going
+// back to the driver at every synchronisation.
+cudaMemPool_t scratch_pool() {
+    int device = 0;
+    check(cudaGetDevice(&device), "cudaGetDevice");
+    static std::mutex lock;
+    static cudaMemPool_t pools[128] = {};
+    if (device < 0 || device >= 128) raise(T8B_ECUDA, "device index out of range");
+    std::lock_guard<std::mutex> guard(lock);
+    if (pools[device] == nullptr) {
+        cudaMemPoolProps props{};
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = device;
+        check(cudaMemPoolCreate(&pools[device], &props), "cudaMemPoolCreate");
+        uint64_t keep = UINT64_MAX;
+        check(cudaMemPoolSetAttribute(pools[device], cudaMemPoolAttrReleaseThreshold, &keep), "pool threshold");
+    }
+    return pools[device];
+}
+
 // Device address of the scratch on the current device. The array's name is only a host-side
 // stand-in in host code, so the address is asked for once per device (with that device
 // current) and kept.
@@ -318,15 +402,41 @@ struct t8b_rollout {
     t8b_comm_t comm{};
     bool comm_active() const { return comm.allreduce_sum_f64 != nullptr && comm.world_size > 1; }
 
-    // uint8 masks materialised from the packed ones for the reference view, when stale
-    void expand_masks(cudaStream_t stream) {
+    // One event per step, recorded on the stream of that step's record_policy_device after its
+    // packed masks are written, so the uint8 expansion can wait for them whatever stream
+    // recorded them.
+    std::vector<cudaEvent_t> recorded;
+
+    ~t8b_rollout() {
+        for (cudaEvent_t e : recorded) {
+            if (e != nullptr) cudaEventDestroy(e);
+        }
+    }
+
+    void mark_recorded(size_t step, cudaStream_t stream) {
+        if (recorded.empty()) recorded.assign(horizon, nullptr);
+        if (recorded[step] == nullptr) check(cudaEventCreateWithFlags(&recorded[step], cudaEventDisableTiming), "event");
+        check(cudaEventRecord(recorded[step], stream), "record event");
+    }
+
+    // uint8 masks materialised from the packed ones for the reference view, when stale. The
+    // view has no stream argument (as the reference's device_view), so the expansion waits for
+    // every stale step's recording, runs on the legacy stream and is complete on return; the
+    // per-step flags are set only then.
+    void expand_masks() {
         bool stale = false;
         for (uint8_t b : bytes_current) stale = stale || b == 0;
         if (!stale) return;
         if (masks.size() == 0) masks.allocate(samples * static_cast<size_t>(action_count));
-        launch("k_expand", k_expand, blocks(samples * static_cast<size_t>(action_count), 256), 256, 0, stream, mask_bits.data(),
-               masks.data(), action_count, samples);
+        for (size_t step = 0; step < bytes_current.size(); ++step) {
+            if (bytes_current[step] == 0 && !recorded.empty() && recorded[step] != nullptr) {
+                check(cudaStreamWaitEvent(cudaStreamLegacy, recorded[step], 0), "wait for the recorded masks");
+            }
+        }
+        launch("k_expand", k_expand, blocks(samples * static_cast<size_t>(action_count), 256), 256, 0, cudaStreamLegacy,
+               mask_bits.data(), masks.data(), action_count, samples);
         check(cudaGetLastError(), "expand masks");
+        check(cudaStreamSynchronize(cudaStreamLegacy), "expand masks");
         std::fill(bytes_current.begin(), bytes_current.end(), 1);
     }
 
@@ -403,7 +513,7 @@ int t8b_rollout_destroy(t8b_rollout* r) {
 static int rollout_view(const t8b_rollout* rc, t8b_rollout_view_t* out, bool bytes) {
     t8b_rollout* r = const_cast<t8b_rollout*>(rc);
     return with_rollout(r, [&](t8b_rollout& s) {
-        if (bytes) s.expand_masks(nullptr);
+        if (bytes) s.expand_masks();
         std::memset(out, 0, sizeof *out);
         out->observations = s.observations.data();
         out->action_masks = bytes ? s.masks.data() : nullptr;
@@ -452,6 +562,7 @@ int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* o
             check(cudaGetLastError(), "pack masks");
         }
         s.bytes_current[step] = 0;
+        s.mark_recorded(step, st);
         check(cudaMemcpyAsync(s.actions.data() + at, actions, sizeof(int64_t) * n, cudaMemcpyDeviceToDevice, st), "actions");
         check(cudaMemcpyAsync(s.log_probs.data() + at, log_probabilities, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "lp");
         check(cudaMemcpyAsync(s.values.data() + at, values, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "values");
@@ -489,7 +600,7 @@ int t8b_rollout_compute_gae(t8b_rollout* r, float gamma, float gae_lambda, int n
             raise(T8B_EINVAL, "gamma and gae_lambda must be in [0, 1]");
         }
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        const unsigned grid = blocks(s.envs, kGaeThreads);
+        const unsigned grid = blocks(s.envs, kGaeFights);
         if (s.partial.size() < 2 * static_cast<size_t>(grid)) s.partial.allocate(2 * static_cast<size_t>(grid));
         launch("k_gae", k_gae, grid, kGaeThreads, 0, st, s.rewards.data(), s.values.data(), s.terminated.data(), s.truncated.data(),
                                             s.next_values.data(), s.envs, s.horizon, gamma, gae_lambda, s.advantages.data(),
@@ -592,18 +703,28 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
         if (action_count < 2 || action_count > 32 * kMaxLogitSlots) raise(T8B_EINVAL, "action_count must be 2..512");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         const unsigned grid = blocks(n, ppo::kWarps);
-        Buffer<double> partial;
-        if (metric_sums) partial.allocate(static_cast<size_t>(grid) * ppo::kMetrics);
-        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st, 
+        double* partial = nullptr;
+        if (metric_sums) {
+            // per-block metric partials from the library's stream-ordered pool: no device-wide
+            // synchronisation, and the memory returns to the pool (not the driver) when freed
+            check(cudaMallocFromPoolAsync(reinterpret_cast<void**>(&partial),
+                                          sizeof(double) * static_cast<size_t>(grid) * ppo::kMetrics, scratch_pool(), st),
+                  "PPO objective partials");
+        }
+        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st,
             outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
             1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
-            config->entropy_coefficient, gradients, metric_sums ? partial.data() : nullptr);
-        check(cudaGetLastError(), "PPO objective");
+            config->entropy_coefficient, gradients, partial);
+        const cudaError_t launched = cudaGetLastError();
         if (metric_sums) {
-            launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, partial.data(), static_cast<int>(grid), ppo::kMetrics,
-                                                               metric_sums, 0);
-            check(cudaStreamSynchronize(st), "PPO objective metrics");
+            if (launched == cudaSuccess) {
+                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, partial, static_cast<int>(grid),
+                       ppo::kMetrics, metric_sums, 0);
+            }
+            check(cudaFreeAsync(partial, st), "PPO objective partials");
         }
+        check(launched, "PPO objective");
+        check(cudaGetLastError(), "PPO objective metrics");
     });
 }
 
@@ -615,7 +736,9 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
 // looks up the array's device address (cudaGetSymbolAddress); make that first call before any
 // stream capture. Every call shares the one array, so calls that overlap on the GPU (two
 // streams, two host threads) race on it; each call overwrites the partials it reads, so nothing
-// needs clearing between calls. At most 524,288 samples per call.
+// needs clearing between calls. At most 524,288 samples per call. It returns once the work is
+// queued, so results are ordered on `stream` only. The address is kept per device index, for the device's primary
+// context: `stream` must belong to the current device.
 int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, const int64_t* actions,
                                    const float* old_log_probabilities, const float* old_values, const float* advantages,
                                    const float* returns, size_t n, int action_count, const t8b_ppo_config_t* config,

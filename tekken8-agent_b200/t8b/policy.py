@@ -286,7 +286,7 @@ class GpuRolloutBuffer:
     def tensor(self, name: str) -> torch.Tensor:
         """A zero-copy torch view of one field of the device view ([horizon, envs] or
         [horizon, envs, width])."""
-        v = self.device_view()
+        v = self.device_view(packed=name != "action_masks")  # the uint8 masks are expanded only when asked for
         t, n = self.horizon, self.environments
         spec = {
             "observations": ((t, n, self.config.observation_size), torch.float32),

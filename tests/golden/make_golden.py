@@ -28,7 +28,7 @@ sys.path.insert(0, str(ROOT / "tekken8-agent_b200"))
 
 from oracle import ref  # noqa: E402
 
-GENERATED = "/root/reference/data/generated"
+GENERATED = str(ref.REFERENCE / "data" / "generated")
 
 
 def digest(array: np.ndarray) -> bytes:

@@ -215,7 +215,8 @@ def test_update_stages_match_oracle(cuda, features):
 
 def test_update_gradient_and_adam_end_to_end(cuda, features):
     """A well-conditioned minibatch (eight distinct samples, each repeated) so the batch gradient
-    does not cancel: the whole update's gradient within 3e-2 of float64, and Adam exact in fp32."""
+    does not cancel: the whole update's gradient within 2e-2 of float64 per tensor (north_star's
+    bound for bf16 GEMMs), and Adam exact in fp32."""
     import torch
     from t8b.policy import GpuActorCritic
     rng = np.random.default_rng(13)
@@ -240,7 +241,8 @@ def test_update_gradient_and_adam_end_to_end(cuda, features):
     grads = policy.gradients()
     got = R.unflatten(grads.astype(np.float64), shapes)
     errors = {name: relative(got[name], want[name]) for name, _ in shapes}
-    assert all(e < 3e-2 for e in errors.values()), errors
+    print(f"end-to-end gradient vs float64: {errors}")
+    assert all(e < 2e-2 for e in errors.values()), errors
     after = policy.parameters()
     m1, m2, step = policy.optimizer_state()
     want_p, want_m, want_v, norm = R.adam(before, grads, np.zeros_like(before), np.zeros_like(before), 1, 1e-3, 0.9,
@@ -324,8 +326,40 @@ def test_gae_and_advantage_normalization_config2(cuda):
     assert count == t * n and np.allclose(disc, running, atol=1e-4)
 
 
-def test_ppo_output_gradient_config2(cuda):
-    """The fused objective on raw logits (K = 256 slots, ~30 % legal) against float64."""
+def objective_against_oracle(outputs, masks, actions, old_lp, old_v, adv, ret, grads, sums, config, batch,
+                             chunk=262144):
+    """The GPU objective (grads [n][k + 1], metric sums) against the float64 C restatement
+    (oracle/objective.c), chunk by chunk: relative norms of the logit and value gradients over the
+    samples not within 1e-5 of a gradient discontinuity (the ratio at 1 +- clip, the value delta
+    at +-clip), the metric sums, and the count of such samples."""
+    from oracle import objective
+    n, width = outputs.shape
+    diff = np.zeros(2)
+    norm = np.zeros(2)
+    want_sums = np.zeros(8)
+    margins = 0
+    host = lambda t: t.cpu().numpy()
+    for begin in range(0, n, chunk):
+        end = min(n, begin + chunk)
+        want, margin, part = objective.objective(
+            host(outputs[begin:end]), host(masks[begin:end]), host(actions[begin:end]), host(old_lp[begin:end]),
+            host(old_v[begin:end]), host(adv[begin:end]), host(ret[begin:end]), batch, config.clip_range,
+            config.value_clip_range, config.value_coefficient, config.entropy_coefficient)
+        want_sums += part
+        keep = ~margin
+        margins += int(margin.sum())
+        got = host(grads[begin:end])[keep].astype(np.float64)
+        want = want[keep]
+        diff += [np.square(got[:, :-1] - want[:, :-1]).sum(), np.square(got[:, -1] - want[:, -1]).sum()]
+        norm += [np.square(want[:, :-1]).sum(), np.square(want[:, -1]).sum()]
+    rel = np.sqrt(diff / norm)
+    got_sums = sums.cpu().numpy()
+    return rel, margins, got_sums, want_sums
+
+
+def test_ppo_output_gradient_small_batch(cuda):
+    """The fused objective on raw logits (K = 256 slots, ~30 % legal, the all-masked fallback on 100
+    rows) against float64: relative norm <= 1e-5 (north_star's fp32 bound)."""
     import torch
     from t8b.policy import ppo_output_gradient, ppo_config
     rng = np.random.default_rng(3)
@@ -341,13 +375,51 @@ def test_ppo_output_gradient_config2(cuda):
     ret = rng.normal(size=n).astype(np.float32)
     d = lambda a: torch.as_tensor(a, device="cuda")
     cfg = ppo_config(entropy_coefficient=0.017)
-    grads, sums = ppo_output_gradient(d(logits), d(masks), d(actions), d(old_lp), d(old_v), d(adv), d(ret), cfg)
-    g, dv, m = R.objective_gradient(logits[:, :k].astype(np.float64), masks, actions, old_lp, old_v, adv, ret,
-                                    logits[:, k].astype(np.float64), 0.2, 0.2, 0.5, 0.017, n)
-    got = grads.cpu().numpy()
-    assert np.allclose(got[:, :k], g, rtol=1e-4, atol=1e-10)
-    assert np.allclose(got[:, k], dv, rtol=1e-5, atol=1e-12)
-    s = sums.cpu().numpy()
-    assert abs(s[0] - m["policy_loss"].sum()) <= 1e-4 * np.abs(m["policy_loss"]).sum()
-    assert abs(s[2] - m["entropy"].sum()) <= 1e-4 * m["entropy"].sum()
-    assert s[6] == m["decision"].sum()
+    inputs = [d(a) for a in (logits, masks, actions, old_lp, old_v, adv, ret)]
+    grads, sums = ppo_output_gradient(*inputs, cfg)
+    rel, margins, got, want = objective_against_oracle(*inputs, grads, sums, cfg, n)
+    assert rel[0] <= 1e-5 and rel[1] <= 1e-5, (rel, margins)
+    assert margins <= 4, margins
+    for index in (0, 1, 2, 3, 7):
+        assert abs(got[index] - want[index]) <= 1e-5 * abs(want[index]), (index, got[index], want[index])
+    assert abs(got[4] - want[4]) <= margins and got[6] == want[6]
+    assert np.all(grads.cpu().numpy()[np.arange(100), 1:k] == 0.0)
+
+
+def test_gae_and_objective_full_config2_rollout(cuda):
+    """BASELINE config 2 at full size: T = 128 x N = 32,768 (4,194,304 samples), K = 256 slots,
+    seed 1 (t8b.workloads.config2_rollout). GAE against float64 within the reference test's 2e-5
+    (tests/rollout_tests.cpp:75-93), its normalisation within 1e-5, then the fp32 objective over all
+    4.19 M samples with the normalised advantages against the float64 C restatement: relative norm
+    of the logit and of the value gradient <= 1e-5 (north_star's fp32 bound), metric sums within
+    1e-5. Samples within 1e-5 of a gradient discontinuity are left out of the norms (a float32 and
+    a float64 evaluation may take different branches there); there are at most a few."""
+    import torch
+    from t8b.policy import GpuRolloutBuffer, ppo_config, ppo_output_gradient
+    from t8b.workloads import config2_rollout
+    w = config2_rollout()
+    buf = GpuRolloutBuffer(w.envs, w.horizon)
+    for name, src in (("rewards", w.rewards), ("old_values", w.values), ("next_values", w.next_values),
+                      ("terminated", w.terminated), ("truncated", w.truncated)):
+        buf.tensor(name).copy_(src)
+    buf.compute_gae(0.99, 0.95, normalize=False)
+    host = lambda t: t.cpu().numpy()
+    want_adv, want_ret = R.gae(host(w.rewards), host(w.values), host(w.terminated), host(w.truncated),
+                               host(w.next_values), 0.99, 0.95)
+    assert np.abs(host(buf.tensor("advantages")) - want_adv).max() < 2e-5
+    assert np.abs(host(buf.tensor("returns")) - want_ret).max() < 2e-5
+    buf.compute_gae(0.99, 0.95, normalize=True)
+    adv = buf.tensor("advantages").reshape(-1)
+    ret = buf.tensor("returns").reshape(-1)
+    norm_want = R.normalize_advantages(want_adv).reshape(-1)
+    assert np.linalg.norm(host(adv) - norm_want) <= 1e-5 * np.linalg.norm(norm_want)
+    cfg = ppo_config(entropy_coefficient=0.01)
+    inputs = (w.outputs, w.masks, w.actions, w.old_log_probabilities, w.values.reshape(-1), adv, ret)
+    grads, sums = ppo_output_gradient(*inputs, cfg)
+    torch.cuda.synchronize()
+    rel, margins, got, want = objective_against_oracle(*inputs, grads, sums, cfg, w.samples)
+    assert rel[0] <= 1e-5 and rel[1] <= 1e-5, (rel, margins)
+    assert margins <= 16, margins
+    for index in (0, 1, 2, 3, 7):
+        assert abs(got[index] - want[index]) <= 1e-5 * abs(want[index]), (index, got[index], want[index])
+    assert abs(got[4] - want[4]) <= margins and got[6] == want[6]

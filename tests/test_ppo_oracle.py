@@ -102,3 +102,34 @@ def test_gae_matches_the_reference_scalar_loop():
 def test_uniform01_is_the_reference_bit_recipe():
     u = R.uniform01(2028, 7, 3)
     assert 0.0 < u < 1.0 and u.dtype == np.float32
+
+
+def test_c_objective_equals_the_numpy_restatement():
+    """oracle/objective.c (float64, used at full config-2 size) against objective_gradient above on
+    a mixed batch: legal sets of every density, the all-masked fallback, clipped and unclipped
+    ratios and values."""
+    from oracle import objective
+    rng = np.random.default_rng(11)
+    n, k = 3000, 40
+    out = rng.normal(size=(n, k + 1)).astype(np.float32)
+    masks = (rng.random((n, k)) < rng.random((n, 1))).astype(np.uint8)
+    masks[:20] = 0
+    legal = R.legal_set(masks)
+    actions = np.array([rng.choice(np.nonzero(m)[0]) for m in legal], np.int64)
+    old_lp = (rng.normal(scale=0.3, size=n) - 3.0).astype(np.float32)
+    old_v = rng.normal(size=n).astype(np.float32)
+    adv = rng.normal(size=n).astype(np.float32)
+    ret = rng.normal(size=n).astype(np.float32)
+    f32 = lambda v: float(np.float32(v))  # the C oracle takes the float32 config values, as the kernel does
+    g, dv, m = R.objective_gradient(out[:, :k].astype(np.float64), masks, actions, old_lp, old_v, adv, ret,
+                                    out[:, k].astype(np.float64), f32(CLIP), f32(VCLIP), f32(VCOEF), f32(ECOEF), n)
+    got, margin, sums = objective.objective(out, masks, actions, old_lp, old_v, adv, ret, n, CLIP, VCLIP, VCOEF, ECOEF,
+                                            threads=3)
+    # summation order differs (numpy sums pairwise): equal to float64 rounding of the whole array
+    assert np.linalg.norm(got[:, :k] - g) <= 1e-9 * np.linalg.norm(g)
+    assert np.linalg.norm(got[:, k] - dv) <= 1e-12 * np.linalg.norm(dv)
+    for index, key in enumerate(("policy_loss", "value_loss", "entropy", "kl", "clip")):
+        assert abs(sums[index] - m[key].sum()) <= 1e-10 * max(1.0, np.abs(m[key]).sum()), key
+    assert sums[6] == m["decision"].sum()
+    assert abs(sums[7] - m["decision_entropy"].sum()) <= 1e-10 * m["decision_entropy"].sum()
+    assert margin.sum() < n // 100

@@ -6,9 +6,9 @@ Tolerances: the reference runs with matmul_precision "bf16" (multiply inputs rou
 fp32 accumulation in cuBLAS), the library on tcgen05 with the same rounding and its own
 accumulation order and tanh; network outputs agree within 2e-2 (relative norm), sampled
 actions in at least 98 % of samples (a different last bit moves a few inverse-CDF
-boundaries), and one well-conditioned PPO update's parameter change and gradient norm within
-5e-2 (relative norm). Initial weights, checkpoint files and GAE are compared exactly or to
-fp32 rounding."""
+boundaries), and minibatch gradients, Adam moments and update metrics within 2e-2 (north_star's
+bound for bf16 GEMMs) at default settings. Initial weights, checkpoint files and GAE are
+compared exactly; normalised advantages to 1e-6."""
 import numpy as np
 import pytest
 
@@ -173,28 +173,22 @@ def test_forward_matches_the_reference(cuda, ref, features, tmp_path, shape):
         assert relative(lp[same], want["log_probabilities"][same]) < 2e-2
 
 
-@pytest.mark.parametrize("shape", sorted(SHAPES))
-def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
-    """One update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
-    weights on the same rollout agrees with the reference's. The comparison is made well
-    conditioned: advantages are all positive and returns sit above the values, so the batch
-    gradient does not cancel, and Adam's epsilon is 1, which keeps the step near-linear in the
-    gradient (with the default 1e-5 the first Adam steps are close to lr * sign(gradient), and
-    the sign of near-zero components is rounding noise in either implementation)."""
+def reference_setup(ref, features, tmp_path, shape, n, seed, scale):
+    """The same starting weights in the library and the reference (through a checkpoint), and a
+    minibatch sampled from that policy: old log-probabilities off by N(0, 0.05), advantages
+    N(0, 1) of both signs, returns scattered N(0, 0.5) around the values."""
     import torch
-    from t8b.policy import GpuActorCritic, actor_config, ppo_config
+    from t8b.policy import GpuActorCritic, actor_config
     from test_ppo_gpu import view_of
-    n = 8192
-    rng = np.random.default_rng(31)
+    rng = np.random.default_rng(seed)
     overrides, feats, obs, tables, masks = shaped(shape, features, rng, n)
     actor = actor_config(**overrides)
     ours = GpuActorCritic(n, actor, seed=7)
     ours.set_action_feature_tables(feats)
     outputs = actor.action_feature_size + 1
     p = ours.parameters()
-    p[-(actor.hidden_size * outputs + outputs):] *= 30.0 if shape == "full_move" else 3.0
+    p[-(actor.hidden_size * outputs + outputs):] *= scale
     ours.set_parameters(p)
-    before = ours.parameters().astype(np.float64)
     ours.save_checkpoint(tmp_path / "start.t8ppo")
     theirs = ref.RefPolicy(ref.config_from(actor), n, 1)
     theirs.set_features(feats)
@@ -204,32 +198,98 @@ def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
     actions = out["actions"].cpu().numpy()
     old_lp = out["log_probabilities"].cpu().numpy() - rng.normal(scale=0.05, size=n).astype(np.float32)
     old_v = out["values"].cpu().numpy()
-    adv = (np.abs(rng.normal(size=n)) + 0.5).astype(np.float32)
-    ret = (old_v + 1.0).astype(np.float32)
+    adv = rng.normal(size=n).astype(np.float32)
+    ret = (old_v + rng.normal(scale=0.5, size=n)).astype(np.float32)
     view, keep = view_of((obs, tables, masks, actions, old_lp, old_v, adv, ret))
-    cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3, adam_epsilon=1.0)
-    got = ours.update_ppo(view, cfg, shuffle_seed=17)
     zeros_f = torch.zeros(n, device="cuda")
     zeros_b = torch.zeros(n, dtype=torch.uint8, device="cuda")
     obs_t, masks_t, actions_t, lp_t, v_t, adv_t, ret_t, tables_t = keep
     pointers = [obs_t.data_ptr(), masks_t.data_ptr(), actions_t.data_ptr(), lp_t.data_ptr(), v_t.data_ptr(),
                 zeros_f.data_ptr(), zeros_b.data_ptr(), zeros_b.data_ptr(), zeros_f.data_ptr(), adv_t.data_ptr(),
                 ret_t.data_ptr(), tables_t.data_ptr(), None]
-    ppo = ref.Ppo(cfg.epochs, cfg.minibatch_size, cfg.learning_rate, cfg.clip_range, cfg.value_clip_range,
-                  cfg.target_kl, cfg.value_coefficient, cfg.entropy_coefficient, cfg.max_gradient_norm,
-                  cfg.adam_beta1, cfg.adam_beta2, cfg.adam_epsilon)
-    want = theirs.update(pointers, n, 1, n, ppo, 17)
-    theirs.save(tmp_path / "after.t8ppo")
-    after = GpuActorCritic(256, actor, seed=3)
-    after.load_checkpoint(tmp_path / "after.t8ppo")
-    delta_ref = after.parameters().astype(np.float64) - before
-    delta_ours = ours.parameters().astype(np.float64) - before
-    assert relative(delta_ours, delta_ref) < 5e-2, relative(delta_ours, delta_ref)
-    for key in ("policy_loss", "value_loss", "entropy", "clip_fraction", "decision_fraction"):
-        assert abs(got[key] - want[key]) <= 2e-2 * max(1.0, abs(want[key])), (key, got[key], want[key])
-    # the pre-clip norm of the minibatch gradients, dominated by bf16-rounded activations
-    assert abs(got["gradient_norm"] - want["gradient_norm"]) <= 5e-2 * want["gradient_norm"]
-    assert got["minibatches"] == want["minibatches"] == 8
+    return actor, ours, theirs, view, (keep, zeros_f, zeros_b), pointers
+
+
+def reference_ppo(ref, cfg):
+    return ref.Ppo(cfg.epochs, cfg.minibatch_size, cfg.learning_rate, cfg.clip_range, cfg.value_clip_range,
+                   cfg.target_kl, cfg.value_coefficient, cfg.entropy_coefficient, cfg.max_gradient_norm,
+                   cfg.adam_beta1, cfg.adam_beta2, cfg.adam_epsilon)
+
+
+def reference_first_moment(actor, theirs, path):
+    """The reference's Adam first moment, read back through its checkpoint."""
+    from t8b.policy import GpuActorCritic
+    theirs.save(path)
+    back = GpuActorCritic(256, actor, seed=3)
+    back.load_checkpoint(path)
+    m1, m2, step = back.optimizer_state()
+    return back, m1.astype(np.float64), m2.astype(np.float64), step
+
+
+def per_tensor(actor, a, b):
+    from oracle import ppo_ref as R
+    shapes = R.layout(actor.observation_size, actor.hidden_size, actor.shared_layers, actor.action_feature_size + 1)
+    ua, ub = R.unflatten(np.asarray(a, np.float64), shapes), R.unflatten(np.asarray(b, np.float64), shapes)
+    return {name: relative(ua[name], ub[name]) for name, _ in shapes}
+
+
+@pytest.mark.parametrize("shape, n", [("full_move", 524288), ("config3", 32768)])
+def test_minibatch_gradient_matches_the_reference(cuda, ref, features, tmp_path, shape, n):
+    """The pre-Adam gradient of one minibatch against the reference's own update_ppo in its bf16
+    matmul mode, at default settings (Adam epsilon 1e-5, the default norm clip, mixed-sign
+    advantages): every parameter tensor within 2e-2 relative norm (north_star's bound for bf16
+    GEMMs), and the gradient norm within 2e-2. At 524,288 rows (config 4's minibatch) the
+    library's weight gradients take the split-K path; 32,768 is config 3's batch. The reference's
+    gradient g is read back from its first Adam moment: with zero initial moments one step stores
+    m1 = (1 - beta1) * s * g, where s = max_norm / |g| when |g| exceeds max_norm (src/ppo.cu:
+    710-736)."""
+    from t8b.policy import ppo_config
+    actor, ours, theirs, view, keep, pointers = reference_setup(ref, features, tmp_path, shape, n, 31,
+                                                                30.0 if shape == "full_move" else 3.0)
+    cfg = ppo_config(epochs=1, minibatch_size=n, target_kl=0.0)
+    got = ours.update_ppo(view, cfg, shuffle_seed=17)
+    g_ours = ours.gradients().astype(np.float64)
+    want = theirs.update(pointers, n, 1, n, reference_ppo(ref, cfg), 17)
+    _, m1, _, step = reference_first_moment(actor, theirs, tmp_path / "after.t8ppo")
+    assert step == 1 and got["minibatches"] == want["minibatches"] == 1
+    norm = np.float32(want["gradient_norm"])
+    scale = np.float32(cfg.max_gradient_norm) / norm if norm > np.float32(cfg.max_gradient_norm) else np.float32(1)
+    g_ref = m1 / float(np.float32(1) - np.float32(cfg.adam_beta1)) / float(scale)
+    errors = per_tensor(actor, g_ours, g_ref)
+    print(f"gradient vs reference ({shape}, {n} rows): {errors}, norm {got['gradient_norm']} vs {norm}")
+    assert all(e <= 2e-2 for e in errors.values()), errors
+    assert abs(got["gradient_norm"] - want["gradient_norm"]) <= 2e-2 * want["gradient_norm"]
+    for key in ("policy_loss", "value_loss", "entropy", "approximate_kl", "clip_fraction", "decision_fraction"):
+        assert abs(got[key] - want[key]) <= 2e-2 * max(abs(want[key]), 1e-2), (key, got[key], want[key])
+
+
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
+    """A whole update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
+    weights on the same rollout, at default settings (Adam epsilon 1e-5, mixed-sign advantages):
+    the metrics and the mean minibatch gradient norm within 2e-2, and both Adam moments after the
+    eight steps (running averages of the eight gradients and of their squares) within 2e-2
+    relative norm per tensor. The parameter change itself is not compared: with epsilon 1e-5 the
+    first Adam steps move every weight by close to lr * sign(gradient), and the sign of a
+    near-zero gradient component is bf16 rounding noise in either implementation."""
+    from t8b.policy import ppo_config
+    n = 8192
+    actor, ours, theirs, view, keep, pointers = reference_setup(ref, features, tmp_path, shape, n, 31,
+                                                                30.0 if shape == "full_move" else 3.0)
+    cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3)
+    got = ours.update_ppo(view, cfg, shuffle_seed=17)
+    want = theirs.update(pointers, n, 1, n, reference_ppo(ref, cfg), 17)
+    after, m1_ref, m2_ref, step = reference_first_moment(actor, theirs, tmp_path / "after.t8ppo")
+    m1, m2, our_step = ours.optimizer_state()
+    assert step == our_step == 8 and got["minibatches"] == want["minibatches"] == 8
+    e1, e2 = per_tensor(actor, m1, m1_ref), per_tensor(actor, m2, m2_ref)
+    delta = ours.parameters().astype(np.float64) - after.parameters().astype(np.float64)
+    print(f"update vs reference ({shape}): m1 {e1}, m2 {e2}, parameters differ by {np.abs(delta).max()}")
+    assert all(e <= 2e-2 for e in e1.values()), e1
+    assert all(e <= 2e-2 for e in e2.values()), e2
+    for key in ("policy_loss", "value_loss", "entropy", "approximate_kl", "clip_fraction", "decision_fraction",
+                "gradient_norm"):
+        assert abs(got[key] - want[key]) <= 2e-2 * max(abs(want[key]), 1e-2), (key, got[key], want[key])
     mean_ours = ours.observation_statistics()[0]
     mean_ref = theirs.observation_statistics()[0]
     assert np.allclose(mean_ours, mean_ref, rtol=1e-5, atol=1e-6)
@@ -258,6 +318,19 @@ def test_gae_and_reward_normalisation_match_the_reference(cuda, ref):
     for step in range(t):
         ours.record_policy_device(step, obs, masks, actions, lp, values[step])
         theirs.record_policy(step, obs, masks, actions, lp, values[step])
+    # GAE on the raw rewards: the same fp32 recurrence in the same order as gae_kernel
+    # (src/ppo.cu:2003-2029), so advantages and returns are bit-identical
+    ours.compute_gae(0.99, 0.95, False)
+    theirs.compute_gae(0.99, 0.95, False)
+    adv_ref, ret_ref, _ = theirs.download()
+    assert np.array_equal(ours.tensor("advantages").cpu().numpy(), adv_ref)
+    assert np.array_equal(ours.tensor("returns").cpu().numpy(), ret_ref)
+    # normalised: the fp64 moments are summed in another order; the float results agree to 1e-6
+    ours.compute_gae(0.99, 0.95, True)
+    theirs.compute_gae(0.99, 0.95, True)
+    adv_ref, _, _ = theirs.download()
+    adv_ours = ours.tensor("advantages").cpu().numpy()
+    assert np.abs(adv_ours - adv_ref).max() <= 1e-6 * np.abs(adv_ref).max()
     std_ours = ours.normalize_rewards(0.99)
     std_ref = theirs.normalize_rewards(0.99)
     assert abs(std_ours - std_ref) <= 1e-6 * abs(std_ref)
@@ -265,5 +338,6 @@ def test_gae_and_reward_normalisation_match_the_reference(cuda, ref):
     theirs.compute_gae(0.99, 0.95, True)
     adv_ref, ret_ref, rew_ref = theirs.download()
     assert np.allclose(ours.tensor("rewards").cpu().numpy(), rew_ref, rtol=1e-6, atol=1e-7)
-    assert np.allclose(ours.tensor("advantages").cpu().numpy(), adv_ref, rtol=1e-4, atol=1e-5)
-    assert np.allclose(ours.tensor("returns").cpu().numpy(), ret_ref, rtol=1e-4, atol=1e-5)
+    # after reward normalisation (the scale agrees to 1e-6), within 1e-6 relative to the largest
+    assert np.abs(ours.tensor("advantages").cpu().numpy() - adv_ref).max() <= 1e-6 * np.abs(adv_ref).max()
+    assert np.abs(ours.tensor("returns").cpu().numpy() - ret_ref).max() <= 1e-6 * np.abs(ret_ref).max()

@@ -51,6 +51,33 @@ def test_static_scratch_objective_matches_allocating_entry_point(cuda):
         assert torch.isfinite(got_g).all()
 
 
+def test_static_entry_point_allocates_nothing(cuda):
+    """After a first call (which looks the array up and loads the kernel), further calls leave the
+    device's free memory unchanged; without metric sums the gradients are unchanged too."""
+    import torch
+    from t8b.policy import ppo_config
+    config = ppo_config()
+    k = 256
+    tensors = batch(131_072, k, seed=7)
+    want_g, _ = call("t8b_ppo_output_gradient", tensors, k, config, True)
+    call("t8b_ppo_output_gradient_static", tensors, k, config, True)
+    grads = torch.empty_like(want_g)
+    sums = torch.empty(8, dtype=torch.float64, device="cuda")
+    from t8b import _lib
+    lib = _lib.lib()
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for metrics in (True, False, True):
+        status = lib.t8b_ppo_output_gradient_static(*[t.data_ptr() for t in tensors], tensors[0].shape[0], k,
+                                                    C.byref(config), grads.data_ptr(),
+                                                    sums.data_ptr() if metrics else None, None)
+        assert status == 0, lib.t8b_last_error()
+        torch.cuda.synchronize()
+        assert torch.allclose(grads, want_g, rtol=1e-6, atol=0.0)
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+
+
 def test_static_entry_point_rejects_sizes_beyond_its_scratch(cuda):
     import torch
     from t8b import _lib
