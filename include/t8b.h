@@ -455,6 +455,15 @@ int t8b_policy_download_outputs(t8b_policy* policy, float* host, size_t n);
  * 1 hidden activation, 2 its pre-activation gradient, 3 output-layer gradient). */
 int t8b_policy_download_activation(t8b_policy* policy, int which, int layer, float* host, size_t n);
 int t8b_policy_synchronize(t8b_policy* policy, void* stream);
+/* config  ppo.hpp:127: the configuration in force (load_checkpoint adopts the file's
+ * observation_normalization). */
+int t8b_policy_get_config(const t8b_policy* policy, t8b_actor_config_t* out);
+/* Test aid behind debug_backprop_relative_error (ppo.hpp:139-142): the network alone on n device
+ * observations (normalised as forward does). Writes the raw outputs [n][feature_size + 1] to
+ * `outputs` (device, may be NULL); with `output_gradients` (device [n][feature_size + 1] fp32)
+ * runs the backward pass from them into the gradient buffer (t8b_policy_get_gradients). */
+int t8b_policy_debug_network(t8b_policy* policy, const float* observations, size_t n, const float* output_gradients,
+                             float* outputs, void* stream);
 
 /* debug_ppo_objective_gradient (include/t8_v2/ppo.hpp:100-108), batched: d(objective)/d(logits,
  * value) of the clipped PPO objective for raw [n][k + 1] outputs. Device pointers. metric_sums

@@ -83,6 +83,17 @@ std::vector<float> xavier(int rows, int cols, std::mt19937_64& random, float dev
 
 using namespace t8b;
 
+namespace t8b {
+// [n][cols] fp32 rows into a zero-padded [n][ld] bf16 operand.
+__global__ void k_rows_to_bf16(const float* in, size_t n, int cols, bf16* out, int ld) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n * static_cast<size_t>(ld)) return;
+    const size_t row = i / static_cast<size_t>(ld);
+    const int col = static_cast<int>(i % static_cast<size_t>(ld));
+    out[i] = __float2bfloat16_rn(col < cols ? in[row * static_cast<size_t>(cols) + col] : 0.0f);
+}
+}  // namespace t8b
+
 struct t8b_policy {
     t8b_actor_config_t config{};
     size_t capacity = 0;
@@ -1236,6 +1247,49 @@ int t8b_policy_download_activation(t8b_policy* p, int which, int layer, float* h
         std::vector<bf16> rows(n * width);
         check(cudaMemcpy(rows.data(), src, rows.size() * sizeof(bf16), cudaMemcpyDeviceToHost), "download activation");
         for (size_t i = 0; i < rows.size(); ++i) host[i] = __bfloat162float(rows[i]);
+    });
+}
+
+// The actor configuration in force (load_checkpoint adopts the file's normaliser setting).
+int t8b_policy_get_config(const t8b_policy* p, t8b_actor_config_t* out) {
+    return with_policy(const_cast<t8b_policy*>(p), [&](t8b_policy& s) {
+        if (out == nullptr) raise(T8B_EINVAL, "null argument");
+        *out = s.config;
+    });
+}
+
+// The network alone on n device observations (normalised as forward does): raw outputs
+// [n][outputs] into `outputs` when given, and with `output_gradients` ([n][outputs] fp32) the
+// backward pass from them into the gradient buffer (t8b_policy_get_gradients).
+int t8b_policy_debug_network(t8b_policy* p, const float* observations, size_t n, const float* output_gradients,
+                             float* outputs, void* stream) {
+    return with_policy(p, [&](t8b_policy& s) {
+        if (observations == nullptr || n == 0 || n > s.capacity) raise(T8B_EINVAL, "debug batch must fit the capacity");
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        ppo::Prep prep{};
+        prep.obs = observations;
+        prep.width = s.width;
+        prep.padded = s.padded;
+        prep.mean = s.obs_mean.data();
+        prep.istd = s.obs_istd.data();
+        prep.clip = s.config.observation_clip;
+        prep.normalize = s.normalizing() ? 1 : 0;
+        prep.count = n;
+        prep.x = s.x.data();
+        launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
+        check(cudaGetLastError(), "prepare inputs");
+        s.network(n, st);
+        if (outputs != nullptr) {
+            check(cudaMemcpy2DAsync(outputs, sizeof(float) * s.outputs, s.out.data(), sizeof(float) * kOutPad,
+                                    sizeof(float) * s.outputs, n, cudaMemcpyDeviceToDevice, st), "network outputs");
+        }
+        if (output_gradients != nullptr) {
+            launch("k_rows_to_bf16", k_rows_to_bf16, blocks(n * kOutPad, 256), 256, 0, st, output_gradients, n, s.outputs,
+                   s.dout.data(), kOutPad);
+            s.column_sums(output_gradients, static_cast<int>(n), s.outputs, s.outputs, s.grads.data() + s.b_off[s.layers], st);
+            s.backward(n, st);
+        }
+        s.sync_error(st);
     });
 }
 
