@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--comm", choices=("native", "torch"), default="native",
+                    help="data-parallel exchanges: the library's NCCL communicator (native) or torch.distributed")
     ap.add_argument("--self-play", action="store_true",
                     help="mirror self-play: a frozen copy of the initial policy plays the other side")
     ap.add_argument("--workload", choices=("iteration", "mlp", "gae_loss", "engine"), default="iteration",
@@ -257,8 +259,10 @@ def run_ours(args):
         import torch.distributed as dist
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device(f"cuda:{local}"))
-        from t8b.policy import TorchComm
-        comm = TorchComm()
+        from t8b.policy import NativeComm, TorchComm
+        # native: the library's own NCCL communicator, all-reduces queued from C on its stream;
+        # torch: the same hooks through torch.distributed (a Python callback per exchange)
+        comm = NativeComm() if args.comm == "native" else TorchComm()
     from t8b import roster as roster_module
     from t8b.train import SelfPlayTrainer
     from t8b.sim import GpuFullMoveSimulator  # noqa: F401  (loads the library)
@@ -358,7 +362,8 @@ def run_ours(args):
                                ("mirror self-play against a frozen policy" if args.self_play else "scripted opponents"),
                    "envs_per_gpu": args.envs, "horizon": args.horizon, "epochs": args.epochs,
                    "minibatch": args.envs * args.horizon // args.minibatches, "parallelism": f"dp{world}",
-                   "l2": "inputs larger than L2 (rollout buffers > 4 GB per GPU)", "target_kl": "off (full 4 epochs)"},
+                   "l2": "inputs larger than L2 (rollout buffers > 4 GB per GPU)", "target_kl": "off (full 4 epochs)",
+                   "comm": args.comm if world > 1 else None},
         "phases_ms_per_step": {"rollout": rollout_total / args.steps,
                                "gae_and_update": (total_device - rollout_total) / args.steps},
         "engine_frames_per_s": frames / (total_device / 1000.0) * world,
@@ -381,6 +386,9 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
+        if hasattr(comm, "close"):
+            torch.cuda.synchronize()
+            comm.close()
         torch.distributed.destroy_process_group()
 
 

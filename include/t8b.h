@@ -397,6 +397,21 @@ typedef struct t8b_comm {
     int32_t world_size, rank;
 } t8b_comm_t;
 
+/* A native communicator for t8b_comm_t (no reference counterpart): NCCL (loaded at run time,
+ * libnccl.so.2) over the ranks of one job, one process per GPU. Rank 0 makes the 128-byte unique
+ * id with t8b_comm_unique_id and hands it to every rank by any means (a file, a socket, an MPI
+ * broadcast); each rank, with its device current, calls t8b_comm_init with it, which fills `out`
+ * with hooks that sum over the ranks with ncclAllReduce on the library's stream (the host never
+ * waits). Set `out` on the policy and the rollout buffer (t8b_policy_set_comm,
+ * t8b_rollout_set_comm). A hook that fails records the error; t8b_comm_status reports it and
+ * NCCL's asynchronous errors. t8b_comm_destroy frees the communicator (after its last use on the
+ * GPU) and zeroes `comm`. */
+int t8b_comm_unique_id(void* id, size_t size);
+int t8b_comm_init(const void* id, size_t size, int world_size, int rank, t8b_comm_t* out);
+int t8b_comm_status(const t8b_comm_t* comm);
+int t8b_comm_allreduce_sum_f32(const t8b_comm_t* comm, float* data, size_t count, void* stream);
+int t8b_comm_destroy(t8b_comm_t* comm);
+
 void t8b_actor_config_default(t8b_actor_config_t* out); /* full-move defaults of the trainer */
 void t8b_ppo_config_default(t8b_ppo_config_t* out);
 

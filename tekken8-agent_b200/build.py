@@ -44,7 +44,7 @@ def build(verbose: bool = False) -> Path:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
     if not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objects):
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-lcudart", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objects), "-lcudart", "-lcuda", "-ldl"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

@@ -350,6 +350,13 @@ PROTOTYPES.update({
                                                       C.POINTER(C.c_double), vp]),
     "t8b_rollout_restore_return_normalizer_state": (C.c_int, [vp, u64, C.c_double, C.c_double, vp]),
     "t8b_rollout_set_comm": (C.c_int, [vp, C.POINTER(Comm)]),
+    "t8b_comm_unique_id": (C.c_int, [vp, C.c_size_t]),
+    "t8b_comm_init": (C.c_int, [vp, C.c_size_t, C.c_int, C.c_int, C.POINTER(Comm)]),
+    "t8b_comm_status": (C.c_int, [C.POINTER(Comm)]),
+    "t8b_comm_allreduce_sum_f32": (C.c_int, [C.POINTER(Comm), vp, C.c_size_t, vp]),
+    "t8b_comm_destroy": (C.c_int, [C.POINTER(Comm)]),
+    "t8b_policy_get_config": (C.c_int, [vp, C.POINTER(ActorConfig)]),
+    "t8b_policy_debug_network": (C.c_int, [vp, vp, C.c_size_t, vp, vp, vp]),
     "t8b_collect_rollout": (C.c_int, [vp, vp, vp, vp, u64, u64, C.c_size_t, C.c_float, vp]),
     "t8b_rollout_synchronize": (C.c_int, [vp, vp]),
 })

@@ -91,6 +91,32 @@ class TorchComm:
             self.dist.all_reduce(tensor, op=self.dist.ReduceOp.SUM, group=self.group)
 
 
+class NativeComm:
+    """t8b_comm_t from the library's own NCCL communicator (t8b_comm_init): the all-reduces are
+    queued in C on the library's stream, with no Python between the kernels. torch.distributed
+    (any backend) only carries rank 0's 128-byte unique id to the other ranks."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        box = [None]
+        if self.rank == 0:
+            raw = (C.c_char * 128)()
+            call("t8b_comm_unique_id", raw, 128)
+            box[0] = bytes(raw)
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group is not None else 0, group=group)
+        self.struct = Comm()
+        call("t8b_comm_init", box[0], 128, self.world, self.rank, C.byref(self.struct))
+
+    def status(self):
+        call("t8b_comm_status", C.byref(self.struct))
+
+    def close(self):
+        if self.struct.user:
+            call("t8b_comm_destroy", C.byref(self.struct))
+
+
 class GpuActorCritic:
     def __init__(self, capacity: int, config: ActorConfig | None = None, seed: int = 2027):
         self.config = config if config is not None else actor_config()

@@ -96,6 +96,23 @@ def main():
     for r in range(1, world):
         assert np.array_equal(params[0], params[r]), f"rank {r} parameters diverged"
         assert np.array_equal(mean[0], mean[r]), f"rank {r} normaliser diverged"
+
+    # the library's own NCCL communicator (t8b_comm_init) gives the same replicas as the
+    # torch.distributed hooks: the same sums in the same order, queued from C
+    from t8b.policy import NativeComm
+    native = NativeComm()
+    twin = GpuActorCritic(n, seed=33)
+    twin.set_action_feature_tables(features)
+    twin.set_comm(native)
+    for update in range(3):
+        arrays = rollout_inputs(twin, features, n, np.random.default_rng(100 + 10 * rank + update))
+        view, keep = view_of(arrays)
+        twin.update_ppo(view, cfg, shuffle_seed=50 + update)
+    torch.cuda.synchronize()
+    native.status()
+    assert np.array_equal(twin.parameters(), policy.parameters()), "native communicator differs from torch's"
+    assert np.array_equal(twin.observation_statistics()[0], policy.observation_statistics()[0])
+    native.close()
     dist.barrier()
     if rank == 0:
         print("DP OK", flush=True)

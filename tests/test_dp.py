@@ -57,6 +57,22 @@ def test_comm_hooks_sum_over_gloo_ranks():
         assert np.array_equal(f64, np.full(7, 2.0))
 
 
+def test_native_communicator_makes_unique_ids_without_a_gpu():
+    """t8b_comm_unique_id loads NCCL at run time and makes the 128-byte id rank 0 hands to the
+    others; a smaller buffer and a null communicator are refused."""
+    import ctypes as C
+    sys.path.insert(0, str(ROOT / "tekken8-agent_b200"))
+    from t8b import _lib
+    lib = _lib.lib()
+    first, second = (C.c_char * 128)(), (C.c_char * 128)()
+    assert lib.t8b_comm_unique_id(first, 128) == 0, lib.t8b_last_error()
+    assert lib.t8b_comm_unique_id(second, 128) == 0
+    assert bytes(first) != bytes(second) and any(bytes(first))
+    assert lib.t8b_comm_unique_id(first, 64) == _lib.T8B_EINVAL
+    assert lib.t8b_comm_status(None) == _lib.T8B_EINVAL
+    assert lib.t8b_comm_destroy(None) == 0
+
+
 def _max_rank(rank, world, port, out):
     sys.path.insert(0, str(ROOT))
     import torch.distributed as dist
