@@ -465,47 +465,68 @@ __host__ __device__ inline uint64_t fight_hash(const Fight& s) {
     return h;
 }
 
-__host__ __device__ inline Input random_legal(const Match& m, const Fight& s, int p, Pcg32& rng) {
+// A uniformly random legal candidate (the harness's pick, tests/full_combat_random_play.hpp), with
+// the candidate scan spread over a warp: every lane holds the same fight, lane
+// l checks candidates l, l + 32, ...; the legal set is 12 ballot words, and the draw (the same
+// PCG32 call on every lane) picks the same candidate index the scalar scan would.
+__device__ __forceinline__ Input random_legal_warp(const Match& m, const Fight& s, int p, Pcg32& rng, int lane) {
     const DCharacter& ch = *m.side[p];
+    constexpr int kWords = (T8B_MAX_CANDIDATES + 31) / 32;
+    uint32_t bits[kWords];
     int legal = 0;
-    for (int c = 0; c < ch.candidate_count; ++c) legal += candidate_ok(m, s, p, c) ? 1 : 0;
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+        const int c = w * 32 + lane;
+        const bool ok = c < ch.candidate_count && candidate_ok(m, s, p, c);
+        bits[w] = __ballot_sync(0xffffffffu, ok);
+        legal += __popc(bits[w]);
+    }
     Input in{-1, kIdle};
     if (legal == 0) return in;
     int pick = static_cast<int>(rng.below(static_cast<uint32_t>(legal)));
-    for (int c = 0; c < ch.candidate_count; ++c) {
-        if (!candidate_ok(m, s, p, c)) continue;
-        if (pick-- == 0) {
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) {
+        const int count = __popc(bits[w]);
+        if (pick < count) {
+            uint32_t word = bits[w];
+            for (int k = 0; k < pick; ++k) word &= word - 1;  // drop the lowest `pick` set bits
+            const int c = w * 32 + (__ffs(static_cast<int>(word)) - 1);
             if (!to_input(ch, c, in)) in = Input{-1, kIdle};
             return in;
         }
+        pick -= count;
     }
     return in;
 }
 
+// The engine-parity workload, one warp per fight. All lanes step the same state (control flow is
+// the same on every lane, so the warp never diverges in the frame step), the decisions' legality
+// scans are shared out over the lanes, and lane 0 writes the frame's hash. 1,024 fights are 1,024
+// warps (about 7 per SM) instead of 32.
 __global__ void __launch_bounds__(kStepThreads) k_random_play(SimView v, int fights, const int32_t* p1,
                                                                 const int32_t* p2, const double* x1, const double* x2,
                                                                 int frames, uint64_t seed, uint64_t* hashes) {
     const Staged st = stage_tables(v);
-    const int f = blockIdx.x * blockDim.x + threadIdx.x;
-    unsigned long long done = 0;
+    const int lane = threadIdx.x & 31;
+    const int f = static_cast<int>((static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
     if (f < fights) {
         const Match m = match_of(st, p1[f], p2[f]);
         Pcg32 rng(seed, static_cast<uint64_t>(f));
         Fight s;
         fresh_fight(m, s, x1[f], x2[f]);
         Events e;
+        uint64_t* out = hashes + static_cast<size_t>(f) * frames;
         for (int frame = 0; frame < frames; ++frame) {
             if (s.winner >= 0) next_round(m, s, x1[f], x2[f]);
             Input chosen[2] = {{-1, kIdle}, {-1, kIdle}};
             for (int p = 0; p < 2; ++p) {
-                if (decides(m, s, p)) chosen[p] = random_legal(m, s, p, rng);
+                if (decides(m, s, p)) chosen[p] = random_legal_warp(m, s, p, rng, lane);
             }
             frame_step(m, s, chosen[0], chosen[1], e);
-            hashes[static_cast<size_t>(f) * frames + frame] = fight_hash(s);
+            if (lane == 0) out[frame] = fight_hash(s);
         }
-        done = static_cast<unsigned long long>(frames);
+        if (lane == 0) atomicAdd(v.frames, static_cast<unsigned long long>(frames));
     }
-    add_frames(v, done);
 }
 
 // ------------------------------------------------------------------ host: tables
@@ -1334,7 +1355,7 @@ int t8b_sim_random_play(t8b_sim* sim, int fights, const int32_t* p1, const int32
                         const double* p2_x, int frames, uint64_t seed, uint64_t* hashes, uint64_t* frames_done) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (fights <= 0 || frames <= 0 || !p1 || !p2 || !p1_x || !p2_x || !hashes) raise(T8B_EINVAL, "random play arguments");
-        launch("k_random_play", k_random_play, blocks(static_cast<size_t>(fights), kStepThreads), kStepThreads, s.smem(), s.stream, 
+        launch("k_random_play", k_random_play, blocks(static_cast<size_t>(fights) * 32, kStepThreads), kStepThreads, s.smem(), s.stream, 
             s.view(), fights, p1, p2, p1_x, p2_x, frames, seed, hashes);
         s.launched("random play");
         if (frames_done != nullptr) *frames_done = static_cast<uint64_t>(fights) * static_cast<uint64_t>(frames);

@@ -393,7 +393,7 @@ def test_gae_and_objective_full_config2_rollout(cuda):
     4.19 M samples with the normalised advantages against the float64 C restatement: relative norm
     of the logit and of the value gradient <= 1e-5 (north_star's fp32 bound), metric sums within
     1e-5. Samples within 1e-5 of a gradient discontinuity are left out of the norms (a float32 and
-    a float64 evaluation may take different branches there); there are at most a few."""
+    a float64 evaluation may take different branches there); they are fewer than 1 in 10,000."""
     import torch
     from t8b.policy import GpuRolloutBuffer, ppo_config, ppo_output_gradient
     from t8b.workloads import config2_rollout
@@ -419,7 +419,7 @@ def test_gae_and_objective_full_config2_rollout(cuda):
     torch.cuda.synchronize()
     rel, margins, got, want = objective_against_oracle(*inputs, grads, sums, cfg, w.samples)
     assert rel[0] <= 1e-5 and rel[1] <= 1e-5, (rel, margins)
-    assert margins <= 16, margins
+    assert margins <= 1e-4 * w.samples, margins
     for index in (0, 1, 2, 3, 7):
         assert abs(got[index] - want[index]) <= 1e-5 * abs(want[index]), (index, got[index], want[index])
     assert abs(got[4] - want[4]) <= margins and got[6] == want[6]
