@@ -41,6 +41,8 @@ def parse():
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--fights", type=int, default=1024, help="engine workload: fights (config 1: 1,024)")
+    ap.add_argument("--frames", type=int, default=3600, help="engine workload: frames per fight (config 1: 3,600)")
     ap.add_argument("--comm", choices=("native", "torch"), default="native",
                     help="data-parallel exchanges: the library's NCCL communicator (native) or torch.distributed")
     ap.add_argument("--self-play", action="store_true",
@@ -489,7 +491,7 @@ def run_gae_loss(args):
     from t8b import profile
     from t8b.policy import GpuRolloutBuffer, ppo_config, ppo_output_gradient
     from t8b.workloads import config2_rollout
-    t, n, k = 128, 32768, 256
+    t, n, k = args.horizon, args.envs, 256
     w = config2_rollout(t, n, k, seed=1)
     buf = GpuRolloutBuffer(n, t)
     fields = (("rewards", w.rewards), ("old_values", w.values), ("next_values", w.next_values),
@@ -569,12 +571,12 @@ def run_gae_loss(args):
             row.update(bound="hbm", achieved=gbs, unit="GB/s", frac=gbs / peak_hbm)
         rows.append(row)
     cpu = cpu_gae_loss(w, adv, ret, cfg) if not args.no_cpu_baseline else None
-    line = {"metric": "GAE + clipped PPO loss samples/s (T=128 x N=32,768, K=256), 1 B200", "value": samples / (ms / 1000.0),
+    line = {"metric": f"GAE + clipped PPO loss samples/s (T={t} x N={n:,}, K={k}), 1 B200", "value": samples / (ms / 1000.0),
             "unit": "samples/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fp64 statistics)",
             "data": "synthetic (seeded, t8b.workloads.config2_rollout)",
             "config": {"workload": "config 2: GAE + advantage normalisation + clipped PPO/value/entropy objective on "
-                                   "raw logits, T=128 x N=32,768, K=256 slots ~30% legal, seed 1",
+                                   f"raw logits, T={t} x N={n:,}, K={k} slots ~30% legal, seed 1",
                        "samples": samples, "slots": k, "l2": "inputs larger than L2 (9.8 GB per step)"},
             "e2e": {"value": samples / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": bytes_up,
                     "d2h_bytes_per_step": 64},
@@ -626,7 +628,7 @@ def run_engine(args):
     from t8b.sim import GpuFullMoveSimulator
     from t8b._lib import call
     from t8b.device import ptr
-    fights, frames = 1024, 3600
+    fights, frames = args.fights, args.frames
     raw = roster_raw()
     roster = roster_module.parse(raw)
     rng = np.random.default_rng(0)
@@ -679,12 +681,12 @@ def run_engine(args):
                "sample": f"the whole workload ({fights} fights x {frames} frames) on the reference's own CPU engine "
                          f"(full_core::step, oracle/_ref), one fight per thread over {threads} threads",
                "hashes_equal": bool(np.array_equal(got, want))}
-    line = {"metric": "engine fight-frames/s (random legal play, 1,024 fights x 3,600 frames), 1 B200",
+    line = {"metric": f"engine fight-frames/s (random legal play, {fights:,} fights x {frames:,} frames), 1 B200",
             "value": units / (ms / 1000.0), "unit": "fight-frames/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f64 engine (no FMA contraction)",
             "data": "synthetic (41-fighter roster tables from the reference loader; PCG32 seed 0 per fight)",
-            "config": {"workload": "config 1: engine parity run, 1,024 fights x 3,600 frames, per-frame state hash",
+            "config": {"workload": f"config 1: engine parity run, {fights:,} fights x {frames:,} frames, per-frame state hash",
                        "fights": fights, "frames": frames,
                        "l2": "not flushed: 240 B of state per fight stays in registers; the 29 MB hash trace is "
                              "written once per step"},
@@ -693,8 +695,8 @@ def run_engine(args):
             "gpu_launches": launches, "gpu_launches_per_step": launches / args.steps,
             "roofline": {"kernel": "k_random_play", "bound": "issue/latency (fp64 + integer branching)",
                          "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
-                         "note": "1,024 fights are 32 warps on 148 SMs: one warp on most SMs; the figure of merit "
-                                 "is fight-frames/s against the CPU engine"},
+                         "note": "one warp per fight (1,024 warps, about 7 per SM); the figure of merit is "
+                                 "fight-frames/s against the CPU engine"},
             "clocks": clocks.summary()}
     if cpu is not None:
         line["cpu_baseline"] = cpu

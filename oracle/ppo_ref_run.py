@@ -91,8 +91,8 @@ class RefPolicy:
         self.handle = handle
 
     def __del__(self):
-        if getattr(self, "handle", None):
-            lib().t8pr_policy_destroy(self.handle)
+        if getattr(self, "handle", None) and _lib is not None:
+            _lib.t8pr_policy_destroy(self.handle)
             self.handle = None
 
     def parameter_count(self) -> int:
@@ -110,7 +110,8 @@ class RefPolicy:
         _ok(lib().t8pr_policy_forward(self.handle, _ptr(obs), _ptr(masks), n, seed, step, 1 if deterministic else 0,
                                       _ptr(tables), out))
         device = torch.cuda.current_device()
-        return {"actions": view(out[1], (n,), torch.int64, device).cpu().numpy(),
+        return {"logits": view(out[0], (n, self.config.action_count), torch.float32, device).cpu().numpy(),
+                "actions": view(out[1], (n,), torch.int64, device).cpu().numpy(),
                 "log_probabilities": view(out[2], (n,), torch.float32, device).cpu().numpy(),
                 "values": view(out[3], (n,), torch.float32, device).cpu().numpy(),
                 "entropies": view(out[4], (n,), torch.float32, device).cpu().numpy()}
@@ -144,8 +145,8 @@ class RefRollout:
         self.handle = handle
 
     def __del__(self):
-        if getattr(self, "handle", None):
-            lib().t8pr_rollout_destroy(self.handle)
+        if getattr(self, "handle", None) and _lib is not None:
+            _lib.t8pr_rollout_destroy(self.handle)
             self.handle = None
 
     def record_policy(self, step, obs, masks, actions, log_probs, values, tables=None, entropies=None):

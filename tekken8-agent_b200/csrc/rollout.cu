@@ -6,6 +6,7 @@
 // the reference. GAE writes advantages and returns and, in the same pass, per-block fp64
 // moments of the advantages, so normalisation needs one more pass instead of two.
 #include "common.cuh"
+#include "gemm_host.cuh"
 #include "ppo_kernels.cuh"
 
 #include <algorithm>
@@ -226,63 +227,84 @@ __global__ void k_scale_rewards(float* rewards, size_t n, float scale, float cli
     if (i < n) rewards[i] = fminf(clip, fmaxf(-clip, rewards[i] * scale));
 }
 
-// ppo_output_gradient_kernel (src/ppo.cu:453-565) on raw outputs [n][k + 1], one warp per sample.
+// ppo_output_gradient_kernel (src/ppo.cu:453-565) on raw outputs [n][k + 1]: one warp per sample
+// at a time, SLOTS logits per lane (k <= 32 * SLOTS). The grid is a fixed number of resident
+// blocks whose warps stride over the samples; each warp loads its next sample's logits and mask
+// bytes before it works on the current one, so a row is in flight while the previous is scored.
+// Each logit takes one exponential (p = e / sum, log p = logit - log sum). Lane m < 8 of each warp
+// adds metric m of every sample the warp scores in fp64, and each block writes one row of
+// [grid][8] partials; the sample-to-warp assignment is fixed, so the sums are reproducible.
 constexpr int kMaxLogitSlots = 16;  // per lane: k <= 512
-__global__ void k_logit_objective(const float* out, const uint8_t* masks, const int64_t* actions, const float* old_lp,
-                                  const float* old_v, const float* adv, const float* ret, size_t n, int k, float inv_batch,
-                                  float clip, float value_clip, float value_coef, float entropy_coef, float* grads,
-                                  double* block_metrics) {
-    __shared__ float metric[ppo::kWarps][ppo::kMetrics];
+constexpr int kObjectiveBlocksPerSm = 6;
+
+template <int SLOTS>
+__global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
+    const float* out, const uint8_t* masks, const int64_t* actions, const float* old_lp, const float* old_v,
+    const float* adv, const float* ret, size_t n, int k, float inv_batch, float clip, float value_clip,
+    float value_coef, float entropy_coef, float* grads, double* block_metrics) {
+    __shared__ double metric[ppo::kWarps][ppo::kMetrics];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t i = static_cast<size_t>(blockIdx.x) * ppo::kWarps + warp;
-    if (lane < ppo::kMetrics) metric[warp][lane] = 0.0f;
-    const int slots = (k + 31) / 32;
-    if (i < n) {
-        const float* o = out + i * static_cast<size_t>(k + 1);
-        const uint8_t* m = masks + i * static_cast<size_t>(k);
-        float logit[kMaxLogitSlots];
-        bool legal[kMaxLogitSlots];
+    const size_t stride = static_cast<size_t>(gridDim.x) * ppo::kWarps;
+    double acc = 0.0;
+    size_t i = static_cast<size_t>(blockIdx.x) * ppo::kWarps + warp;
+    float next_logit[SLOTS];
+    uint8_t next_mask[SLOTS];
+    const auto load = [&](size_t row) {
+        const float* o = out + row * static_cast<size_t>(k + 1);
+        const uint8_t* m = masks + row * static_cast<size_t>(k);
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            const int a = j * 32 + lane;
+            next_logit[j] = a < k ? o[a] : 0.0f;
+            next_mask[j] = a < k ? m[a] : 0;
+        }
+    };
+    if (i < n) load(i);
+    for (; i < n; i += stride) {
+        float logit[SLOTS];
+        bool legal[SLOTS];
         bool any_local = false;
 #pragma unroll
-        for (int j = 0; j < kMaxLogitSlots; ++j) {
-            const int a = j * 32 + lane;
-            const bool inside = j < slots && a < k;
-            logit[j] = inside ? o[a] : 0.0f;
-            legal[j] = inside && m[a] != 0;
+        for (int j = 0; j < SLOTS; ++j) {
+            logit[j] = next_logit[j];
+            legal[j] = next_mask[j] != 0;
             any_local = any_local || legal[j];
         }
+        if (i + stride < n) load(i + stride);
+        const int64_t action = actions[i];
+        const float old_log = old_lp[i], a_i = adv[i], r_i = ret[i], v_old = old_v[i];
+        const float v = out[i * static_cast<size_t>(k + 1) + k];
         const bool any = __any_sync(0xffffffffu, any_local);
         float local_max = -3.402823466e38f;
 #pragma unroll
-        for (int j = 0; j < kMaxLogitSlots; ++j) {
-            const int a = j * 32 + lane;
-            if (!any) legal[j] = j < slots && a == 0;
+        for (int j = 0; j < SLOTS; ++j) {
+            if (!any) legal[j] = j * 32 + lane == 0;
             if (legal[j]) local_max = fmaxf(local_max, logit[j]);
         }
         const float maximum = ppo::warp_max(local_max);
+        float e[SLOTS];
         float local = 0.0f;
 #pragma unroll
-        for (int j = 0; j < kMaxLogitSlots; ++j) {
-            if (legal[j]) local += expf(logit[j] - maximum);
+        for (int j = 0; j < SLOTS; ++j) {
+            e[j] = legal[j] ? expf(logit[j] - maximum) : 0.0f;
+            local += e[j];
         }
         const float sum = fmaxf(ppo::warp_sum(local), 1e-20f);
         const float log_sum = logf(sum) + maximum;
-        const int selected = any ? static_cast<int>(actions[i]) : 0;
-        const float chosen = __shfl_sync(0xffffffffu, logit[(selected >> 5) % kMaxLogitSlots], selected & 31);
-        const float log_ratio = (chosen - log_sum) - old_lp[i];
+        const int selected = any ? static_cast<int>(action) : 0;
+        const float chosen = __shfl_sync(0xffffffffu, logit[(selected >> 5) % SLOTS], selected & 31);
+        const float log_ratio = (chosen - log_sum) - old_log;
         const float ratio = expf(log_ratio);
-        const float a_i = adv[i];
         const float unclipped = ratio * a_i;
         const float clipped = fminf(1.0f + clip, fmaxf(1.0f - clip, ratio)) * a_i;
         const float lp_grad = unclipped <= clipped ? -a_i * ratio : 0.0f;
         float entropy = 0.0f;
         int legal_count = 0;
-        float prob[kMaxLogitSlots];
 #pragma unroll
-        for (int j = 0; j < kMaxLogitSlots; ++j) {
-            prob[j] = legal[j] ? expf(logit[j] - log_sum) : 0.0f;
+        for (int j = 0; j < SLOTS; ++j) {
+            e[j] = e[j] / sum;  // the probability
             if (legal[j]) {
-                entropy -= prob[j] * (logit[j] - log_sum);
+                entropy -= e[j] * (logit[j] - log_sum);
                 ++legal_count;
             }
         }
@@ -291,41 +313,42 @@ __global__ void k_logit_objective(const float* out, const uint8_t* masks, const 
         for (int off = 16; off > 0; off >>= 1) legal_count += __shfl_xor_sync(0xffffffffu, legal_count, off);
         float* g = grads + i * static_cast<size_t>(k + 1);
 #pragma unroll
-        for (int j = 0; j < kMaxLogitSlots; ++j) {
+        for (int j = 0; j < SLOTS; ++j) {
             const int a = j * 32 + lane;
-            if (j >= slots || a >= k) continue;
+            if (a >= k) continue;
             float value = 0.0f;
             if (legal[j]) {
-                value = (lp_grad * ((a == selected ? 1.0f : 0.0f) - prob[j])) * inv_batch;
-                value += entropy_coef * prob[j] * ((logit[j] - log_sum) + entropy) * inv_batch;
+                value = (lp_grad * ((a == selected ? 1.0f : 0.0f) - e[j])) * inv_batch;
+                value += entropy_coef * e[j] * ((logit[j] - log_sum) + entropy) * inv_batch;
             }
             g[a] = value;
         }
-        const float v = o[k];
-        const float error = v - ret[i];
+        const float error = v - r_i;
         float vgrad = error;
         float vloss = 0.5f * error * error;
         if (value_clip > 0.0f) {
-            const float delta = v - old_v[i];
-            const float cv = old_v[i] + fminf(value_clip, fmaxf(-value_clip, delta));
-            const float cerr = cv - ret[i];
+            const float delta = v - v_old;
+            const float cv = v_old + fminf(value_clip, fmaxf(-value_clip, delta));
+            const float cerr = cv - r_i;
             const float closs = 0.5f * cerr * cerr;
             if (closs > vloss) {
                 vloss = closs;
                 vgrad = fabsf(delta) <= value_clip ? cerr : 0.0f;
             }
         }
-        if (lane == 0) {
-            g[k] = value_coef * vgrad * inv_batch;
-            metric[warp][0] = -fminf(unclipped, clipped);
-            metric[warp][1] = vloss;
-            metric[warp][2] = entropy;
-            metric[warp][3] = (ratio - 1.0f) - log_ratio;
-            metric[warp][4] = fabsf(ratio - 1.0f) > clip ? 1.0f : 0.0f;
-            metric[warp][6] = legal_count > 1 ? 1.0f : 0.0f;
-            metric[warp][7] = legal_count > 1 ? entropy : 0.0f;
-        }
+        if (lane == 0) g[k] = value_coef * vgrad * inv_batch;
+        const bool decision = legal_count > 1;
+        const float mine = lane == 0 ? -fminf(unclipped, clipped)
+                         : lane == 1 ? vloss
+                         : lane == 2 ? entropy
+                         : lane == 3 ? (ratio - 1.0f) - log_ratio
+                         : lane == 4 ? (fabsf(ratio - 1.0f) > clip ? 1.0f : 0.0f)
+                         : lane == 6 ? (decision ? 1.0f : 0.0f)
+                         : lane == 7 ? (decision ? entropy : 0.0f)
+                                     : 0.0f;
+        acc += static_cast<double>(mine);
     }
+    if (lane < ppo::kMetrics) metric[warp][lane] = acc;
     __syncthreads();
     if (block_metrics != nullptr && threadIdx.x < ppo::kMetrics) {
         double s = 0.0;
@@ -334,8 +357,33 @@ __global__ void k_logit_objective(const float* out, const uint8_t* masks, const 
     }
 }
 
-// Scratch of t8b_ppo_output_gradient_static: the per-block metric partials (8 doubles for each
-// block of 8 samples). One copy per device that loads the library, held until the process exits.
+// The objective's launch: `grid` resident blocks (at most kObjectiveBlocksPerSm per SM), the
+// instantiation with the fewest logit slots per lane that holds k.
+unsigned objective_grid(size_t n) {
+    const size_t blocks_needed = (n + ppo::kWarps - 1) / ppo::kWarps;
+    return static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(blocks_needed,
+                                                                        static_cast<size_t>(sm_count()) * kObjectiveBlocksPerSm)));
+}
+
+void launch_objective(cudaStream_t st, unsigned grid, const float* outputs, const uint8_t* masks, const int64_t* actions,
+                      const float* old_lp, const float* old_v, const float* adv, const float* ret, size_t n, int k,
+                      const t8b_ppo_config_t& c, float* gradients, double* partial) {
+    const float inv = 1.0f / static_cast<float>(n);
+#define T8B_OBJECTIVE(SLOTS)                                                                                          \
+    launch("k_logit_objective", k_logit_objective<SLOTS>, grid, 32 * ppo::kWarps, 0, st, outputs, masks, actions,      \
+           old_lp, old_v, adv, ret, n, k, inv, c.clip_range, c.value_clip_range, c.value_coefficient,                   \
+           c.entropy_coefficient, gradients, partial)
+    if (k <= 64) T8B_OBJECTIVE(2);
+    else if (k <= 128) T8B_OBJECTIVE(4);
+    else if (k <= 256) T8B_OBJECTIVE(8);
+    else if (k <= 384) T8B_OBJECTIVE(12);
+    else T8B_OBJECTIVE(16);
+#undef T8B_OBJECTIVE
+}
+
+// Scratch of t8b_ppo_output_gradient_static: the per-block metric partials (8 doubles per block;
+// the objective's grid is at most kObjectiveBlocksPerSm blocks per SM, far below this array's
+// 65,536 rows). One copy per device that loads the library, held until the process exits.
 constexpr size_t kStaticObjectiveSamples = 524288;
 constexpr size_t kStaticObjectiveBlocks = kStaticObjectiveSamples / ppo::kWarps;
 static __device__ __align__(256) double g_objective_scratch[kStaticObjectiveBlocks * ppo::kMetrics];  // 4 MiB
@@ -702,7 +750,7 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
         }
         if (action_count < 2 || action_count > 32 * kMaxLogitSlots) raise(T8B_EINVAL, "action_count must be 2..512");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
-        const unsigned grid = blocks(n, ppo::kWarps);
+        const unsigned grid = objective_grid(n);
         double* partial = nullptr;
         if (metric_sums) {
             // per-block metric partials from the library's stream-ordered pool: no device-wide
@@ -711,10 +759,8 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
                                           sizeof(double) * static_cast<size_t>(grid) * ppo::kMetrics, scratch_pool(), st),
                   "PPO objective partials");
         }
-        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st,
-            outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
-            1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
-            config->entropy_coefficient, gradients, partial);
+        launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n,
+                         action_count, *config, gradients, partial);
         const cudaError_t launched = cudaGetLastError();
         if (metric_sums) {
             if (launched == cudaSuccess) {
@@ -754,11 +800,9 @@ int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, c
         if (action_count < 2 || action_count > 32 * kMaxLogitSlots) raise(T8B_EINVAL, "action_count must be 2..512");
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         double* scratch = metric_sums ? objective_scratch() : nullptr;
-        const unsigned grid = blocks(n, ppo::kWarps);
-        launch("k_logit_objective", k_logit_objective, grid, 32 * ppo::kWarps, 0, st, 
-            outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n, action_count,
-            1.0f / static_cast<float>(n), config->clip_range, config->value_clip_range, config->value_coefficient,
-            config->entropy_coefficient, gradients, scratch);
+        const unsigned grid = objective_grid(n);
+        launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n,
+                         action_count, *config, gradients, scratch);
         check(cudaGetLastError(), "PPO objective");
         if (metric_sums) {
             launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, scratch, static_cast<int>(grid), ppo::kMetrics,

@@ -173,13 +173,37 @@ def test_forward_matches_the_reference(cuda, ref, features, tmp_path, shape):
         assert relative(lp[same], want["log_probabilities"][same]) < 2e-2
 
 
+def own_inputs(lp, v, noise, adv, offset):
+    """What a trainer hands the update, from the acting policy's own forward: old log-probabilities
+    (its log-probability of the sampled action, moved by the shared `noise`), old values (its
+    values) and returns (its values plus the shared `offset`), with the shared advantages."""
+    lp = np.asarray(lp, np.float64)
+    v = np.asarray(v, np.float64)
+    return ((lp - noise).astype(np.float32), v.astype(np.float32), adv.astype(np.float32),
+            (v + offset).astype(np.float32))
+
+
+def masked_log_probability(logits, masks, actions):
+    """log softmax over each row's legal candidates (action 0 alone when none is), at `actions`."""
+    from oracle import ppo_ref as R
+    out = np.empty(len(actions), np.float64)
+    for b in range(0, len(actions), 65536):
+        rows = slice(b, min(len(actions), b + 65536))
+        lp, _, _ = R.log_softmax_masked(np.asarray(logits[rows], np.float64), masks[rows])
+        out[rows] = lp[np.arange(lp.shape[0]), actions[rows]]
+    return out
+
+
 def reference_setup(ref, features, tmp_path, shape, n, seed, scale):
-    """The same starting weights in the library and the reference (through a checkpoint), and a
-    minibatch sampled from that policy: old log-probabilities off by N(0, 0.05), advantages
-    N(0, 1) of both signs, returns scattered N(0, 0.5) around the values."""
+    """The same starting weights in the library and the reference (through a checkpoint), the same
+    observations, masks, feature tables and sampled actions, and per implementation the inputs a
+    trainer would build from that implementation's own forward pass (own_inputs): old
+    log-probabilities off by N(0, 0.05), advantages N(0, 1) of both signs, returns N(0, 0.5)
+    around the values. Built this way the comparison is well conditioned: with inputs taken from
+    one implementation's forward, the other's own rounding of the values would enter every
+    sample's value error with the same sign and swamp the mean-zero gradient of a large batch."""
     import torch
     from t8b.policy import GpuActorCritic, actor_config
-    from test_ppo_gpu import view_of
     rng = np.random.default_rng(seed)
     overrides, feats, obs, tables, masks = shaped(shape, features, rng, n)
     actor = actor_config(**overrides)
@@ -196,18 +220,63 @@ def reference_setup(ref, features, tmp_path, shape, n, seed, scale):
     d = lambda a: torch.as_tensor(a, device="cuda")
     out = ours.forward(d(obs), d(masks), n, seed=1, step=0, tables=d(tables))
     actions = out["actions"].cpu().numpy()
-    old_lp = out["log_probabilities"].cpu().numpy() - rng.normal(scale=0.05, size=n).astype(np.float32)
-    old_v = out["values"].cpu().numpy()
-    adv = rng.normal(size=n).astype(np.float32)
-    ret = (old_v + rng.normal(scale=0.5, size=n)).astype(np.float32)
-    view, keep = view_of((obs, tables, masks, actions, old_lp, old_v, adv, ret))
+    noise = rng.normal(scale=0.05, size=n)
+    adv = rng.normal(size=n)
+    offset = rng.normal(scale=0.5, size=n)
+    mine = own_inputs(out["log_probabilities"].cpu().numpy(), out["values"].cpu().numpy(), noise, adv, offset)
+    want = theirs.forward(d(obs), d(masks), n, 1, 0, True, d(tables))
+    lp_ref = masked_log_probability(want["logits"], masks, actions)
+    theirs_in = own_inputs(lp_ref, want["values"], noise, adv, offset)
+    case = dict(actor=actor, features=feats, obs=obs, tables=tables, masks=masks, actions=actions, noise=noise,
+                adv=adv, offset=offset, params=p.copy())
+    return case, ours, theirs, mine, theirs_in
+
+
+def update_inputs(case, scalars):
+    """The library's rollout view and the reference harness's pointer list for one set of inputs."""
+    import torch
+    from test_ppo_gpu import view_of
+    old_lp, old_v, adv, ret = scalars
+    view, keep = view_of((case["obs"], case["tables"], case["masks"], case["actions"], old_lp, old_v, adv, ret))
+    n = case["obs"].shape[0]
     zeros_f = torch.zeros(n, device="cuda")
     zeros_b = torch.zeros(n, dtype=torch.uint8, device="cuda")
     obs_t, masks_t, actions_t, lp_t, v_t, adv_t, ret_t, tables_t = keep
     pointers = [obs_t.data_ptr(), masks_t.data_ptr(), actions_t.data_ptr(), lp_t.data_ptr(), v_t.data_ptr(),
                 zeros_f.data_ptr(), zeros_b.data_ptr(), zeros_b.data_ptr(), zeros_f.data_ptr(), adv_t.data_ptr(),
                 ret_t.data_ptr(), tables_t.data_ptr(), None]
-    return actor, ours, theirs, view, (keep, zeros_f, zeros_b), pointers
+    return view, pointers, (keep, zeros_f, zeros_b)
+
+
+def oracle_gradient(case, cfg, chunk=16384):
+    """The minibatch gradient in float64 (oracle/ppo_ref.py): the oracle's own forward gives its
+    old log-probabilities, values and returns (own_inputs), then the objective's gradient is
+    backpropagated through the network, chunk by chunk (the batch mean is a sum over samples)."""
+    from oracle import ppo_ref as R
+    actor = case["actor"]
+    shapes = R.layout(actor.observation_size, actor.hidden_size, actor.shared_layers, actor.action_feature_size + 1)
+    params = R.unflatten(case["params"].astype(np.float64), shapes)
+    f = case["features"].astype(np.float64)
+    q = actor.action_feature_size
+    n = case["obs"].shape[0]
+    total = {name: 0.0 for name, _ in shapes}
+    for b in range(0, n, chunk):
+        rows = slice(b, min(n, b + chunk))
+        x = case["obs"][rows].astype(np.float64)
+        hs, out = R.forward(x, params, actor.shared_layers)
+        logits = R.parametric_scores(out[:, :q], f, case["tables"][rows])
+        lp = masked_log_probability(logits, case["masks"][rows], case["actions"][rows])
+        old_lp, old_v, adv, ret = own_inputs(lp, out[:, q], case["noise"][rows], case["adv"][rows],
+                                             case["offset"][rows])
+        g, dv, _ = R.objective_gradient(logits, case["masks"][rows], case["actions"][rows], old_lp.astype(np.float64),
+                                        old_v.astype(np.float64), adv.astype(np.float64), ret.astype(np.float64),
+                                        out[:, q], cfg.clip_range, cfg.value_clip_range, cfg.value_coefficient,
+                                        cfg.entropy_coefficient, n)
+        dout = np.concatenate([R.query_gradient(g, f, case["tables"][rows]), dv[:, None]], 1)
+        grads = R.backward(x, hs, params, dout, actor.shared_layers)
+        for name in total:
+            total[name] = total[name] + grads[name]
+    return R.flatten(total, shapes)
 
 
 def reference_ppo(ref, cfg):
@@ -217,7 +286,7 @@ def reference_ppo(ref, cfg):
 
 
 def reference_first_moment(actor, theirs, path):
-    """The reference's Adam first moment, read back through its checkpoint."""
+    """The reference's Adam moments and step, read back through its checkpoint."""
     from t8b.policy import GpuActorCritic
     theirs.save(path)
     back = GpuActorCritic(256, actor, seed=3)
@@ -235,29 +304,38 @@ def per_tensor(actor, a, b):
 
 @pytest.mark.parametrize("shape, n", [("full_move", 524288), ("config3", 32768)])
 def test_minibatch_gradient_matches_the_reference(cuda, ref, features, tmp_path, shape, n):
-    """The pre-Adam gradient of one minibatch against the reference's own update_ppo in its bf16
-    matmul mode, at default settings (Adam epsilon 1e-5, the default norm clip, mixed-sign
-    advantages): every parameter tensor within 2e-2 relative norm (north_star's bound for bf16
-    GEMMs), and the gradient norm within 2e-2. At 524,288 rows (config 4's minibatch) the
-    library's weight gradients take the split-K path; 32,768 is config 3's batch. The reference's
-    gradient g is read back from its first Adam moment: with zero initial moments one step stores
-    m1 = (1 - beta1) * s * g, where s = max_norm / |g| when |g| exceeds max_norm (src/ppo.cu:
-    710-736)."""
+    """The pre-Adam gradient of one minibatch from the library, from the reference's own
+    update_ppo in its bf16 matmul mode, and in float64 (oracle/ppo_ref.py), at default settings
+    (Adam epsilon 1e-5, the default norm clip, mixed-sign advantages): every parameter tensor of
+    the library's gradient within 2e-2 relative norm of the float64 one and of the reference's
+    (north_star's bound for bf16 GEMMs), and the gradient norms within 2e-2. At 524,288 rows
+    (config 4's minibatch) the library's weight gradients take the split-K path; 32,768 is config
+    3's batch. The reference's gradient g is read back from its first Adam moment: with zero
+    initial moments one step stores m1 = (1 - beta1) * s * g, where s = max_norm / |g| when |g|
+    exceeds max_norm (src/ppo.cu:710-736)."""
     from t8b.policy import ppo_config
-    actor, ours, theirs, view, keep, pointers = reference_setup(ref, features, tmp_path, shape, n, 31,
-                                                                30.0 if shape == "full_move" else 3.0)
+    case, ours, theirs, mine, theirs_in = reference_setup(ref, features, tmp_path, shape, n, 31,
+                                                          30.0 if shape == "full_move" else 3.0)
+    actor = case["actor"]
     cfg = ppo_config(epochs=1, minibatch_size=n, target_kl=0.0)
+    view, _, keep_ours = update_inputs(case, mine)
     got = ours.update_ppo(view, cfg, shuffle_seed=17)
     g_ours = ours.gradients().astype(np.float64)
+    _, pointers, keep_ref = update_inputs(case, theirs_in)
     want = theirs.update(pointers, n, 1, n, reference_ppo(ref, cfg), 17)
     _, m1, _, step = reference_first_moment(actor, theirs, tmp_path / "after.t8ppo")
     assert step == 1 and got["minibatches"] == want["minibatches"] == 1
     norm = np.float32(want["gradient_norm"])
     scale = np.float32(cfg.max_gradient_norm) / norm if norm > np.float32(cfg.max_gradient_norm) else np.float32(1)
     g_ref = m1 / float(np.float32(1) - np.float32(cfg.adam_beta1)) / float(scale)
-    errors = per_tensor(actor, g_ours, g_ref)
-    print(f"gradient vs reference ({shape}, {n} rows): {errors}, norm {got['gradient_norm']} vs {norm}")
-    assert all(e <= 2e-2 for e in errors.values()), errors
+    g_64 = oracle_gradient(case, cfg)
+    vs_oracle, vs_ref = per_tensor(actor, g_ours, g_64), per_tensor(actor, g_ours, g_ref)
+    ref_vs_oracle = per_tensor(actor, g_ref, g_64)
+    print(f"gradient ({shape}, {n} rows): library vs float64 {vs_oracle}; library vs reference {vs_ref}; "
+          f"reference vs float64 {ref_vs_oracle}; norms {got['gradient_norm']} {norm} {np.linalg.norm(g_64)}")
+    assert all(e <= 2e-2 for e in vs_oracle.values()), vs_oracle
+    assert all(e <= 2e-2 for e in vs_ref.values()), vs_ref
+    assert abs(got["gradient_norm"] - np.linalg.norm(g_64)) <= 2e-2 * np.linalg.norm(g_64)
     assert abs(got["gradient_norm"] - want["gradient_norm"]) <= 2e-2 * want["gradient_norm"]
     for key in ("policy_loss", "value_loss", "entropy", "approximate_kl", "clip_fraction", "decision_fraction"):
         assert abs(got[key] - want[key]) <= 2e-2 * max(abs(want[key]), 1e-2), (key, got[key], want[key])
@@ -266,18 +344,22 @@ def test_minibatch_gradient_matches_the_reference(cuda, ref, features, tmp_path,
 @pytest.mark.parametrize("shape", sorted(SHAPES))
 def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
     """A whole update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
-    weights on the same rollout, at default settings (Adam epsilon 1e-5, mixed-sign advantages):
-    the metrics and the mean minibatch gradient norm within 2e-2, and both Adam moments after the
-    eight steps (running averages of the eight gradients and of their squares) within 2e-2
-    relative norm per tensor. The parameter change itself is not compared: with epsilon 1e-5 the
-    first Adam steps move every weight by close to lr * sign(gradient), and the sign of a
-    near-zero gradient component is bf16 rounding noise in either implementation."""
+    weights, each implementation on the inputs its own forward gives (reference_setup), at
+    default settings (Adam epsilon 1e-5, mixed-sign advantages): the metrics and the mean
+    minibatch gradient norm within 2e-2, and both Adam moments after the eight steps (running
+    averages of the eight gradients and of their squares) within 2e-2 relative norm per tensor.
+    The parameter change itself is not compared: with epsilon 1e-5 the first Adam steps move
+    every weight by close to lr * sign(gradient), and the sign of a near-zero gradient component
+    is bf16 rounding noise in either implementation."""
     from t8b.policy import ppo_config
     n = 8192
-    actor, ours, theirs, view, keep, pointers = reference_setup(ref, features, tmp_path, shape, n, 31,
-                                                                30.0 if shape == "full_move" else 3.0)
+    case, ours, theirs, mine, theirs_in = reference_setup(ref, features, tmp_path, shape, n, 31,
+                                                          30.0 if shape == "full_move" else 3.0)
+    actor = case["actor"]
     cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3)
+    view, _, keep_ours = update_inputs(case, mine)
     got = ours.update_ppo(view, cfg, shuffle_seed=17)
+    _, pointers, keep_ref = update_inputs(case, theirs_in)
     want = theirs.update(pointers, n, 1, n, reference_ppo(ref, cfg), 17)
     after, m1_ref, m2_ref, step = reference_first_moment(actor, theirs, tmp_path / "after.t8ppo")
     m1, m2, our_step = ours.optimizer_state()
