@@ -166,17 +166,82 @@ struct t8b_policy {
     }
 
     // forward of the network on x[0..n) -> out [n][64]
-    void network(size_t n, cudaStream_t stream) {
+    // rows [row, row + n) of the activation buffers: two row ranges can run on two streams at once
+    void network(size_t n, cudaStream_t stream, size_t row = 0) {
         const int m = static_cast<int>(n);
+        bf16* x0 = x.data() + row * static_cast<size_t>(padded);
         for (int l = 0; l < layers; ++l) {
-            const Operand a = l == 0 ? Operand{x.data(), m, padded, padded, false} : Operand{h[l - 1].data(), m, hidden, hidden, false};
+            bf16* below = l == 0 ? x0 : h[l - 1].data() + row * static_cast<size_t>(hidden);
+            const Operand a = l == 0 ? Operand{below, m, padded, padded, false} : Operand{below, m, hidden, hidden, false};
             const Operand b{w_bf[l].data(), hidden, a.k, a.k, false};
-            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data(), hidden, m, hidden};
+            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data() + row * static_cast<size_t>(hidden), hidden, m, hidden};
             if (bn_hidden() == 256) dense<256>("gemm_forward_hidden", a, b, epi, stream); else dense<64>("gemm_forward_hidden", a, b, epi, stream);
         }
-        const Operand a{h[layers - 1].data(), m, hidden, hidden, false};
+        const Operand a{h[layers - 1].data() + row * static_cast<size_t>(hidden), m, hidden, hidden, false};
         const Operand b{w_bf[layers].data(), kOutPad, hidden, hidden, false};
-        dense<64>("gemm_forward_output", a, b, ppo::EpiBias{params.data() + b_off[layers], out.data(), kOutPad, m, outputs}, stream);
+        dense<64>("gemm_forward_output", a, b,
+                  ppo::EpiBias{params.data() + b_off[layers], out.data() + row * static_cast<size_t>(kOutPad), kOutPad, m, outputs},
+                  stream);
+    }
+
+    // forward's work on rows [row, row + n) of a batch: the inputs are the batch's base pointers
+    // (observations [batch][width], packed masks [batch][12] or uint8 masks [batch][action_count],
+    // tables [batch]) and the outputs land in rows [row, row + n) of the inference buffers; the
+    // sampler's uniforms are keyed by the row in the batch, so a batch forwarded in row ranges
+    // samples exactly as a whole one.
+    void forward_rows(size_t row, size_t n, const float* obs, const uint8_t* masks, const uint32_t* mask_bits,
+                      const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, bool want_logits,
+                      cudaStream_t st) {
+        if (!features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
+        if (row + n > capacity) raise(T8B_EINVAL, "forward rows exceed the policy capacity");
+        ppo::Prep prep{};
+        prep.obs = obs + row * static_cast<size_t>(width);
+        prep.width = width;
+        prep.padded = padded;
+        prep.mean = obs_mean.data();
+        prep.istd = obs_istd.data();
+        prep.clip = config.observation_clip;
+        prep.normalize = normalizing() ? 1 : 0;
+        prep.count = n;
+        prep.x = x.data() + row * static_cast<size_t>(padded);
+        launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
+        check(cudaGetLastError(), "prepare inputs");
+        network(n, st, row);
+        ppo::Sample smp{};
+        smp.out = out.data() + row * static_cast<size_t>(kOutPad);
+        smp.ld = kOutPad;
+        smp.feature_size = feature_size;
+        smp.action_count = config.action_count;
+        smp.features = features.data();
+        smp.table_count = this->tables;
+        smp.tables = tables ? tables + row : nullptr;
+        smp.bits = mask_bits ? mask_bits + row * 12 : nullptr;
+        smp.bytes = mask_bits ? nullptr : masks + row * static_cast<size_t>(config.action_count);
+        smp.count = n;
+        smp.seed = seed;
+        smp.step = step;
+        smp.lane_offset = row;
+        smp.deterministic = deterministic;
+        smp.logits = want_logits ? logits.data() + row * static_cast<size_t>(config.action_count) : nullptr;
+        smp.actions = actions.data() + row;
+        smp.log_probs = log_probs.data() + row;
+        smp.values = values.data() + row;
+        smp.entropies = entropies.data() + row;
+        // one group per feature table (plus one for out-of-range table indices), each split into
+        // parts so that the grid fills one wave of two blocks per SM (at most 256 samples a block
+        // beyond that): at 32,768 samples over 42 groups, 7 parts (294 blocks) measured 12 %
+        // faster than 13 parts of about 64 samples (546 blocks, 1.8 waves)
+        const size_t groups = tables ? static_cast<size_t>(this->tables) + 1 : 1;
+        const size_t wave = static_cast<size_t>(2 * sm_count()) / groups;
+        smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>({(n + groups * 256 - 1) / (groups * 256), wave, 1}), 4096));
+        const unsigned sample_grid = static_cast<unsigned>(groups * smp.parts);
+        const size_t sample_bytes = ppo::sample_smem(feature_size);
+        if (feature_size == 48) {
+            launch("k_sample", ppo::k_sample<48>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
+        } else {
+            launch("k_sample", ppo::k_sample<32>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
+        }
+        check(cudaGetLastError(), "sample actions");
     }
 
     int splits_for(int tiles) const {
@@ -585,61 +650,35 @@ int t8b_policy_set_action_feature_tables(t8b_policy* p, const float* features, i
     });
 }
 
+}  // extern "C"
+
+namespace t8b::internal {
+
+void policy_forward_rows(t8b_policy* p, size_t row, size_t n, const float* observations, const uint32_t* mask_bits,
+                         const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, cudaStream_t stream,
+                         t8b_policy_output_t* out) {
+    if (observations == nullptr || mask_bits == nullptr || n == 0) raise(T8B_EINVAL, "policy input pointers cannot be null");
+    p->forward_rows(row, n, observations, nullptr, mask_bits, tables, seed, step, deterministic, false, stream);
+    out->logits = nullptr;
+    out->actions = p->actions.data();
+    out->log_probabilities = p->log_probs.data();
+    out->values = p->values.data();
+    out->entropies = p->entropies.data();
+    out->environment_count = row + n;
+}
+
+}  // namespace t8b::internal
+
+extern "C" {
+
 int t8b_policy_forward(t8b_policy* p, const float* obs, const uint8_t* masks, const uint32_t* mask_bits, size_t n,
                        uint64_t seed, uint64_t step, int deterministic, void* stream, const int32_t* tables,
                        int want_logits, t8b_policy_output_t* out) {
     return with_policy(p, [&](t8b_policy& s) {
         if (obs == nullptr || (masks == nullptr && mask_bits == nullptr)) raise(T8B_EINVAL, "policy input pointers cannot be null");
         if (n == 0 || n > s.capacity) raise(T8B_EINVAL, "environment_count exceeds policy capacity");
-        if (!s.features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
-        cudaStream_t st = static_cast<cudaStream_t>(stream);
-        ppo::Prep prep{};
-        prep.obs = obs;
-        prep.width = s.width;
-        prep.padded = s.padded;
-        prep.mean = s.obs_mean.data();
-        prep.istd = s.obs_istd.data();
-        prep.clip = s.config.observation_clip;
-        prep.normalize = s.normalizing() ? 1 : 0;
-        prep.count = n;
-        prep.x = s.x.data();
-        launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
-        check(cudaGetLastError(), "prepare inputs");
-        s.network(n, st);
-        ppo::Sample smp{};
-        smp.out = s.out.data();
-        smp.ld = kOutPad;
-        smp.feature_size = s.feature_size;
-        smp.action_count = s.config.action_count;
-        smp.features = s.features.data();
-        smp.table_count = s.tables;
-        smp.tables = tables;
-        smp.bits = mask_bits;
-        smp.bytes = mask_bits ? nullptr : masks;
-        smp.count = n;
-        smp.seed = seed;
-        smp.step = step;
-        smp.deterministic = deterministic;
-        smp.logits = want_logits ? s.logits.data() : nullptr;
-        smp.actions = s.actions.data();
-        smp.log_probs = s.log_probs.data();
-        smp.values = s.values.data();
-        smp.entropies = s.entropies.data();
-        // one group per feature table (plus one for out-of-range table indices), each split into
-        // parts so that the grid fills one wave of two blocks per SM (at most 256 samples a block
-        // beyond that): at 32,768 samples over 42 groups, 7 parts (294 blocks) measured 12 %
-        // faster than 13 parts of about 64 samples (546 blocks, 1.8 waves)
-        const size_t groups = tables ? static_cast<size_t>(s.tables) + 1 : 1;
-        const size_t wave = static_cast<size_t>(2 * sm_count()) / groups;
-        smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>({(n + groups * 256 - 1) / (groups * 256), wave, 1}), 4096));
-        const unsigned sample_grid = static_cast<unsigned>(groups * smp.parts);
-        const size_t sample_bytes = ppo::sample_smem(s.feature_size);
-        if (s.feature_size == 48) {
-            launch("k_sample", ppo::k_sample<48>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
-        } else {
-            launch("k_sample", ppo::k_sample<32>, sample_grid, 32 * ppo::kSampleWarps, sample_bytes, st, smp);
-        }
-        check(cudaGetLastError(), "sample actions");
+        s.forward_rows(0, n, obs, masks, mask_bits, tables, seed, step, deterministic, want_logits != 0,
+                       static_cast<cudaStream_t>(stream));
         if (out) {
             out->logits = want_logits ? s.logits.data() : nullptr;
             out->actions = s.actions.data();

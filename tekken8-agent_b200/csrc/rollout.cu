@@ -7,6 +7,7 @@
 // moments of the advantages, so normalisation needs one more pass instead of two.
 #include "common.cuh"
 #include "gemm_host.cuh"
+#include "internal.cuh"
 #include "ppo_kernels.cuh"
 
 #include <algorithm>
@@ -231,7 +232,9 @@ __global__ void k_scale_rewards(float* rewards, size_t n, float scale, float cli
 // at a time, SLOTS logits per lane (k <= 32 * SLOTS). The grid is a fixed number of resident
 // blocks whose warps stride over the samples; each warp loads its next sample's logits and mask
 // bytes before it works on the current one, so a row is in flight while the previous is scored.
-// Each logit takes one exponential (p = e / sum, log p = logit - log sum). Lane m < 8 of each warp
+// The kernel is bound by instruction issue more than by memory, so each logit takes one fast
+// exponential (the __expf intrinsic; p = e * (1 / sum), log p = logit - log sum), the legal count
+// comes from ballots, and the per-sample factors of the gradient are formed once. Lane m < 8 of each warp
 // adds metric m of every sample the warp scores in fp64, and each block writes one row of
 // [grid][8] partials; the sample-to-warp assignment is fixed, so the sums are reproducible.
 constexpr int kMaxLogitSlots = 16;  // per lane: k <= 512
@@ -263,22 +266,26 @@ __global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
     for (; i < n; i += stride) {
         float logit[SLOTS];
         bool legal[SLOTS];
-        bool any_local = false;
+        unsigned legal_count = 0;
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
             logit[j] = next_logit[j];
             legal[j] = next_mask[j] != 0;
-            any_local = any_local || legal[j];
+            legal_count += __popc(__ballot_sync(0xffffffffu, legal[j]));
         }
         if (i + stride < n) load(i + stride);
         const int64_t action = actions[i];
         const float old_log = old_lp[i], a_i = adv[i], r_i = ret[i], v_old = old_v[i];
         const float v = out[i * static_cast<size_t>(k + 1) + k];
-        const bool any = __any_sync(0xffffffffu, any_local);
+        const bool any = legal_count != 0;
+        if (!any) {
+            legal_count = 1;
+#pragma unroll
+            for (int j = 0; j < SLOTS; ++j) legal[j] = j * 32 + lane == 0;
+        }
         float local_max = -3.402823466e38f;
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
-            if (!any) legal[j] = j * 32 + lane == 0;
             if (legal[j]) local_max = fmaxf(local_max, logit[j]);
         }
         const float maximum = ppo::warp_max(local_max);
@@ -286,10 +293,11 @@ __global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
         float local = 0.0f;
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
-            e[j] = legal[j] ? expf(logit[j] - maximum) : 0.0f;
+            e[j] = legal[j] ? __expf(logit[j] - maximum) : 0.0f;
             local += e[j];
         }
         const float sum = fmaxf(ppo::warp_sum(local), 1e-20f);
+        const float inv_sum = 1.0f / sum;
         const float log_sum = logf(sum) + maximum;
         const int selected = any ? static_cast<int>(action) : 0;
         const float chosen = __shfl_sync(0xffffffffu, logit[(selected >> 5) % SLOTS], selected & 31);
@@ -299,29 +307,22 @@ __global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
         const float clipped = fminf(1.0f + clip, fmaxf(1.0f - clip, ratio)) * a_i;
         const float lp_grad = unclipped <= clipped ? -a_i * ratio : 0.0f;
         float entropy = 0.0f;
-        int legal_count = 0;
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
-            e[j] = e[j] / sum;  // the probability
-            if (legal[j]) {
-                entropy -= e[j] * (logit[j] - log_sum);
-                ++legal_count;
-            }
+            e[j] *= inv_sum;  // the probability
+            entropy -= e[j] * (logit[j] - log_sum);  // zero for the illegal (p = 0)
         }
         entropy = ppo::warp_sum(entropy);
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) legal_count += __shfl_xor_sync(0xffffffffu, legal_count, off);
+        // d/d logit = (lp_grad (onehot - p) + entropy_coef p (log p + entropy)) / batch
+        const float policy_scale = lp_grad * inv_batch, entropy_scale = entropy_coef * inv_batch;
+        const float shift = entropy - log_sum;
         float* g = grads + i * static_cast<size_t>(k + 1);
 #pragma unroll
         for (int j = 0; j < SLOTS; ++j) {
             const int a = j * 32 + lane;
             if (a >= k) continue;
-            float value = 0.0f;
-            if (legal[j]) {
-                value = (lp_grad * ((a == selected ? 1.0f : 0.0f) - e[j])) * inv_batch;
-                value += entropy_coef * e[j] * ((logit[j] - log_sum) + entropy) * inv_batch;
-            }
-            g[a] = value;
+            const float onehot = a == selected ? 1.0f : 0.0f;
+            g[a] = legal[j] ? policy_scale * (onehot - e[j]) + entropy_scale * e[j] * (logit[j] + shift) : 0.0f;
         }
         const float error = v - r_i;
         float vgrad = error;
@@ -640,6 +641,46 @@ int t8b_rollout_record_outcome_device(t8b_rollout* r, size_t step, const float* 
         check(cudaGetLastError(), "record outcome");
     });
 }
+
+}  // extern "C"
+
+namespace t8b::internal {
+
+void rollout_record_policy_rows(t8b_rollout* r, size_t step, size_t row, size_t n, const float* observations,
+                                const uint32_t* mask_bits, const int64_t* actions, const float* log_probabilities,
+                                const float* values, const int32_t* tables, const float* entropies, cudaStream_t st) {
+    t8b_rollout& s = *r;
+    if (step >= s.horizon || row + n > s.envs) raise(T8B_ERANGE, "rollout rows exceed the buffer");
+    const size_t at = step * s.envs + row;
+    const auto copy = [&](void* to, const void* from, size_t bytes, const char* what) {
+        check(cudaMemcpyAsync(to, from, bytes, cudaMemcpyDeviceToDevice, st), what);
+    };
+    copy(s.observations.data() + at * s.width, observations + row * s.width, sizeof(float) * n * s.width, "observations");
+    copy(s.mask_bits.data() + at * 12, mask_bits + row * 12, sizeof(uint32_t) * n * 12, "masks");
+    copy(s.actions.data() + at, actions + row, sizeof(int64_t) * n, "actions");
+    copy(s.log_probs.data() + at, log_probabilities + row, sizeof(float) * n, "log-probabilities");
+    copy(s.values.data() + at, values + row, sizeof(float) * n, "values");
+    copy(s.tables.data() + at, tables + row, sizeof(int32_t) * n, "tables");
+    copy(s.entropies.data() + at, entropies + row, sizeof(float) * n, "entropies");
+    s.bytes_current[step] = 0;
+    s.entropy_recorded[step] = 1;
+}
+
+void rollout_record_outcome_rows(t8b_rollout* r, size_t step, size_t row, size_t n, const float* rewards,
+                                 const uint8_t* terminated, const uint8_t* truncated, const float* next_values,
+                                 float reward_scale, cudaStream_t st) {
+    t8b_rollout& s = *r;
+    if (step >= s.horizon || row + n > s.envs) raise(T8B_ERANGE, "rollout rows exceed the buffer");
+    const size_t at = step * s.envs + row;
+    launch("k_record_outcome", k_record_outcome, blocks(n, 256), 256, 0, st, s.rewards.data() + at,
+           s.terminated.data() + at, s.truncated.data() + at, s.next_values.data() + at, rewards + row,
+           terminated + row, truncated + row, next_values + row, reward_scale, n);
+    check(cudaGetLastError(), "record outcome");
+}
+
+}  // namespace t8b::internal
+
+extern "C" {
 
 int t8b_rollout_compute_gae(t8b_rollout* r, float gamma, float gae_lambda, int normalize, void* stream) {
     return with_rollout(r, [&](t8b_rollout& s) {

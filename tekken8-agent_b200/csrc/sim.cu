@@ -13,6 +13,7 @@
 // Roster tables are repacked at creation into the compact DMove/DHit/DStance layout and
 // the per-block character table and engine config are staged in shared memory.
 #include "common.cuh"
+#include "internal.cuh"
 #include "contract.cuh"
 
 #include <algorithm>
@@ -82,6 +83,7 @@ struct SimView {
     int roster;
     int width;  // observation floats per environment
     size_t count;
+    size_t first;  // k_masks: the first environment of the range it covers (count environments)
 };
 
 // Copies the character table and configs into shared memory; returns the staged view.
@@ -342,9 +344,10 @@ __global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t
     __shared__ Fight fights[kMaskThreads / 32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t item = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + warp;
-    const size_t env = sides == 3 ? item >> 1 : item;
+    const size_t local = sides == 3 ? item >> 1 : item;
+    const size_t env = v.first + local;
     const int side = sides == 3 ? static_cast<int>(item & 1) : sides - 1;
-    const bool active = env < v.count && (only == nullptr || only[env]);
+    const bool active = local < v.count && (only == nullptr || only[env]);
     if (active) {
         const uint32_t* src = reinterpret_cast<const uint32_t*>(v.states + env);
         uint32_t* dst = reinterpret_cast<uint32_t*>(fights + warp);
@@ -832,8 +835,6 @@ struct t8b_sim {
     Buffer<int32_t> p1, p2, pending_opponents, pending_learners, scenarios, pending_scenarios;
     Buffer<uint8_t> learner_is_p1, terminated, truncated;
     Buffer<uint32_t> side_order;
-    Buffer<unsigned> step_tickets;
-    uint32_t p1_fights = 0;
     int sm_count = 1;
     Buffer<float> aggression, pending_aggression;
     Buffer<Noise> noise;
@@ -869,18 +870,65 @@ struct t8b_sim {
         return v;
     }
     size_t smem() const { return stage_bytes(roster); }
-    // Learner sides from the host, plus the fight order k_step walks: fights with the learner
-    // on P1 first, then those on P2 (each in index order).
-    void set_sides(const uint8_t* host) {
-        learner_is_p1.upload(host, n, stream);
+
+    // Fight groups: the environments split into contiguous ranges that can be stepped on separate
+    // streams (one group, all fights, unless the native rollout loop asks for more). Each group's
+    // slice of side_order lists its fights with the learner on P1 first, then those on P2 (each in
+    // index order), and has its own pair of k_step tickets.
+    std::vector<uint8_t> host_sides;
+    std::vector<size_t> group_first, group_count;
+    std::vector<uint32_t> group_p1;
+    Buffer<unsigned> group_tickets;
+
+    void build_order(int groups) {
+        groups = std::max(1, std::min<int>(groups, static_cast<int>(n)));
+        if (host_sides.size() != n) host_sides.assign(n, 1);
+        group_first.assign(static_cast<size_t>(groups), 0);
+        group_count.assign(static_cast<size_t>(groups), 0);
+        group_p1.assign(static_cast<size_t>(groups), 0);
         std::vector<uint32_t> order;
         order.reserve(n);
-        for (size_t i = 0; i < n; ++i) if (host[i]) order.push_back(static_cast<uint32_t>(i));
-        p1_fights = static_cast<uint32_t>(order.size());
-        for (size_t i = 0; i < n; ++i) if (!host[i]) order.push_back(static_cast<uint32_t>(i));
+        for (int g = 0; g < groups; ++g) {
+            const size_t first = n * static_cast<size_t>(g) / static_cast<size_t>(groups);
+            const size_t last = n * static_cast<size_t>(g + 1) / static_cast<size_t>(groups);
+            group_first[g] = first;
+            group_count[g] = last - first;
+            for (size_t i = first; i < last; ++i) if (host_sides[i]) order.push_back(static_cast<uint32_t>(i));
+            group_p1[g] = static_cast<uint32_t>(order.size() - first);
+            for (size_t i = first; i < last; ++i) if (!host_sides[i]) order.push_back(static_cast<uint32_t>(i));
+        }
         if (side_order.size() < n) side_order.allocate(n);
         side_order.upload(order.data(), n, stream);
-        check(cudaStreamSynchronize(stream), "learner sides");
+        if (group_tickets.size() < 2 * static_cast<size_t>(groups)) group_tickets.allocate(2 * static_cast<size_t>(groups));
+        check(cudaStreamSynchronize(stream), "fight order");
+    }
+    int groups() const { return static_cast<int>(group_first.size()); }
+
+    // Learner sides from the host, plus the fight order k_step walks.
+    void set_sides(const uint8_t* host) {
+        learner_is_p1.upload(host, n, stream);
+        host_sides.assign(host, host + n);
+        build_order(std::max(1, groups()));
+    }
+
+    // env_step over one group's fights on `st` (k_step, then the learner's masks of the group).
+    void step_group(int g, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter, bool reset,
+                    cudaStream_t st) {
+        SimView v = view();
+        v.side_order = side_order.data() + group_first[g];
+        v.count = group_count[g];
+        unsigned* tickets = group_tickets.data() + 2 * static_cast<size_t>(g);
+        check(cudaMemsetAsync(tickets, 0, 2 * sizeof(unsigned), st), "step tickets");
+        const StepGrid grid = step_grid(group_count[g], group_p1[g], sm_count);
+        launch("k_step", k_step, grid.blocks, grid.threads, smem(), st, v, learner, opponent, seed, counter, tickets,
+               group_p1[g], reset ? 1 : 0);
+        launched("step");
+        v.first = group_first[g];
+        const unsigned warps_per_block = kMaskThreads / 32;
+        launch("k_masks", k_masks, blocks(group_count[g], warps_per_block), kMaskThreads, smem(), st, v,
+               static_cast<const uint8_t*>(nullptr), 1);
+        launched("candidate masks");
+        opponent_bits_stale = true;
     }
     void launched(const char* what) const { check(cudaGetLastError(), what); }
 
@@ -1200,16 +1248,30 @@ static int step_launch(t8b_sim* sim, const int64_t* learner, const int64_t* oppo
                 bool reset) {
     return with_sim(sim, [&](t8b_sim& s) {
         if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
-        if (s.step_tickets.size() == 0) s.step_tickets.allocate(2);
-        s.step_tickets.zero(s.stream);
-        const StepGrid g = step_grid(s.n, s.p1_fights, s.sm_count);
-        launch("k_step", k_step, g.blocks, g.threads, s.smem(), s.stream, s.view(), learner, opponent, seed, counter,
-               s.step_tickets.data(), s.p1_fights, reset ? 1 : 0);
-        s.launched("step");
-        s.masks(nullptr);
+        for (int g = 0; g < s.groups(); ++g) s.step_group(g, learner, opponent, seed, counter, reset, s.stream);
     });
 }
 }  // namespace t8b
+
+}  // extern "C"
+
+namespace t8b::internal {
+
+void sim_set_groups(t8b_sim* sim, int groups) {
+    if (sim->groups() != groups) sim->build_order(groups);
+}
+size_t sim_group_first(const t8b_sim* sim, int group) { return sim->group_first[static_cast<size_t>(group)]; }
+size_t sim_group_count(const t8b_sim* sim, int group) { return sim->group_count[static_cast<size_t>(group)]; }
+void sim_step_group(t8b_sim* sim, int group, const int64_t* learner, const int64_t* opponent, uint64_t seed,
+                    uint64_t counter, bool reset, cudaStream_t stream) {
+    if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
+    if (group < 0 || group >= sim->groups()) raise(T8B_ERANGE, "fight group");
+    sim->step_group(group, learner, opponent, seed, counter, reset, stream);
+}
+
+}  // namespace t8b::internal
+
+extern "C" {
 
 int t8b_sim_step(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter) {
     return t8b::step_launch(sim, learner, opponent, seed, counter, false);

@@ -11,7 +11,100 @@
 // opponent policy its forward (seed + 2) runs on a second stream that overlaps the learner's.
 // Every decision but the last steps and resets in one call (t8b_sim_step_and_reset): nothing
 // reads the terminal observations there, while the last decision's bootstrap forward does.
+//
+// Against scripted opponents the fights are split into two groups (contiguous halves) and each
+// half's decision runs on a stream of its own: while one half's frame step holds the SMs' issue
+// slots at a low rate (one thread per fight, divergent lanes), the other half's forward,
+// sampler, masks and records run beside it. Everything per fight is the same computation as in
+// one stream (the sampler's uniforms are keyed by the fight's row), so the rollout is
+// bit-identical. T8B_ROLLOUT_GROUPS=1 in the environment keeps one stream.
 #include "common.cuh"
+#include "internal.cuh"
+
+#include <cstdlib>
+
+namespace {
+
+int rollout_groups(size_t fights, bool opponent) {
+    static const int configured = [] {
+        const char* text = std::getenv("T8B_ROLLOUT_GROUPS");
+        return text != nullptr ? std::atoi(text) : 2;
+    }();
+    if (opponent || fights < 8192) return 1;
+    return configured == 1 ? 1 : 2;
+}
+
+// The grouped loop: per decision and group, on the group's stream, the learner's forward on the
+// group's rows, the previous decision's outcome, the record and the group's step (with the reset
+// of finished rounds); after the last decision the bootstrap forward per group, then one reset
+// of finished rounds over all fights on the main stream.
+void collect_grouped(t8b_sim* sim, t8b_policy* policy, t8b_rollout* rollout, uint64_t seed, uint64_t update,
+                     size_t horizon, float reward_scale, cudaStream_t main) {
+    using namespace t8b;
+    const auto ok = [](int status) {
+        if (status != T8B_OK) raise(status, t8b_last_error());
+    };
+    constexpr int kGroups = 2;
+    internal::sim_set_groups(sim, kGroups);
+    cudaStream_t streams[kGroups] = {};
+    cudaEvent_t done[kGroups] = {};
+    cudaEvent_t start = nullptr;
+    struct Cleanup {
+        cudaStream_t* streams;
+        cudaEvent_t* done;
+        cudaEvent_t* start;
+        ~Cleanup() {
+            for (int g = 0; g < kGroups; ++g) {
+                if (done[g]) cudaEventDestroy(done[g]);
+                if (streams[g]) cudaStreamDestroy(streams[g]);
+            }
+            if (*start) cudaEventDestroy(*start);
+        }
+    } cleanup{streams, done, &start};
+    check(cudaEventCreateWithFlags(&start, cudaEventDisableTiming), "event");
+    for (int g = 0; g < kGroups; ++g) {
+        // blocking streams: the legacy stream (the uint8 mask expansion of the reference view)
+        // waits for them
+        check(cudaStreamCreate(&streams[g]), "group stream");
+        check(cudaEventCreateWithFlags(&done[g], cudaEventDisableTiming), "event");
+    }
+    check(cudaEventRecord(start, main), "event");
+    for (int g = 0; g < kGroups; ++g) check(cudaStreamWaitEvent(streams[g], start, 0), "wait");
+    const int32_t* tables = t8b_sim_learner_feature_tables(sim);
+    const float* obs = t8b_sim_learner_observations(sim);
+    const uint32_t* bits = t8b_sim_learner_mask_bits(sim);
+    for (size_t step = 0; step < horizon; ++step) {
+        const uint64_t counter = update * horizon + step;
+        for (int g = 0; g < kGroups; ++g) {
+            const size_t row = internal::sim_group_first(sim, g), n = internal::sim_group_count(sim, g);
+            cudaStream_t st = streams[g];
+            t8b_policy_output_t out{};
+            internal::policy_forward_rows(policy, row, n, obs, bits, tables, seed + 1, counter, 0, st, &out);
+            if (step > 0) {
+                internal::rollout_record_outcome_rows(rollout, step - 1, row, n, t8b_sim_rewards(sim),
+                                                      t8b_sim_terminated(sim), t8b_sim_truncated(sim), out.values,
+                                                      reward_scale, st);
+            }
+            internal::rollout_record_policy_rows(rollout, step, row, n, obs, bits, out.actions, out.log_probabilities,
+                                                 out.values, tables, out.entropies, st);
+            internal::sim_step_group(sim, g, out.actions, nullptr, seed, counter + 1, step + 1 < horizon, st);
+            if (step + 1 == horizon) {
+                t8b_policy_output_t last{};
+                internal::policy_forward_rows(policy, row, n, obs, bits, tables, seed + 3, counter, 1, st, &last);
+                internal::rollout_record_outcome_rows(rollout, step, row, n, t8b_sim_rewards(sim),
+                                                      t8b_sim_terminated(sim), t8b_sim_truncated(sim), last.values,
+                                                      reward_scale, st);
+            }
+        }
+    }
+    for (int g = 0; g < kGroups; ++g) {
+        check(cudaEventRecord(done[g], streams[g]), "event");
+        check(cudaStreamWaitEvent(main, done[g], 0), "wait");
+    }
+    ok(t8b_sim_reset_done(sim, seed, update * horizon + horizon));
+}
+
+}  // namespace
 
 extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout* rollout, t8b_policy* opponent,
                                    uint64_t seed, uint64_t update, size_t horizon, float reward_scale, void* stream) {
@@ -24,6 +117,11 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
             if (status != T8B_OK) raise(status, t8b_last_error());
         };
         ok(t8b_sim_set_stream(sim, stream));
+        if (rollout_groups(n, opponent != nullptr) > 1) {
+            collect_grouped(sim, policy, rollout, seed, update, horizon, reward_scale, main);
+            return;
+        }
+        internal::sim_set_groups(sim, 1);
         cudaStream_t side = nullptr;
         cudaEvent_t sim_ready = nullptr, opponent_done = nullptr;
         struct Cleanup {

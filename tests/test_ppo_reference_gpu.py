@@ -345,7 +345,7 @@ def test_minibatch_gradient_matches_the_reference(cuda, ref, features, tmp_path,
 def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
     """A whole update (2 epochs x 4 minibatches, the same std::shuffle permutations) from the same
     weights, each implementation on the inputs its own forward gives (reference_setup), at
-    default settings (Adam epsilon 1e-5, mixed-sign advantages): the metrics and the mean
+    default settings (learning rate 3e-4, Adam epsilon 1e-5, mixed-sign advantages): the metrics and the mean
     minibatch gradient norm within 2e-2, and both Adam moments after the eight steps (running
     averages of the eight gradients and of their squares) within 2e-2 relative norm per tensor.
     The parameter change itself is not compared: with epsilon 1e-5 the first Adam steps move
@@ -356,7 +356,7 @@ def test_update_matches_the_reference(cuda, ref, features, tmp_path, shape):
     case, ours, theirs, mine, theirs_in = reference_setup(ref, features, tmp_path, shape, n, 31,
                                                           30.0 if shape == "full_move" else 3.0)
     actor = case["actor"]
-    cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0, learning_rate=1e-3)
+    cfg = ppo_config(epochs=2, minibatch_size=n // 4, target_kl=0.0)
     view, _, keep_ours = update_inputs(case, mine)
     got = ours.update_ppo(view, cfg, shuffle_seed=17)
     _, pointers, keep_ref = update_inputs(case, theirs_in)

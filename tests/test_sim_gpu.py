@@ -320,10 +320,12 @@ def test_self_play_iteration_with_a_checkpoint_opponent(cuda, roster, tmp_path):
     assert np.array_equal(results[0][1], results[1][1])
 
 
-@pytest.mark.parametrize("self_play", [False, True])
-def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self_play):
+@pytest.mark.parametrize("self_play, envs", [(False, 1024), (True, 1024), (False, 8192)])
+def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self_play, envs):
     """t8b_collect_rollout issues the same calls as the trainer's Python loop: one iteration
-    from the same seeds gives bit-identical weights, simulator states and advantages."""
+    from the same seeds gives bit-identical weights, simulator states and advantages. At 8,192
+    fights against scripted opponents the native loop runs the two halves of the fights on two
+    streams, which must not change a bit."""
     import torch
     from t8b.policy import GpuActorCritic, actor_config
     from t8b.train import SelfPlayTrainer
@@ -333,7 +335,7 @@ def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self
         opponent = tmp_path / "frozen.t8ppo"
     results = []
     for native in (True, False):
-        trainer = SelfPlayTrainer(roster, environments=1024, horizon=8, epochs=1, minibatches=2, seed=11,
+        trainer = SelfPlayTrainer(roster, environments=envs, horizon=8, epochs=1, minibatches=2, seed=11,
                                   opponent=opponent)
         trainer.iterate(native=native)
         torch.cuda.synchronize()
