@@ -41,6 +41,7 @@ def parse():
     ap.add_argument("--epochs", type=int, default=4)
     ap.add_argument("--minibatches", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=32768, help="mlp workload: rows (config 3: 32,768)")
     ap.add_argument("--fights", type=int, default=1024, help="engine workload: fights (config 1: 1,024)")
     ap.add_argument("--frames", type=int, default=3600, help="engine workload: frames per fight (config 1: 3,600)")
     ap.add_argument("--comm", choices=("native", "torch"), default="native",
@@ -175,6 +176,15 @@ GEMM_FLOPS_PER_SAMPLE = {
     "gemm_weight_grad": 2 * (OBS * HIDDEN + HIDDEN * HIDDEN + HIDDEN * OUTPUTS),
     "gemm_input_grad": 2 * (HIDDEN * OUTPUTS + HIDDEN * HIDDEN),
 }
+# GEMM algorithmic bytes per sample (bf16 activations, weights negligible): the operand rows each
+# GEMM must read and the epilogue rows it must write. At K = 512 every label has less than the
+# B200's ridge intensity (about 220 FLOP/B against the measured peaks), so each is bound by HBM:
+#   forward hidden: x 384 + h1 1,024 written, h1 1,024 read + h2 1,024 written = 3,456
+#   forward output: h2 1,024 read + outputs 64 x 4 written = 1,280
+#   weight gradients: (h2 1,024 + dO 128) + (dZ2 1,024 + h1 1,024) + (dZ1 1,024 + x 384) = 4,608
+#   input gradients: (dO 128 + h2 1,024 + dZ2 1,024 written) + (dZ2 1,024 + h1 1,024 + dZ1 1,024 written) = 5,248
+GEMM_BYTES_PER_SAMPLE = {"gemm_forward_hidden": 3456, "gemm_forward_output": 1280, "gemm_weight_grad": 4608,
+                         "gemm_input_grad": 5248}
 # GAE: read reward, value, next value (4 B each), terminated, truncated (1 B each); write
 # advantage and return (4 B each) = 22 B per sample.
 GAE_BYTES_PER_SAMPLE = 22
@@ -208,8 +218,16 @@ def kernel_table(args, profile, steps, peaks):
         row = {"kernel": label, "launches_per_step": launches / steps, "ms_per_step": ms / steps,
                "share": ms / total}
         if label in GEMM_FLOPS_PER_SAMPLE:
-            tflops = GEMM_FLOPS_PER_SAMPLE[label] * samples[label] * steps / (ms / 1000.0) / 1e12
-            row.update(bound="tensor", achieved=tflops, peak=peak_bf16, unit="TFLOP/s", frac=tflops / peak_bf16)
+            seconds = ms / 1000.0
+            tflops = GEMM_FLOPS_PER_SAMPLE[label] * samples[label] * steps / seconds / 1e12
+            gbs = GEMM_BYTES_PER_SAMPLE[label] * samples[label] * steps / seconds / 1e9
+            # the binding roof is the one whose time for this work is longer
+            hbm_bound = GEMM_BYTES_PER_SAMPLE[label] / (peak_hbm * 1e9) > GEMM_FLOPS_PER_SAMPLE[label] / (peak_bf16 * 1e12)
+            row.update(tensor_tflops=tflops, tensor_frac=tflops / peak_bf16, hbm_gbs=gbs, hbm_frac=gbs / peak_hbm)
+            if hbm_bound:
+                row.update(bound="hbm", achieved=gbs, peak=peak_hbm, unit="GB/s", frac=gbs / peak_hbm)
+            else:
+                row.update(bound="tensor", achieved=tflops, peak=peak_bf16, unit="TFLOP/s", frac=tflops / peak_bf16)
         elif label in ("k_step", "k_gae", "k_loss"):
             per = {"k_step": STEP_BYTES_PER_ENV * n, "k_gae": GAE_BYTES_PER_SAMPLE * t * n,
                    "k_loss": LOSS_BYTES_PER_SAMPLE * n * t // args.minibatches}[label]
@@ -396,13 +414,14 @@ def run_ours(args):
 
 def run_mlp(args):
     """Policy forward + backward (one PPO minibatch update: forward, objective, backward, Adam)
-    on a batch of 32,768 at the microbench shapes, with the GEMMs' tensor-core roofline."""
+    on a batch (config 3: 32,768; --batch 524288 is config 4's minibatch) at the microbench
+    shapes, with the GEMMs' tensor-core roofline."""
     import numpy as np
     import torch
     from t8b import profile
     from t8b.policy import GpuActorCritic, actor_config, ppo_config
     from t8b._lib import RolloutView
-    batch = 32768
+    batch = args.batch
     obs_size, actions, features_size, hidden = 128, 256, 48, 512
     rng = np.random.default_rng(2)
     tables = 41
@@ -457,7 +476,7 @@ def run_mlp(args):
     gemm_ms = sum(kernels[k][1] for k in flops if k in kernels) / args.steps
     _, peak_bf16, peak_sustained, peak_kind = measured_peaks()
     achieved = gemm_flops / (gemm_ms / 1000.0) / 1e12
-    line = {"metric": "policy fwd+bwd samples/s, batch 32,768, config-3 shapes", "value": batch / (ms / 1000.0),
+    line = {"metric": f"policy fwd+bwd samples/s, batch {batch:,}, config-3 shapes", "value": batch / (ms / 1000.0),
             "unit": "samples/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16 tensor-core products, fp32 accumulation and master weights", "data": "synthetic",

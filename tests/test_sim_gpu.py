@@ -324,8 +324,9 @@ def test_self_play_iteration_with_a_checkpoint_opponent(cuda, roster, tmp_path):
 def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self_play, envs):
     """t8b_collect_rollout issues the same calls as the trainer's Python loop: one iteration
     from the same seeds gives bit-identical weights, simulator states and advantages. At 8,192
-    fights against scripted opponents the native loop runs the two halves of the fights on two
-    streams, which must not change a bit."""
+    fights against scripted opponents the native loop also runs with the two halves of the
+    fights on two streams (T8B_ROLLOUT_GROUPS=2), which must not change a bit."""
+    import os
     import torch
     from t8b.policy import GpuActorCritic, actor_config
     from t8b.train import SelfPlayTrainer
@@ -334,10 +335,16 @@ def test_native_rollout_loop_equals_the_python_loop(cuda, roster, tmp_path, self
         GpuActorCritic(1024, actor_config(), 8).save_checkpoint(tmp_path / "frozen.t8ppo")
         opponent = tmp_path / "frozen.t8ppo"
     results = []
+    grouped = envs >= 8192 and not self_play
     for native in (True, False):
         trainer = SelfPlayTrainer(roster, environments=envs, horizon=8, epochs=1, minibatches=2, seed=11,
                                   opponent=opponent)
-        trainer.iterate(native=native)
+        if native and grouped:
+            os.environ["T8B_ROLLOUT_GROUPS"] = "2"
+        try:
+            trainer.iterate(native=native)
+        finally:
+            os.environ.pop("T8B_ROLLOUT_GROUPS", None)
         torch.cuda.synchronize()
         results.append((trainer.policy.parameters(), trainer.sim.download_state_bytes(),
                         trainer.rollout.tensor("advantages").cpu().numpy().copy()))
