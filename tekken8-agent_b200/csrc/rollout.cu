@@ -358,28 +358,189 @@ __global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
     }
 }
 
-// The objective's launch: `grid` resident blocks (at most kObjectiveBlocksPerSm per SM), the
-// instantiation with the fewest logit slots per lane that holds k.
+// The same objective with two samples per warp, one per half-warp (16 lanes, SLOTS logits per
+// lane: k <= 16 * SLOTS), for k <= 256. Reductions take four butterfly steps inside each half,
+// and the per-sample work (the scalars, the ratio, the value loss, the metrics) is issued once
+// for both samples, which matters because the kernel is bound by instruction issue. Each
+// half-warp strides over sample pairs like the warps of k_logit_objective, with the next pair
+// prefetched; the arithmetic per logit is that kernel's.
+template <int SLOTS>
+__global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective_pair(
+    const float* out, const uint8_t* masks, const int64_t* actions, const float* old_lp, const float* old_v,
+    const float* adv, const float* ret, size_t n, int k, float inv_batch, float clip, float value_clip,
+    float value_coef, float entropy_coef, float* grads, double* block_metrics) {
+    __shared__ double metric[ppo::kWarps][ppo::kMetrics];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int half = lane >> 4, l = lane & 15;
+    const unsigned full = 0xffffffffu;
+    const size_t stride = static_cast<size_t>(gridDim.x) * ppo::kWarps * 2;
+    double acc = 0.0;
+    size_t i = (static_cast<size_t>(blockIdx.x) * ppo::kWarps + warp) * 2 + half;
+    float next_logit[SLOTS] = {};
+    uint8_t next_mask[SLOTS] = {};
+    const auto load = [&](size_t row) {
+        const float* o = out + row * static_cast<size_t>(k + 1);
+        const uint8_t* m = masks + row * static_cast<size_t>(k);
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            const int a = j * 16 + l;
+            next_logit[j] = a < k ? o[a] : 0.0f;
+            next_mask[j] = a < k ? m[a] : 0;
+        }
+    };
+    const auto half_sum = [](float v) {
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        return v;
+    };
+    const auto half_max = [](float v) {
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        return v;
+    };
+    if (i < n) load(i);
+    // every lane runs every iteration (the shuffles span the warp); a half whose sample is past
+    // the end computes on zeros and stores nothing
+    for (size_t base = i - half; base < n; base += stride, i += stride) {
+        const bool live = i < n;
+        float logit[SLOTS];
+        bool legal[SLOTS];
+        unsigned legal_count = 0;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            logit[j] = next_logit[j];
+            legal[j] = live && next_mask[j] != 0;
+            legal_count += __popc((__ballot_sync(full, legal[j]) >> (16 * half)) & 0xffffu);
+        }
+        if (i + stride < n) load(i + stride);
+        const size_t at = live ? i : 0;
+        const int64_t action = actions[at];
+        const float old_log = old_lp[at], a_i = adv[at], r_i = ret[at], v_old = old_v[at];
+        const float v = out[at * static_cast<size_t>(k + 1) + k];
+        const bool any = legal_count != 0;
+        if (!any) {
+            legal_count = 1;
+#pragma unroll
+            for (int j = 0; j < SLOTS; ++j) legal[j] = j * 16 + l == 0;
+        }
+        float local_max = -3.402823466e38f;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            if (legal[j]) local_max = fmaxf(local_max, logit[j]);
+        }
+        const float maximum = half_max(local_max);
+        float e[SLOTS];
+        float local = 0.0f;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            e[j] = legal[j] ? __expf(logit[j] - maximum) : 0.0f;
+            local += e[j];
+        }
+        const float sum = fmaxf(half_sum(local), 1e-20f);
+        const float inv_sum = 1.0f / sum;
+        const float log_sum = logf(sum) + maximum;
+        const int selected = any ? static_cast<int>(action) : 0;
+        float mine_logit = 0.0f;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) mine_logit = j * 16 + l == selected ? logit[j] : mine_logit;
+        const float chosen = __shfl_sync(full, mine_logit, (half << 4) | (selected & 15));
+        const float log_ratio = (chosen - log_sum) - old_log;
+        const float ratio = expf(log_ratio);
+        const float unclipped = ratio * a_i;
+        const float clipped = fminf(1.0f + clip, fmaxf(1.0f - clip, ratio)) * a_i;
+        const float lp_grad = unclipped <= clipped ? -a_i * ratio : 0.0f;
+        float entropy = 0.0f;
+#pragma unroll
+        for (int j = 0; j < SLOTS; ++j) {
+            e[j] *= inv_sum;  // the probability
+            entropy -= e[j] * (logit[j] - log_sum);
+        }
+        entropy = half_sum(entropy);
+        const float policy_scale = lp_grad * inv_batch, entropy_scale = entropy_coef * inv_batch;
+        const float shift = entropy - log_sum;
+        if (live) {
+            float* g = grads + i * static_cast<size_t>(k + 1);
+#pragma unroll
+            for (int j = 0; j < SLOTS; ++j) {
+                const int a = j * 16 + l;
+                if (a >= k) continue;
+                const float onehot = a == selected ? 1.0f : 0.0f;
+                g[a] = legal[j] ? policy_scale * (onehot - e[j]) + entropy_scale * e[j] * (logit[j] + shift) : 0.0f;
+            }
+        }
+        const float error = v - r_i;
+        float vgrad = error;
+        float vloss = 0.5f * error * error;
+        if (value_clip > 0.0f) {
+            const float delta = v - v_old;
+            const float cv = v_old + fminf(value_clip, fmaxf(-value_clip, delta));
+            const float cerr = cv - r_i;
+            const float closs = 0.5f * cerr * cerr;
+            if (closs > vloss) {
+                vloss = closs;
+                vgrad = fabsf(delta) <= value_clip ? cerr : 0.0f;
+            }
+        }
+        if (live && l == 0) grads[i * static_cast<size_t>(k + 1) + k] = value_coef * vgrad * inv_batch;
+        const bool decision = legal_count > 1;
+        const float mine = !live ? 0.0f
+                         : l == 0 ? -fminf(unclipped, clipped)
+                         : l == 1 ? vloss
+                         : l == 2 ? entropy
+                         : l == 3 ? (ratio - 1.0f) - log_ratio
+                         : l == 4 ? (fabsf(ratio - 1.0f) > clip ? 1.0f : 0.0f)
+                         : l == 6 ? (decision ? 1.0f : 0.0f)
+                         : l == 7 ? (decision ? entropy : 0.0f)
+                                  : 0.0f;
+        acc += static_cast<double>(mine);
+    }
+    acc += __shfl_down_sync(full, acc, 16);  // the halves' sums, in fixed order
+    if (lane < ppo::kMetrics) metric[warp][lane] = acc;
+    __syncthreads();
+    if (block_metrics != nullptr && threadIdx.x < ppo::kMetrics) {
+        double sm = 0.0;
+        for (int w = 0; w < ppo::kWarps; ++w) sm += metric[w][threadIdx.x];
+        block_metrics[static_cast<size_t>(blockIdx.x) * ppo::kMetrics + threadIdx.x] = sm;
+    }
+}
+
+// The objective's grid: the blocks that are resident at once (at most kObjectiveBlocksPerSm per
+// SM, fewer when the instantiation's registers allow fewer), or fewer when n needs fewer.
 unsigned objective_grid(size_t n) {
-    const size_t blocks_needed = (n + ppo::kWarps - 1) / ppo::kWarps;
+    const size_t blocks_needed = (n + 2 * ppo::kWarps - 1) / (2 * ppo::kWarps);
     return static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(blocks_needed,
                                                                         static_cast<size_t>(sm_count()) * kObjectiveBlocksPerSm)));
 }
 
-void launch_objective(cudaStream_t st, unsigned grid, const float* outputs, const uint8_t* masks, const int64_t* actions,
-                      const float* old_lp, const float* old_v, const float* adv, const float* ret, size_t n, int k,
-                      const t8b_ppo_config_t& c, float* gradients, double* partial) {
+template <typename Kernel>
+unsigned resident_grid(Kernel kernel, unsigned grid) {
+    int per_sm = 0;
+    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 32 * ppo::kWarps, 0), "objective occupancy");
+    return std::max(1u, std::min(grid, static_cast<unsigned>(std::max(per_sm, 1) * sm_count())));
+}
+
+// Launches the instantiation with the fewest logit slots per lane that holds k, on `grid` blocks
+// at most; `partial` (when given) receives one row of metric partials per block launched, and the
+// number of rows is returned.
+unsigned launch_objective(cudaStream_t st, unsigned grid, const float* outputs, const uint8_t* masks,
+                          const int64_t* actions, const float* old_lp, const float* old_v, const float* adv,
+                          const float* ret, size_t n, int k, const t8b_ppo_config_t& c, float* gradients,
+                          double* partial) {
     const float inv = 1.0f / static_cast<float>(n);
-#define T8B_OBJECTIVE(SLOTS)                                                                                          \
-    launch("k_logit_objective", k_logit_objective<SLOTS>, grid, 32 * ppo::kWarps, 0, st, outputs, masks, actions,      \
-           old_lp, old_v, adv, ret, n, k, inv, c.clip_range, c.value_clip_range, c.value_coefficient,                   \
-           c.entropy_coefficient, gradients, partial)
-    if (k <= 64) T8B_OBJECTIVE(2);
-    else if (k <= 128) T8B_OBJECTIVE(4);
-    else if (k <= 256) T8B_OBJECTIVE(8);
-    else if (k <= 384) T8B_OBJECTIVE(12);
-    else T8B_OBJECTIVE(16);
+#define T8B_OBJECTIVE(KERNEL, SLOTS)                                                                                  \
+    do {                                                                                                               \
+        grid = resident_grid(KERNEL<SLOTS>, grid);                                                                     \
+        launch("k_logit_objective", KERNEL<SLOTS>, grid, 32 * ppo::kWarps, 0, st, outputs, masks, actions, old_lp,      \
+               old_v, adv, ret, n, k, inv, c.clip_range, c.value_clip_range, c.value_coefficient,                      \
+               c.entropy_coefficient, gradients, partial);                                                             \
+    } while (0)
+    if (k <= 64) T8B_OBJECTIVE(k_logit_objective_pair, 4);
+    else if (k <= 128) T8B_OBJECTIVE(k_logit_objective_pair, 8);
+    else if (k <= 256) T8B_OBJECTIVE(k_logit_objective_pair, 16);
+    else if (k <= 384) T8B_OBJECTIVE(k_logit_objective, 12);
+    else T8B_OBJECTIVE(k_logit_objective, 16);
 #undef T8B_OBJECTIVE
+    return grid;
 }
 
 // Scratch of t8b_ppo_output_gradient_static: the per-block metric partials (8 doubles per block;
@@ -800,12 +961,12 @@ int t8b_ppo_output_gradient(const float* outputs, const uint8_t* masks, const in
                                           sizeof(double) * static_cast<size_t>(grid) * ppo::kMetrics, scratch_pool(), st),
                   "PPO objective partials");
         }
-        launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n,
-                         action_count, *config, gradients, partial);
+        const unsigned rows = launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values,
+                                               advantages, returns, n, action_count, *config, gradients, partial);
         const cudaError_t launched = cudaGetLastError();
         if (metric_sums) {
             if (launched == cudaSuccess) {
-                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, partial, static_cast<int>(grid),
+                launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, partial, static_cast<int>(rows),
                        ppo::kMetrics, metric_sums, 0);
             }
             check(cudaFreeAsync(partial, st), "PPO objective partials");
@@ -842,11 +1003,11 @@ int t8b_ppo_output_gradient_static(const float* outputs, const uint8_t* masks, c
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         double* scratch = metric_sums ? objective_scratch() : nullptr;
         const unsigned grid = objective_grid(n);
-        launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values, advantages, returns, n,
-                         action_count, *config, gradients, scratch);
+        const unsigned rows = launch_objective(st, grid, outputs, masks, actions, old_log_probabilities, old_values,
+                                               advantages, returns, n, action_count, *config, gradients, scratch);
         check(cudaGetLastError(), "PPO objective");
         if (metric_sums) {
-            launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, scratch, static_cast<int>(grid), ppo::kMetrics,
+            launch("k_sum_rows_f64", ppo::k_sum_rows_f64, ppo::kMetrics, 256, 0, st, scratch, static_cast<int>(rows), ppo::kMetrics,
                                                                metric_sums, 0);
             check(cudaGetLastError(), "PPO objective metrics");
         }
