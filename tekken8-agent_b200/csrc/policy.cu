@@ -15,6 +15,7 @@
 // operands (samples as K, split-K) -> fixed-order reductions -> gradient norm -> Adam + casts.
 #include "gemm_host.cuh"
 #include "ppo_kernels.cuh"
+#include "scorer_tc.cuh"
 
 #include <algorithm>
 #include <cmath>
@@ -410,6 +411,12 @@ __global__ void k_decision_finish(const double* partial, int blocks, double* out
 // feature table; the runs of the kBuckets tables add at most one partial run each.
 size_t loss_blocks(size_t n) { return (n + ppo::kLossRows - 1) / ppo::kLossRows + ppo::kBuckets; }
 
+// The tensor-core objective (ppo::k_loss_tc) serves 32-feature tables of at most 368 candidates;
+// other shapes take the SIMT k_loss.
+bool tensor_core_objective(int feature_size, int action_count) {
+    return feature_size == ppo::kFeatures && action_count <= ppo::kTcCandidates && kOutPad == 64;
+}
+
 // Reorders every minibatch slice of the epoch permutation (s.perm) by feature table into
 // s.grouped and records each slice's table offsets in s.bucket_start.
 void group_minibatches(t8b_policy& s, const t8b_rollout_view_t& r, size_t samples, size_t minibatch, cudaStream_t st) {
@@ -556,11 +563,13 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
         }
         p->out.allocate(cap * kOutPad);
         p->dout.allocate(cap * kOutPad);
-        const size_t partial_rows = std::max((cap + ppo::kWarps - 1) / ppo::kWarps, loss_blocks(cap));
+        const size_t partial_rows = std::max({(cap + ppo::kWarps - 1) / ppo::kWarps, loss_blocks(cap), ppo::tc_tiles(cap)});
         p->out_colsum.allocate(partial_rows * kOutPad);
         check(cudaFuncSetAttribute(ppo::k_loss<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kMaxTableBytes),
               "objective shared memory");
         check(cudaFuncSetAttribute(ppo::k_loss<48>, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kMaxTableBytes),
+              "objective shared memory");
+        check(cudaFuncSetAttribute(ppo::k_loss_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kTcSmemBytes),
               "objective shared memory");
         check(cudaFuncSetAttribute(ppo::k_sample<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(ppo::sample_smem(32))), "sampler shared memory");
@@ -858,9 +867,15 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                 loss.perm = s.grouped.data();
                 loss.offset = offset;
                 loss.bucket_start = s.bucket_start.data() + (offset / mb) * (ppo::kBuckets + 1);
-                const unsigned loss_grid = static_cast<unsigned>(loss_blocks(n));
+                unsigned loss_grid = static_cast<unsigned>(loss_blocks(n));
                 const size_t table_bytes = static_cast<size_t>(s.config.action_count) * s.feature_size * sizeof(float);
-                if (s.feature_size == 48) {
+                if (tensor_core_objective(s.feature_size, s.config.action_count)) {
+                    // one row of partials per 128-row tile; persistent CTAs, one per SM
+                    loss_grid = static_cast<unsigned>(ppo::tc_tiles(n));
+                    const unsigned ctas = std::min(loss_grid, static_cast<unsigned>(sm_count()));
+                    launch("k_loss", ppo::k_loss_tc, ctas, ppo::kTcThreads, ppo::kTcSmemBytes, st, loss,
+                           static_cast<int>(loss_grid), s.error.data());
+                } else if (s.feature_size == 48) {
                     launch("k_loss", ppo::k_loss<48>, loss_grid, 32 * ppo::kWarps, table_bytes, st, loss);
                 } else {
                     launch("k_loss", ppo::k_loss<32>, loss_grid, 32 * ppo::kWarps, table_bytes, st, loss);

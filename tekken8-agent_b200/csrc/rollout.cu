@@ -359,7 +359,9 @@ __global__ void __launch_bounds__(32 * ppo::kWarps) k_logit_objective(
 }
 
 // The same objective with two samples per warp, one per half-warp (16 lanes, SLOTS logits per
-// lane: k <= 16 * SLOTS), for k <= 256. Reductions take four butterfly steps inside each half,
+// lane: k <= 16 * SLOTS), for k <= 128. (At k = 256 its 16 logits per lane took 128 registers,
+// two blocks per SM, and it measured 3.33 ms against the one-sample warp's 3.18 ms over
+// 4,194,304 samples, so k > 128 stays on k_logit_objective.) Reductions take four butterfly steps inside each half,
 // and the per-sample work (the scalars, the ratio, the value loss, the metrics) is issued once
 // for both samples, which matters because the kernel is bound by instruction issue. Each
 // half-warp strides over sample pairs like the warps of k_logit_objective, with the next pair
@@ -536,7 +538,7 @@ unsigned launch_objective(cudaStream_t st, unsigned grid, const float* outputs, 
     } while (0)
     if (k <= 64) T8B_OBJECTIVE(k_logit_objective_pair, 4);
     else if (k <= 128) T8B_OBJECTIVE(k_logit_objective_pair, 8);
-    else if (k <= 256) T8B_OBJECTIVE(k_logit_objective_pair, 16);
+    else if (k <= 256) T8B_OBJECTIVE(k_logit_objective, 8);
     else if (k <= 384) T8B_OBJECTIVE(k_logit_objective, 12);
     else T8B_OBJECTIVE(k_logit_objective, 16);
 #undef T8B_OBJECTIVE
