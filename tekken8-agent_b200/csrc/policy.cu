@@ -34,6 +34,12 @@ namespace t8b {
 using bf16 = __nv_bfloat16;
 constexpr int kOutPad = 64;  // output layer width on the tensor cores (query + value + zero padding)
 
+// The tensor-core scorer (ppo::k_loss_tc for the objective, ppo::k_sample_tc for the sampler)
+// serves 32-feature tables of at most 368 candidates; other shapes take the SIMT kernels.
+bool tensor_core_objective(int feature_size, int action_count) {
+    return feature_size == ppo::kFeatures && action_count <= ppo::kTcCandidates && kOutPad == 64;
+}
+
 struct Comm {
     t8b_comm_t hooks{};
     bool active() const { return hooks.allreduce_sum_f32 != nullptr && hooks.world_size > 1; }
@@ -125,6 +131,7 @@ struct t8b_policy {
     Buffer<int32_t> mb_actions, mb_tables;
     Buffer<float> mb_old_lp, mb_old_v, mb_adv, mb_ret;
     Buffer<double> block_metrics, metrics, norm_partial, norm_sq, entropy_sums;
+    Buffer<uint4> table_images;  // the tensor-core scorer's per-table shared-memory images
     Buffer<float> sample_entropy;
     Buffer<uint8_t> sample_decision;
     Buffer<int> error, invalid;
@@ -233,6 +240,14 @@ struct t8b_policy {
         // beyond that): at 32,768 samples over 42 groups, 7 parts (294 blocks) measured 12 %
         // faster than 13 parts of about 64 samples (546 blocks, 1.8 waves)
         const size_t groups = tables ? static_cast<size_t>(this->tables) + 1 : 1;
+        if (tensor_core_objective(feature_size, config.action_count)) {
+            // one wave of one CTA per SM: (groups x parts) CTAs
+            const int parts = std::max(1, static_cast<int>(static_cast<size_t>(sm_count()) / groups));
+            launch("k_sample", ppo::k_sample_tc, static_cast<unsigned>(groups * parts), ppo::kTcThreads, ppo::kTsSmemBytes, st,
+                   smp, static_cast<const uint4*>(table_images.data()), parts, error.data());
+            check(cudaGetLastError(), "sample actions");
+            return;
+        }
         const size_t wave = static_cast<size_t>(2 * sm_count()) / groups;
         smp.parts = static_cast<unsigned>(std::min<size_t>(std::max<size_t>({(n + groups * 256 - 1) / (groups * 256), wave, 1}), 4096));
         const unsigned sample_grid = static_cast<unsigned>(groups * smp.parts);
@@ -411,11 +426,6 @@ __global__ void k_decision_finish(const double* partial, int blocks, double* out
 // feature table; the runs of the kBuckets tables add at most one partial run each.
 size_t loss_blocks(size_t n) { return (n + ppo::kLossRows - 1) / ppo::kLossRows + ppo::kBuckets; }
 
-// The tensor-core objective (ppo::k_loss_tc) serves 32-feature tables of at most 368 candidates;
-// other shapes take the SIMT k_loss.
-bool tensor_core_objective(int feature_size, int action_count) {
-    return feature_size == ppo::kFeatures && action_count <= ppo::kTcCandidates && kOutPad == 64;
-}
 
 // Reorders every minibatch slice of the epoch permutation (s.perm) by feature table into
 // s.grouped and records each slice's table offsets in s.bucket_start.
@@ -571,6 +581,8 @@ int t8b_policy_create(size_t capacity, const t8b_actor_config_t* config, uint64_
               "objective shared memory");
         check(cudaFuncSetAttribute(ppo::k_loss_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kTcSmemBytes),
               "objective shared memory");
+        check(cudaFuncSetAttribute(ppo::k_sample_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kTsSmemBytes),
+              "sampler shared memory");
         check(cudaFuncSetAttribute(ppo::k_sample<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    static_cast<int>(ppo::sample_smem(32))), "sampler shared memory");
         check(cudaFuncSetAttribute(ppo::k_sample<48>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -653,6 +665,14 @@ int t8b_policy_set_action_feature_tables(t8b_policy* p, const float* features, i
         }
         if (s.features.size() != count) s.features.allocate(count);
         s.features.upload(features, count, static_cast<cudaStream_t>(stream));
+        if (tensor_core_objective(s.feature_size, s.config.action_count)) {
+            const size_t chunks = static_cast<size_t>(tables) * ppo::kTcImageChunks;
+            if (s.table_images.size() != chunks) s.table_images.allocate(chunks);
+            const dim3 grid((ppo::kTcCandidates * 8 + 32 * 96 + 255) / 256, static_cast<unsigned>(tables));
+            launch("k_table_images", ppo::k_table_images, grid, 256, 0, static_cast<cudaStream_t>(stream), s.features.data(),
+                   s.config.action_count, tables, s.table_images.data());
+            check(cudaGetLastError(), "feature table images");
+        }
         check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "upload features");
         s.tables = tables;
         s.features_ready = true;
@@ -874,7 +894,7 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
                     loss_grid = static_cast<unsigned>(ppo::tc_tiles(n));
                     const unsigned ctas = std::min(loss_grid, static_cast<unsigned>(sm_count()));
                     launch("k_loss", ppo::k_loss_tc, ctas, ppo::kTcThreads, ppo::kTcSmemBytes, st, loss,
-                           static_cast<int>(loss_grid), s.error.data());
+                           static_cast<const uint4*>(s.table_images.data()), static_cast<int>(loss_grid), s.error.data());
                 } else if (s.feature_size == 48) {
                     launch("k_loss", ppo::k_loss<48>, loss_grid, 32 * ppo::kWarps, table_bytes, st, loss);
                 } else {
