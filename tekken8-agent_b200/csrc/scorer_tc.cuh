@@ -35,14 +35,12 @@ constexpr int kTcChunks = 12 / kTcSlices;   // 32-column chunks per warp
 constexpr int kTcThreads = 128 * kTcSlices;
 constexpr int kTcTmemColumns = 512;   // scores / score gradients [0, 384), dq [384, 416)
 constexpr int kTcDq = 384;
-constexpr int kTcStage = 33;          // staged gradient row: 32 query columns + the value column
+constexpr int kTcStage = 33;          // gradient columns of a row: 32 query columns + the value column
 constexpr int kTcOffTlo = kTcTableBytes;
 constexpr int kTcOffTt = 2 * kTcTableBytes;
 constexpr int kTcOffQhi = kTcOffTt + kTcTransposeBytes;
 constexpr int kTcOffQlo = kTcOffQhi + kTcQBytes;
-constexpr int kTcOffStage = kTcOffQlo + kTcQBytes;
-constexpr int kTcOffMetric = kTcOffStage + kTcRows * kTcStage * 4;
-constexpr int kTcOffPart = kTcOffMetric + kTcRows * kMetrics * 4;
+constexpr int kTcOffPart = kTcOffQlo + kTcQBytes;
 constexpr int kTcOffSums = kTcOffPart + 4 * kTcSlices * kTcRows * 4;  // column and metric partials
 constexpr int kTcOffBar = kTcOffSums + 1024;
 constexpr int kTcSmemBytes = kTcOffBar + 64 + 1024;  // + alignment of the dynamic base to 1024
@@ -177,11 +175,9 @@ __device__ __forceinline__ void copy_image(uint32_t dst, const uint4* image, int
 __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* images, int tiles, int* error) {
     extern __shared__ __align__(1024) unsigned char tc_raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_raw) + 1023) & ~uintptr_t(1023));
-    float* stage = reinterpret_cast<float*>(base + kTcOffStage);       // [128][33]
-    float* row_metric = reinterpret_cast<float*>(base + kTcOffMetric);  // [128][8]
     float* part = reinterpret_cast<float*>(base + kTcOffPart);          // [4 quantities][slices][128 rows]
-    float* column_part = reinterpret_cast<float*>(base + kTcOffSums);   // [33][4]
-    double* metric_part = reinterpret_cast<double*>(base + kTcOffSums + 33 * 4 * 4 + 48);  // [8][4]
+    float* column_part = reinterpret_cast<float*>(base + kTcOffSums);   // [4 quarters][33]
+    double* metric_part = reinterpret_cast<double*>(base + kTcOffSums + 33 * 4 * 4 + 48);  // [4 quarters][8]
     uint64_t* bar = reinterpret_cast<uint64_t*>(base + kTcOffBar);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -304,8 +300,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
         const int sel_chunk = selected >> 5, sel_bit = selected & 31;
         float v[32];
 
-        // pass 1: the largest legal raw dot product of this slice
-        float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+        // pass 1 (online, per slice): the largest legal score m, sum of exp(s - m), sum of
+        // exp(s - m) (s - m), rescaled whenever a chunk raises m; and the chosen score
+        float m_slice = -INFINITY, s_slice = 0.0f, u_slice = 0.0f;
+        float chosen_slice = __int_as_float(0x7fc00000);
         if (!bad) {
             if (!tc::bar_wait(bar, phase, abort)) *abort = 1;
             tc::fence_after();
@@ -313,6 +311,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
             for (int c2 = 0; c2 < kTcChunks; ++c2) {
                 tc::tmem_load32(lanes + static_cast<uint32_t>((j0 + c2) * 32), v);
                 const uint32_t w = mine[c2];
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
                 for (int b = 0; b < 32; b += 4) {
                     mx0 = fmaxf(mx0, (w >> b) & 1u ? v[b] : -INFINITY);
@@ -320,52 +319,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
                     mx2 = fmaxf(mx2, (w >> (b + 2)) & 1u ? v[b + 2] : -INFINITY);
                     mx3 = fmaxf(mx3, (w >> (b + 3)) & 1u ? v[b + 3] : -INFINITY);
                 }
-            }
-            phase ^= 1u;
-        }
-        part[(0 * kTcSlices + slice) * kTcRows + r] = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-        __syncthreads();
-        float raw_max = part[r];
-#pragma unroll
-        for (int sl = 1; sl < kTcSlices; ++sl) raw_max = fmaxf(raw_max, part[sl * kTcRows + r]);
-        const float maximum = raw_max * scale;
-
-        // pass 2: sum of exp(s - max), sum of exp(s - max) (s - max), and the chosen score
-        const float k_exp = scale * kLog2e, m_exp = maximum * kLog2e;
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f, u0 = 0.0f, u1 = 0.0f, u2 = 0.0f, u3 = 0.0f;
-        float chosen_slice = __int_as_float(0x7fc00000);
-        if (!bad) {
-#pragma unroll
-            for (int c2 = 0; c2 < kTcChunks; ++c2) {
-                tc::tmem_load32(lanes + static_cast<uint32_t>((j0 + c2) * 32), v);
-                const uint32_t w = mine[c2];
+                const float chunk_max = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * scale;
+                if (chunk_max > m_slice) {
+                    if (s_slice > 0.0f) {
+                        const float f = ex2((m_slice - chunk_max) * kLog2e);
+                        u_slice = f * fmaf(m_slice - chunk_max, s_slice, u_slice);
+                        s_slice *= f;
+                    }
+                    m_slice = chunk_max;
+                }
+                const float k_exp = scale * kLog2e, m_exp = m_slice * kLog2e;
+                float s0 = 0.0f, s1 = 0.0f, u0 = 0.0f, u1 = 0.0f;
 #pragma unroll
                 for (int b = 0; b < 32; ++b) {
                     const bool legal = (w >> b) & 1u;
                     const float e = legal ? ex2(fmaf(v[b], k_exp, -m_exp)) : 0.0f;
-                    const float u = legal ? fmaf(v[b], scale, -maximum) : 0.0f;
-                    if ((b & 3) == 0) { s0 += e; u0 = fmaf(e, u, u0); }
-                    if ((b & 3) == 1) { s1 += e; u1 = fmaf(e, u, u1); }
-                    if ((b & 3) == 2) { s2 += e; u2 = fmaf(e, u, u2); }
-                    if ((b & 3) == 3) { s3 += e; u3 = fmaf(e, u, u3); }
+                    const float u = legal ? fmaf(v[b], scale, -m_slice) : 0.0f;
+                    if (b & 1) { s1 += e; u1 = fmaf(e, u, u1); } else { s0 += e; u0 = fmaf(e, u, u0); }
                 }
+                s_slice += s0 + s1;
+                u_slice += u0 + u1;
                 if (j0 + c2 == sel_chunk) {
 #pragma unroll
                     for (int b = 0; b < 32; ++b) chosen_slice = b == sel_bit ? v[b] * scale : chosen_slice;
                 }
                 __syncwarp();  // reconverge before the next warp-collective tensor-memory load
             }
+            phase ^= 1u;
         }
-        part[(1 * kTcSlices + slice) * kTcRows + r] = (s0 + s1) + (s2 + s3);
-        part[(2 * kTcSlices + slice) * kTcRows + r] = (u0 + u1) + (u2 + u3);
+        part[(0 * kTcSlices + slice) * kTcRows + r] = m_slice;
+        part[(1 * kTcSlices + slice) * kTcRows + r] = s_slice;
+        part[(2 * kTcSlices + slice) * kTcRows + r] = u_slice;
         part[(3 * kTcSlices + slice) * kTcRows + r] = chosen_slice;
         __syncthreads();
-        float exp_sum = part[(1 * kTcSlices) * kTcRows + r], weighted = part[(2 * kTcSlices) * kTcRows + r];
+        float maximum = part[r];
 #pragma unroll
-        for (int sl = 1; sl < kTcSlices; ++sl) {
-            exp_sum += part[(1 * kTcSlices + sl) * kTcRows + r];
-            weighted += part[(2 * kTcSlices + sl) * kTcRows + r];
+        for (int sl = 1; sl < kTcSlices; ++sl) maximum = fmaxf(maximum, part[sl * kTcRows + r]);
+        // the slices' sums moved to the common maximum, added in slice order
+        float exp_sum = 0.0f, weighted = 0.0f;
+#pragma unroll
+        for (int sl = 0; sl < kTcSlices; ++sl) {
+            const float m = part[sl * kTcRows + r], sm = part[(kTcSlices + sl) * kTcRows + r];
+            if (sm > 0.0f) {
+                const float f = ex2((m - maximum) * kLog2e);
+                exp_sum += f * sm;
+                weighted += f * fmaf(m - maximum, sm, part[(2 * kTcSlices + sl) * kTcRows + r]);
+            }
         }
+        const float k_exp = scale * kLog2e, m_exp = maximum * kLog2e;
         const int owner = sel_chunk / kTcChunks;
         const float chosen = bad || owner >= kTcSlices ? __int_as_float(0x7fc00000) : part[(3 * kTcSlices + owner) * kTcRows + r];
         const float sum = fmaxf(exp_sum, 1e-20f);
@@ -451,12 +452,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
 #pragma unroll
                 for (int f = 0; f < 32; ++f) v[f] = __int_as_float(0x7fc00000);
             }
-            float* st = stage + r * kTcStage;
-            float* mt = row_metric + r * kMetrics;
+            float mt[kMetrics] = {policy_loss, vloss, entropy, (ratio - 1.0f) - log_ratio,
+                                  fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f, 0.0f, count > 1 ? 1.0f : 0.0f,
+                                  count > 1 ? entropy : 0.0f};
+            float value_column = value_grad;
             if (valid) {
-#pragma unroll
-                for (int f = 0; f < 32; ++f) st[f] = v[f];
-                st[32] = value_grad;
                 uint32_t packed[32];
 #pragma unroll
                 for (int f = 0; f < 32; f += 2) {
@@ -472,14 +472,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
                 uint4* row_out = reinterpret_cast<uint4*>(p.dout + i * p.ld_grad);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) row_out[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-                mt[0] = policy_loss;
-                mt[1] = vloss;
-                mt[2] = entropy;
-                mt[3] = (ratio - 1.0f) - log_ratio;
-                mt[4] = fabsf(ratio - 1.0f) > p.clip ? 1.0f : 0.0f;
-                mt[5] = 0.0f;
-                mt[6] = count > 1 ? 1.0f : 0.0f;
-                mt[7] = count > 1 ? entropy : 0.0f;
                 if (p.sample_entropy) {
                     const size_t sample = p.perm[p.offset + i];
                     p.sample_entropy[sample] = entropy;
@@ -487,36 +479,37 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_loss_tc(Loss p, const uint4* 
                 }
             } else {
 #pragma unroll
-                for (int f = 0; f < kTcStage; ++f) st[f] = 0.0f;
+                for (int f = 0; f < 32; ++f) v[f] = 0.0f;
+                value_column = 0.0f;
 #pragma unroll
                 for (int m = 0; m < kMetrics; ++m) mt[m] = 0.0f;
+            }
+            // this quarter's 32 rows summed per column (fixed butterflies): the fp32 gradient
+            // columns (the output bias gradient) and the metrics in fp64
+            const float column = transpose_sum32(v, lane);
+            const float value_total = warp_sum(value_column);
+            column_part[quarter * kTcStage + lane] = column;
+            if (lane == 0) column_part[quarter * kTcStage + 32] = value_total;
+#pragma unroll
+            for (int m = 0; m < kMetrics; ++m) {
+                double x = static_cast<double>(mt[m]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+                if (lane == m) metric_part[quarter * kMetrics + m] = x;
             }
         }
         if (!bad) phase ^= 1u;  // every thread tracks the barrier's phase; only the slice-0 warps waited
         tc::fence_before();
         __syncthreads();
-        // per-tile partials in row order: four 32-row parts per column, then the parts in order
+        // per-tile partials: the four quarters in order
         const int t = threadIdx.x;
-        if (t < kTcStage * 4) {
-            const int c = t >> 2, q = t & 3;
-            float total = 0.0f;
-#pragma unroll 8
-            for (int row = q * 32; row < q * 32 + 32; ++row) total += stage[row * kTcStage + c];
-            column_part[c * 4 + q] = total;
-        } else if (t >= 256 && t < 256 + kMetrics * 4) {
-            const int m = (t - 256) >> 2, q = (t - 256) & 3;
-            double total = 0.0;
-#pragma unroll 8
-            for (int row = q * 32; row < q * 32 + 32; ++row) total += static_cast<double>(row_metric[row * kMetrics + m]);
-            metric_part[m * 4 + q] = total;
-        }
-        __syncthreads();
         if (t < p.ld_grad) {
-            colsum_out[t] = t < kTcStage ? (column_part[t * 4] + column_part[t * 4 + 1]) + (column_part[t * 4 + 2] + column_part[t * 4 + 3])
+            colsum_out[t] = t < kTcStage ? (column_part[t] + column_part[kTcStage + t]) +
+                                               (column_part[2 * kTcStage + t] + column_part[3 * kTcStage + t])
                                          : 0.0f;
         } else if (t >= 256 && t < 256 + kMetrics) {
             const int m = t - 256;
-            metric_out[m] = (metric_part[m * 4] + metric_part[m * 4 + 1]) + (metric_part[m * 4 + 2] + metric_part[m * 4 + 3]);
+            metric_out[m] = (metric_part[m] + metric_part[kMetrics + m]) + (metric_part[2 * kMetrics + m] + metric_part[3 * kMetrics + m]);
         }
         if (*abort) break;
     }
@@ -700,8 +693,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
             const float value = p.out[i * p.ld + 32];
             float v[32];
 
-            // pass 1: the largest legal score of this slice and its lowest candidate; the scores out
-            float best = -INFINITY;
+            // pass 1 (online, per slice): the largest legal score and its lowest candidate, the sums
+            // of exp(s - max) and exp(s - max) (s - max) rescaled whenever a chunk raises the
+            // maximum; the scores out when asked
+            float best = -INFINITY, s_slice = 0.0f, u_slice = 0.0f;
             int best_c = -1;
             if (!bad) {
                 if (!tc::bar_wait(bar, phase, abort)) *abort = 1;
@@ -713,6 +708,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
                 const int j = j0 + c2;
                 if (!bad) tc::tmem_load32(lanes + static_cast<uint32_t>(j * 32), v);
                 const uint32_t w = mine[c2];
+                const float previous = best;
 #pragma unroll
                 for (int b = 0; b < 32; ++b) {
                     const float sc = bad ? nan : v[b] * scale;
@@ -720,6 +716,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
                         best = sc;
                         best_c = j * 32 + b;
                     }
+                }
+                if (!bad) {
+                    if (best > previous && s_slice > 0.0f) {
+                        const float f = ex2((previous - best) * kLog2e);
+                        u_slice = f * fmaf(previous - best, s_slice, u_slice);
+                        s_slice *= f;
+                    }
+                    const float k_exp = scale * kLog2e, m_exp = best * kLog2e;
+                    float s0 = 0.0f, s1 = 0.0f, u0 = 0.0f, u1 = 0.0f;
+#pragma unroll
+                    for (int b = 0; b < 32; ++b) {
+                        const bool legal = (w >> b) & 1u;
+                        const float e = legal ? ex2(fmaf(v[b], k_exp, -m_exp)) : 0.0f;
+                        const float u = legal ? fmaf(v[b], scale, -best) : 0.0f;
+                        if (b & 1) { s1 += e; u1 = fmaf(e, u, u1); } else { s0 += e; u0 = fmaf(e, u, u0); }
+                    }
+                    s_slice += s0 + s1;
+                    u_slice += u0 + u1;
                 }
                 if (p.logits && valid) {
                     float* out = p.logits + i * p.action_count;
@@ -733,6 +747,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
             }
             at(0, slice, r) = best;
             at(1, slice, r) = __int_as_float(best_c);
+            at(2, slice, r) = s_slice;
+            at(3, slice, r) = u_slice;
             __syncthreads();
             float maximum = nan;
             int chosen = -1;
@@ -746,33 +762,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
                 }
             }
             if (chosen < 0) chosen = 0;
-
-            // pass 2: sum of exp(s - max) and of exp(s - max) (s - max)
             const float k_exp = scale * kLog2e, m_exp = maximum * kLog2e;
-            float s0 = 0.0f, s1 = 0.0f, u0 = 0.0f, u1 = 0.0f;
-            if (!bad) {
-#pragma unroll
-                for (int c2 = 0; c2 < kTcChunks; ++c2) {
-                    tc::tmem_load32(lanes + static_cast<uint32_t>((j0 + c2) * 32), v);
-                    const uint32_t w = mine[c2];
-#pragma unroll
-                    for (int b = 0; b < 32; ++b) {
-                        const bool legal = (w >> b) & 1u;
-                        const float e = legal ? ex2(fmaf(v[b], k_exp, -m_exp)) : 0.0f;
-                        const float u = legal ? fmaf(v[b], scale, -maximum) : 0.0f;
-                        if (b & 1) { s1 += e; u1 = fmaf(e, u, u1); } else { s0 += e; u0 = fmaf(e, u, u0); }
-                    }
-                }
-            }
-            at(2, slice, r) = s0 + s1;
-            at(3, slice, r) = u0 + u1;
-            __syncthreads();
+            // the slices' sums moved to the common maximum; prefix = the slices before this one
             float exp_sum = 0.0f, weighted = 0.0f, prefix = 0.0f;
 #pragma unroll
             for (int sl = 0; sl < kTcSlices; ++sl) {
-                if (sl < slice) prefix += at(2, sl, r);
-                exp_sum += at(2, sl, r);
-                weighted += at(3, sl, r);
+                const float sm = at(2, sl, r);
+                if (sm > 0.0f) {
+                    const float m = at(0, sl, r);
+                    const float f = ex2((m - maximum) * kLog2e);
+                    if (sl < slice) prefix += f * sm;
+                    exp_sum += f * sm;
+                    weighted += f * fmaf(m - maximum, sm, at(3, sl, r));
+                }
             }
             const float sum = fmaxf(exp_sum, 1e-20f);
             float score = maximum;  // the chosen candidate's score

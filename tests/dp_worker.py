@@ -1,6 +1,8 @@
 """Data-parallel worker, run as `torchrun --nproc-per-node 2 tests/dp_worker.py` (one rank per
 GPU, NCCL): the PPO update and the rollout statistics with the gradient, KL, observation
-normaliser and advantage moments summed over ranks.
+normaliser and advantage moments summed over ranks. With T8B_DP_BACKEND=gloo every rank runs on
+cuda:0 and the hooks' sums go through gloo (host copies), so the same checks run on a one-GPU
+machine; the library's own NCCL communicator needs a GPU per rank and is checked only with NCCL.
 
 Checks, printing "DP OK" on rank 0 when all hold:
   * identical shards on every rank give bit-identical parameters, Adam state, normaliser mean
@@ -26,17 +28,25 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 
+BACKEND = os.environ.get("T8B_DP_BACKEND", "nccl")
+
+
 def gather(array: np.ndarray) -> list[np.ndarray]:
-    t = torch.as_tensor(np.ascontiguousarray(array)).cuda()
+    t = torch.as_tensor(np.ascontiguousarray(array))
+    if BACKEND == "nccl":
+        t = t.cuda()
     out = [torch.empty_like(t) for _ in range(dist.get_world_size())]
     dist.all_gather(out, t)
     return [o.cpu().numpy() for o in out]
 
 
 def main():
-    local = int(os.environ["LOCAL_RANK"])
+    local = int(os.environ["LOCAL_RANK"]) if BACKEND == "nccl" else 0
     torch.cuda.set_device(local)
-    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    if BACKEND == "nccl":
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
+    else:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
     rank, world = dist.get_rank(), dist.get_world_size()
     from t8b import roster as roster_module
     from t8b.policy import GpuActorCritic, GpuRolloutBuffer, TorchComm, actor_config, ppo_config
@@ -99,20 +109,21 @@ def main():
 
     # the library's own NCCL communicator (t8b_comm_init) gives the same replicas as the
     # torch.distributed hooks: the same sums in the same order, queued from C
-    from t8b.policy import NativeComm
-    native = NativeComm()
-    twin = GpuActorCritic(n, seed=33)
-    twin.set_action_feature_tables(features)
-    twin.set_comm(native)
-    for update in range(3):
-        arrays = rollout_inputs(twin, features, n, np.random.default_rng(100 + 10 * rank + update))
-        view, keep = view_of(arrays)
-        twin.update_ppo(view, cfg, shuffle_seed=50 + update)
-    torch.cuda.synchronize()
-    native.status()
-    assert np.array_equal(twin.parameters(), policy.parameters()), "native communicator differs from torch's"
-    assert np.array_equal(twin.observation_statistics()[0], policy.observation_statistics()[0])
-    native.close()
+    if BACKEND == "nccl":
+        from t8b.policy import NativeComm
+        native = NativeComm()
+        twin = GpuActorCritic(n, seed=33)
+        twin.set_action_feature_tables(features)
+        twin.set_comm(native)
+        for update in range(3):
+            arrays = rollout_inputs(twin, features, n, np.random.default_rng(100 + 10 * rank + update))
+            view, keep = view_of(arrays)
+            twin.update_ppo(view, cfg, shuffle_seed=50 + update)
+        torch.cuda.synchronize()
+        native.status()
+        assert np.array_equal(twin.parameters(), policy.parameters()), "native communicator differs from torch's"
+        assert np.array_equal(twin.observation_statistics()[0], policy.observation_statistics()[0])
+        native.close()
     dist.barrier()
     if rank == 0:
         print("DP OK", flush=True)

@@ -1,5 +1,6 @@
 """Data parallelism: the t8b_comm_t hooks over torch.distributed, exercised on CPU with gloo
-ranks (world size 2, host buffers), and the NCCL path on two GPUs through tests/dp_worker.py."""
+ranks (world size 2, host buffers), and the update through tests/dp_worker.py: NCCL on two GPUs,
+or two gloo ranks sharing one GPU."""
 import os
 import socket
 import subprocess
@@ -105,6 +106,21 @@ def test_data_parallel_update_on_two_gpus():
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
+           str(ROOT / "tests" / "dp_worker.py")]
+    run = subprocess.run(cmd, capture_output=True, text=True, env=env, cwd=ROOT)
+    assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-3000:]
+    assert "DP OK" in run.stdout
+
+
+@pytest.mark.gpu
+def test_data_parallel_update_two_ranks_on_one_gpu():
+    """The data-parallel semantics of tests/dp_worker.py on a one-GPU machine: two ranks share
+    cuda:0 and the library's sum hooks go through gloo (no device-side waits between the ranks).
+    Identical shards equal the single-rank run bit for bit, the rank-merged advantage statistics
+    equal the single-rank ones, and different shards keep the replicas bit-identical."""
+    env = dict(os.environ, T8B_DP_BACKEND="gloo")
     cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node=2", "--master-addr=127.0.0.1", f"--master-port={free_port()}",
            str(ROOT / "tests" / "dp_worker.py")]
