@@ -33,6 +33,7 @@ constexpr int kTcTransposeBytes = 12 * 4096;  // 32 feature rows x 384 candidate
 constexpr int kTcSlices = 4;                // warps per lane quarter
 constexpr int kTcChunks = 12 / kTcSlices;   // 32-column chunks per warp
 constexpr int kTcThreads = 128 * kTcSlices;
+static_assert(kTcChunks == 3, "the sampler's rolled chunk loops pick among three mask words");
 constexpr int kTcTmemColumns = 512;   // scores / score gradients [0, 384), dq [384, 416)
 constexpr int kTcDq = 384;
 constexpr int kTcStage = 33;          // gradient columns of a row: 32 query columns + the value column
@@ -703,11 +704,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
                 tc::fence_after();
                 phase ^= 1u;
             }
-#pragma unroll
+            // the chunk loops stay rolled: a sampler CTA scores two or three tiles, and unrolled
+            // code mostly misses in the instruction cache
+#pragma unroll 1
             for (int c2 = 0; c2 < kTcChunks; ++c2) {
                 const int j = j0 + c2;
                 if (!bad) tc::tmem_load32(lanes + static_cast<uint32_t>(j * 32), v);
-                const uint32_t w = mine[c2];
+                const uint32_t w = c2 == 0 ? mine[0] : (c2 == 1 ? mine[1] : mine[2]);
                 const float previous = best;
 #pragma unroll
                 for (int b = 0; b < 32; ++b) {
@@ -785,10 +788,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_sample_tc(Sample p, const uin
                 float running = prefix;
                 int hit = -1;
                 float hit_score = 0.0f;
-#pragma unroll
+#pragma unroll 1
                 for (int c2 = 0; c2 < kTcChunks; ++c2) {
                     tc::tmem_load32(lanes + static_cast<uint32_t>((j0 + c2) * 32), v);
-                    const uint32_t w = mine[c2];
+                    const uint32_t w = c2 == 0 ? mine[0] : (c2 == 1 ? mine[1] : mine[2]);
 #pragma unroll
                     for (int b = 0; b < 32; ++b) {
                         const bool legal = (w >> b) & 1u;
