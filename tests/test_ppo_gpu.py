@@ -425,3 +425,51 @@ def test_gae_and_objective_full_config2_rollout(cuda):
     for index in (1, 2, 3, 7):
         assert abs(got[index] - want[index]) <= 1e-5 * abs(want[index]), (index, got[index], want[index])
     assert abs(got[4] - want[4]) <= margins and got[6] == want[6]
+
+
+def test_tensor_core_scorer_with_fewer_candidates(cuda, features):
+    """The tensor-core scorer (32 features) at 200 candidates instead of 368: the table image's
+    rows past the table are zero and the mask words past the candidates are empty. Forward logits
+    and argmax actions against float64, and one update's output-layer gradient rows and metrics
+    against the float64 objective on the GPU's own network outputs."""
+    import torch
+    from t8b.policy import GpuActorCritic, actor_config, ppo_config
+    k, n = 200, 4096
+    rng = np.random.default_rng(21)
+    table = np.ascontiguousarray(features[:, :k, :])
+    policy = GpuActorCritic(n, actor_config(action_count=k), seed=13)
+    policy.set_action_feature_tables(table)
+    shapes, p = oracle_params(policy)
+    p["w_out"] *= 30.0
+    policy.set_parameters(R.flatten(p, shapes).astype(np.float32))
+    obs, tables, _ = make_batch(n, table.shape[0], rng)
+    masks = (rng.random((n, k)) < 0.3).astype(np.uint8)
+    masks[:, 0] = 1
+    d = lambda a: torch.as_tensor(a, device="cuda")
+    out = policy.forward(d(obs), d(masks), n, seed=3, step=1, deterministic=True, tables=d(tables), want_logits=True)
+    got = policy.outputs(n).astype(np.float64)
+    logits = R.parametric_scores(got[:, :32], table.astype(np.float64), tables)
+    assert np.allclose(out["logits"].cpu().numpy(), logits, atol=1e-5, rtol=1e-4)
+    _, prob, legal = R.log_softmax_masked(logits, masks)
+    assert np.array_equal(out["actions"].cpu().numpy(), np.argmax(np.where(legal, logits, -np.inf), axis=1))
+    # one update on these samples
+    sampled = policy.forward(d(obs), d(masks), n, seed=1, step=0, tables=d(tables))
+    actions = sampled["actions"].cpu().numpy()
+    old_lp = sampled["log_probabilities"].cpu().numpy() - rng.normal(scale=0.05, size=n).astype(np.float32)
+    old_v = sampled["values"].cpu().numpy()
+    adv = rng.normal(size=n).astype(np.float32)
+    ret = (old_v + rng.normal(scale=0.5, size=n)).astype(np.float32)
+    view, keep = view_of((obs, tables, masks, actions, old_lp, old_v, adv, ret))
+    cfg = ppo_config(epochs=1, minibatch_size=n, learning_rate=1e-3, target_kl=0.0, entropy_coefficient=0.01)
+    metrics = policy.update_ppo(view, cfg, shuffle_seed=5)
+    order, _ = gathered_order(policy, obs, n)
+    dg = policy.activation(3, 0, n)[:, :33].astype(np.float64)
+    o = policy.outputs(n).astype(np.float64)
+    lg = R.parametric_scores(o[:, :32], table.astype(np.float64), tables[order])
+    g, dv, m = R.objective_gradient(lg, masks[order], actions[order], old_lp[order], old_v[order], adv[order],
+                                    ret[order], o[:, 32], 0.2, 0.2, 0.5, 0.01, n)
+    want_dout = np.concatenate([R.query_gradient(g, table.astype(np.float64), tables[order]), dv[:, None]], 1)
+    assert relative(dg, want_dout) < 1e-2
+    for key, name in (("policy_loss", "policy_loss"), ("value_loss", "value_loss"), ("entropy", "entropy"),
+                      ("approximate_kl", "kl"), ("decision_fraction", "decision")):
+        assert abs(metrics[key] - m[name].mean()) <= 1e-4 * max(1.0, abs(m[name].mean())), key
