@@ -17,11 +17,19 @@ size_t sim_group_count(const t8b_sim* sim, int group);
 void sim_step_group(t8b_sim* sim, int group, const int64_t* learner, const int64_t* opponent, uint64_t seed,
                     uint64_t counter, bool reset, cudaStream_t stream);
 
+// env_step over all fights (one group) on `stream` without the learner's masks, which
+// sim_learner_masks then computes on another stream (they depend only on the new states).
+void sim_step_without_masks(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed,
+                            uint64_t counter, bool reset, cudaStream_t stream);
+void sim_learner_masks(t8b_sim* sim, cudaStream_t stream);
+
 // The policy's forward on rows [row, row + n) of a batch (base pointers in; outputs in those rows
 // of the buffers `out` points at, with the same samples a whole-batch forward would draw).
+// With `masks_ready`, the sampler (the only part that reads the masks) waits for that event, so
+// the input preparation and the network's GEMMs run while the masks are still being computed.
 void policy_forward_rows(t8b_policy* policy, size_t row, size_t n, const float* observations, const uint32_t* mask_bits,
                          const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, cudaStream_t stream,
-                         t8b_policy_output_t* out);
+                         t8b_policy_output_t* out, cudaEvent_t masks_ready = nullptr);
 
 // record_policy_device / record_outcome_device for environments [row, row + n) of one step.
 void rollout_record_policy_rows(t8b_rollout* rollout, size_t step, size_t row, size_t n, const float* observations,

@@ -199,7 +199,7 @@ struct t8b_policy {
     // samples exactly as a whole one.
     void forward_rows(size_t row, size_t n, const float* obs, const uint8_t* masks, const uint32_t* mask_bits,
                       const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, bool want_logits,
-                      cudaStream_t st) {
+                      cudaStream_t st, cudaEvent_t masks_ready = nullptr) {
         if (!features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
         if (row + n > capacity) raise(T8B_EINVAL, "forward rows exceed the policy capacity");
         ppo::Prep prep{};
@@ -215,6 +215,7 @@ struct t8b_policy {
         launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
         check(cudaGetLastError(), "prepare inputs");
         network(n, st, row);
+        if (masks_ready != nullptr) check(cudaStreamWaitEvent(st, masks_ready, 0), "wait for the masks");
         ppo::Sample smp{};
         smp.out = out.data() + row * static_cast<size_t>(kOutPad);
         smp.ld = kOutPad;
@@ -685,9 +686,9 @@ namespace t8b::internal {
 
 void policy_forward_rows(t8b_policy* p, size_t row, size_t n, const float* observations, const uint32_t* mask_bits,
                          const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, cudaStream_t stream,
-                         t8b_policy_output_t* out) {
+                         t8b_policy_output_t* out, cudaEvent_t masks_ready) {
     if (observations == nullptr || mask_bits == nullptr || n == 0) raise(T8B_EINVAL, "policy input pointers cannot be null");
-    p->forward_rows(row, n, observations, nullptr, mask_bits, tables, seed, step, deterministic, false, stream);
+    p->forward_rows(row, n, observations, nullptr, mask_bits, tables, seed, step, deterministic, false, stream, masks_ready);
     out->logits = nullptr;
     out->actions = p->actions.data();
     out->log_probabilities = p->log_probs.data();

@@ -913,7 +913,7 @@ struct t8b_sim {
 
     // env_step over one group's fights on `st` (k_step, then the learner's masks of the group).
     void step_group(int g, const int64_t* learner, const int64_t* opponent, uint64_t seed, uint64_t counter, bool reset,
-                    cudaStream_t st) {
+                    cudaStream_t st, bool with_masks = true) {
         SimView v = view();
         v.side_order = side_order.data() + group_first[g];
         v.count = group_count[g];
@@ -923,6 +923,8 @@ struct t8b_sim {
         launch("k_step", k_step, grid.blocks, grid.threads, smem(), st, v, learner, opponent, seed, counter, tickets,
                group_p1[g], reset ? 1 : 0);
         launched("step");
+        opponent_bits_stale = true;
+        if (!with_masks) return;
         v.first = group_first[g];
         const unsigned warps_per_block = kMaskThreads / 32;
         launch("k_masks", k_masks, blocks(group_count[g], warps_per_block), kMaskThreads, smem(), st, v,
@@ -931,6 +933,8 @@ struct t8b_sim {
         opponent_bits_stale = true;
     }
     void launched(const char* what) const { check(cudaGetLastError(), what); }
+    // k_masks' grid over `items` (fight, side) items: one warp each
+    unsigned mask_grid(size_t items) const { return blocks(items, kMaskThreads / 32); }
 
     // The learner's masks after every state change; the opponent's are computed when asked for
     // (opponent_bits_stale), which a scripted-opponent trainer never does.
@@ -1267,6 +1271,17 @@ void sim_step_group(t8b_sim* sim, int group, const int64_t* learner, const int64
     if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
     if (group < 0 || group >= sim->groups()) raise(T8B_ERANGE, "fight group");
     sim->step_group(group, learner, opponent, seed, counter, reset, stream);
+}
+void sim_step_without_masks(t8b_sim* sim, const int64_t* learner, const int64_t* opponent, uint64_t seed,
+                            uint64_t counter, bool reset, cudaStream_t stream) {
+    if (learner == nullptr) raise(T8B_EINVAL, "learner candidates are required");
+    if (sim->groups() != 1) raise(T8B_ESTATE, "the fights are split into groups");
+    sim->step_group(0, learner, opponent, seed, counter, reset, stream, false);
+}
+void sim_learner_masks(t8b_sim* sim, cudaStream_t stream) {
+    launch("k_masks", k_masks, sim->mask_grid(sim->n), kMaskThreads, sim->smem(), stream, sim->view(),
+           static_cast<const uint8_t*>(nullptr), 1);
+    check(cudaGetLastError(), "candidate masks");
 }
 
 }  // namespace t8b::internal

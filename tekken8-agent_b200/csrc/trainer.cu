@@ -9,8 +9,10 @@
 // decision itself, the simulator step, and the reset of finished rounds. After the last
 // decision one deterministic forward (seed + 3) gives the final bootstrap. With a frozen
 // opponent policy its forward (seed + 2) runs on a second stream that overlaps the learner's.
-// Every decision but the last steps and resets in one call (t8b_sim_step_and_reset): nothing
-// reads the terminal observations there, while the last decision's bootstrap forward does.
+// Every decision but the last steps and resets in one launch (the reset of t8b_sim_step_and_reset):
+// nothing reads the terminal observations there, while the last decision's bootstrap forward
+// does. The learner's masks of those steps are computed on a second stream while the next
+// forward prepares its inputs and runs its GEMMs; its sampler waits for them.
 //
 //
 // With T8B_ROLLOUT_GROUPS=2 in the environment (scripted opponents, at least 8,192 fights) the
@@ -122,23 +124,31 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
             return;
         }
         internal::sim_set_groups(sim, 1);
-        cudaStream_t side = nullptr;
-        cudaEvent_t sim_ready = nullptr, opponent_done = nullptr;
+        cudaStream_t side = nullptr, mask_stream = nullptr;
+        cudaEvent_t sim_ready = nullptr, opponent_done = nullptr, stepped = nullptr, masks_ready = nullptr;
         struct Cleanup {
-            cudaStream_t* side;
-            cudaEvent_t* a;
-            cudaEvent_t* b;
+            cudaStream_t* streams[2];
+            cudaEvent_t* events[4];
             ~Cleanup() {
-                if (*a) cudaEventDestroy(*a);
-                if (*b) cudaEventDestroy(*b);
-                if (*side) cudaStreamDestroy(*side);
+                for (cudaEvent_t* e : events) {
+                    if (*e) cudaEventDestroy(*e);
+                }
+                for (cudaStream_t* s : streams) {
+                    if (*s) cudaStreamDestroy(*s);
+                }
             }
-        } cleanup{&side, &sim_ready, &opponent_done};
+        } cleanup{{&side, &mask_stream}, {&sim_ready, &opponent_done, &stepped, &masks_ready}};
         if (opponent) {
             check(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking), "opponent stream");
             check(cudaEventCreateWithFlags(&sim_ready, cudaEventDisableTiming), "event");
             check(cudaEventCreateWithFlags(&opponent_done, cudaEventDisableTiming), "event");
         }
+        // the learner's masks of a step run on their own stream beside the next forward's input
+        // preparation and GEMMs (only its sampler reads them)
+        check(cudaStreamCreateWithFlags(&mask_stream, cudaStreamNonBlocking), "mask stream");
+        check(cudaEventCreateWithFlags(&stepped, cudaEventDisableTiming), "event");
+        check(cudaEventCreateWithFlags(&masks_ready, cudaEventDisableTiming), "event");
+        bool masks_pending = false;
         const int32_t* tables = t8b_sim_learner_feature_tables(sim);
         t8b_policy_output_t out{}, last{}, theirs{};
         for (size_t step = 0; step < horizon; ++step) {
@@ -158,7 +168,9 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
                 check(cudaEventRecord(opponent_done, side), "event");
                 opponent_actions = theirs.actions;
             }
-            ok(t8b_policy_forward(policy, obs, nullptr, bits, n, seed + 1, counter, 0, stream, tables, 0, &out));
+            internal::policy_forward_rows(policy, 0, n, obs, bits, tables, seed + 1, counter, 0, main, &out,
+                                          masks_pending ? masks_ready : nullptr);
+            masks_pending = false;
             if (step > 0) {
                 ok(t8b_rollout_record_outcome_device(rollout, step - 1, t8b_sim_rewards(sim), t8b_sim_terminated(sim),
                                                      t8b_sim_truncated(sim), out.values, reward_scale, stream));
@@ -167,7 +179,12 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
                                                 out.values, stream, tables, out.entropies));
             if (opponent) check(cudaStreamWaitEvent(main, opponent_done, 0), "wait");
             if (step + 1 < horizon) {
-                ok(t8b_sim_step_and_reset(sim, out.actions, opponent_actions, seed, counter + 1));
+                internal::sim_step_without_masks(sim, out.actions, opponent_actions, seed, counter + 1, true, main);
+                check(cudaEventRecord(stepped, main), "event");
+                check(cudaStreamWaitEvent(mask_stream, stepped, 0), "wait");
+                internal::sim_learner_masks(sim, mask_stream);
+                check(cudaEventRecord(masks_ready, mask_stream), "event");
+                masks_pending = true;
                 continue;
             }
             ok(t8b_sim_step(sim, out.actions, opponent_actions, seed, counter + 1));
@@ -178,5 +195,6 @@ extern "C" int t8b_collect_rollout(t8b_sim* sim, t8b_policy* policy, t8b_rollout
             ok(t8b_sim_reset_done(sim, seed, counter + 1));
         }
         if (opponent) check(cudaStreamSynchronize(side), "opponent stream");
+        check(cudaStreamSynchronize(mask_stream), "mask stream");
     });
 }
