@@ -67,6 +67,40 @@ T8B_HD bool candidate_ok(const Match& m, const Fight& s, int p, int candidate) {
     return input_ok(m, s, p, in);
 }
 
+// candidate_ok for the universal candidates 0..21 of fighter p, as bit c of one word: the same
+// decisions (to_input's mapping, candidate 6's crouch requirement, input_ok's cases) taken once
+// for the fight instead of once per candidate, so the lanes of a warp that each check one
+// candidate of the same fight follow one path. `can` is can_act(m, s, p). Bits at or past the
+// fighter's candidate count are the caller's to clear.
+T8B_HD uint32_t universal_mask(const Match& m, const Fight& s, int p, bool can) {
+    uint32_t mask = 1u;  // candidate 0 is always legal
+    if (s.winner >= 0) return mask;
+    const Fighter& f = s.f[p];
+    const Cfg& c = *m.cfg;
+    const bool wake = f.posture == kGrounded && f.grounded_elapsed >= c.knockdown_frames;
+    const bool tech = f.posture == kGrounded && on(f, fTechable) && f.grounded_elapsed < c.tech_window_frames;
+    const bool escape = f.break_frames > 0 && !on(f, fBreakAttempted);
+    bool heat_dash = false;
+    if (f.move >= 0 && on(f, fHeat) && f.dash_from != kNoContactFrom) {
+        const DMove& mv = move_at(m, p, f.move);
+        heat_dash = f.dash_from == kBlocked ? has(mv, kHasHeatDashBlock) : has(mv, kHasHeatDashHit);
+    }
+#pragma unroll
+    for (int candidate = 1; candidate < kUniversalCount; ++candidate) {
+        const int u = universal_of_candidate(candidate);
+        bool legal;
+        if (u < 0) legal = false;
+        else if (candidate == 6) legal = f.posture == kCrouching && can;
+        else if (u == kWakeupStand || u == kWakeupRoll) legal = wake;
+        else if (u == kTechRoll) legal = tech;
+        else if (u == kThrowBreak || u == kThrowBreak1 || u == kThrowBreak2) legal = escape;
+        else if (u == kHeatDash) legal = heat_dash;
+        else legal = can;
+        mask |= (legal ? 1u : 0u) << candidate;
+    }
+    return mask;
+}
+
 // has_decision (full_move_contract.hpp:52-67)
 T8B_HD bool decides(const Match& m, const Fight& s, int p) {
     if (s.winner >= 0) return false;

@@ -363,6 +363,7 @@ __global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t
     const Fight& s = fights[warp];
     // move candidates: the gate record against the fighter's side of move_allowed, derived once
     const MoveContext context = move_context(m, s, player);
+    const uint32_t universal = universal_mask(m, s, player, context.can);
     const DGate* gates = m.side[player]->gates;
     uint32_t mine = 0;
     // unrolled so the twelve gate loads issue together (12 % faster than the rolled loop)
@@ -375,7 +376,7 @@ __global__ void __launch_bounds__(kMaskThreads) k_masks(SimView v, const uint8_t
             legal = g.move >= 0 && s.winner < 0 &&
                 context_allows(context, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
         } else if (c < count) {
-            legal = candidate_ok(m, s, player, c);
+            legal = (universal >> c) & 1u;  // c < kUniversalCount: word 0
         }
         const uint32_t bits = __ballot_sync(0xffffffffu, legal);
         if (lane == word) mine = bits;
@@ -475,12 +476,22 @@ __host__ __device__ inline uint64_t fight_hash(const Fight& s) {
 __device__ __forceinline__ Input random_legal_warp(const Match& m, const Fight& s, int p, Pcg32& rng, int lane) {
     const DCharacter& ch = *m.side[p];
     constexpr int kWords = (T8B_MAX_CANDIDATES + 31) / 32;
+    // candidate_ok per lane, with the fight's side of it derived once (as k_masks does)
+    const MoveContext context = move_context(m, s, p);
+    const uint32_t universal = universal_mask(m, s, p, context.can);
     uint32_t bits[kWords];
     int legal = 0;
 #pragma unroll
     for (int w = 0; w < kWords; ++w) {
         const int c = w * 32 + lane;
-        const bool ok = c < ch.candidate_count && candidate_ok(m, s, p, c);
+        bool ok = false;
+        if (c >= kUniversalCount && c < ch.candidate_count) {
+            const DGate g = ch.gates[c];
+            ok = g.move >= 0 && s.winner < 0 &&
+                context_allows(context, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
+        } else if (c < ch.candidate_count) {
+            ok = (universal >> c) & 1u;
+        }
         bits[w] = __ballot_sync(0xffffffffu, ok);
         legal += __popc(bits[w]);
     }
