@@ -101,6 +101,28 @@ T8B_HD uint32_t universal_mask(const Match& m, const Fight& s, int p, bool can) 
     return mask;
 }
 
+// candidate_ok for many candidates of one fighter in one state (a scripted opponent's choice):
+// can_act and the universal candidates' word are taken once.
+struct Legality {
+    const Match& m;
+    const Fight& s;
+    int p;
+    bool can;
+    uint32_t universal;
+    T8B_HD Legality(const Match& match, const Fight& state, int player)
+        : m(match), s(state), p(player), can(can_act(match, state, player)),
+          universal(universal_mask(match, state, player, can)) {}
+    T8B_HD bool operator()(int candidate) const {
+        if (candidate == 0) return true;
+        const DCharacter& ch = *m.side[p];
+        if (candidate < 0 || candidate >= ch.candidate_count) return false;
+        if (candidate < kUniversalCount) return ((universal >> candidate) & 1u) != 0u;
+        const DGate g = ch.gates[candidate];
+        if (g.move < 0 || s.winner >= 0) return false;
+        return move_allowed_given(m, s, p, can, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
+    }
+};
+
 // has_decision (full_move_contract.hpp:52-67)
 T8B_HD bool decides(const Match& m, const Fight& s, int p) {
     if (s.winner >= 0) return false;
@@ -151,27 +173,28 @@ T8B_HD double unit(uint64_t bits) { return static_cast<double>(bits >> 11) * (1.
 // scripted_candidate (full_move_contract.hpp:90-119): the legacy random opponent.
 T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggression, uint64_t prefix, uint64_t counter) {
     const DCharacter& ch = *m.side[p];
+    const Legality legal(m, s, p);
     const bool close = mag(s.f[p].x - s.f[1 - p].x) < 1.6;
     uint64_t draw_index = 0;
     const int roll = below(draw(prefix, counter * 64u + draw_index++), 100);
     if (!close && roll < 55) {
         const int approach = roll < 30 ? 3 : 1;
-        if (candidate_ok(m, s, p, approach)) return approach;
+        if (legal(approach)) return approach;
     }
     if (close && roll < 15) {
         const int guard = roll < 8 ? 0 : 5;
-        if (candidate_ok(m, s, p, guard)) return guard;
+        if (legal(guard)) return guard;
     }
     const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
     if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
         for (int k = 0; k < 24; ++k) {
             const int c = kUniversalCount + below_with(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount, ch.move_candidate_inverse);
-            if (candidate_ok(m, s, p, c)) return c;
+            if (legal(c)) return c;
         }
     }
     for (int k = 0; k < 24; ++k) {
         const int c = below(draw(prefix, counter * 64u + draw_index++), kUniversalCount);
-        if (candidate_ok(m, s, p, c)) return c;
+        if (legal(c)) return c;
     }
     return 0;
 }
@@ -194,7 +217,8 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     constexpr int cStepLeft = 8, cStepRight = 9, cBreak1 = 15, cBreak2 = 16, cBreak12 = 17;
     constexpr int cWakeStand = 19, cWakeRoll = 20, cTechRoll = 21;
     const DCharacter& ch = *m.side[p];
-    if (pr.fixed >= 0) return candidate_ok(m, s, p, pr.fixed) ? pr.fixed : cNeutral;
+    const Legality legal(m, s, p);
+    if (pr.fixed >= 0) return legal(pr.fixed) ? pr.fixed : cNeutral;
     const Fighter& own = s.f[p];
     const Fighter& other = s.f[1 - p];
     const double distance = mag(own.x - other.x);
@@ -214,14 +238,14 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
         if (rule == kBreakTwo) right = cBreak2;
         int choice = right;
         if (T8B_ATTACK_ROLL(1ull) >= pr.throw_break) choice = right == cBreak12 ? cBreak1 : (right == cBreak1 ? cBreak2 : cBreak12);
-        if (candidate_ok(m, s, p, choice)) return choice;
+        if (legal(choice)) return choice;
     }
     // getting up
     if (own.posture == kGrounded) {
         const int options[3] = {cWakeStand, cWakeRoll, cTechRoll};
         const int first = below(draw(prefix, counter * 64u + 63u), 3);
         for (int k = 0; k < 3; ++k) {
-            if (candidate_ok(m, s, p, options[(first + k) % 3])) return options[(first + k) % 3];
+            if (legal(options[(first + k) % 3])) return options[(first + k) % 3];
         }
     }
     // defense
@@ -237,19 +261,19 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
             const double answer = T8B_ATTACK_ROLL(2ull);
             if (!(hit.flags & kHoming) && until >= 12 && answer < pr.sidestep) {
                 const int side = T8B_ATTACK_ROLL(3ull) < 0.5 ? cStepLeft : cStepRight;
-                if (candidate_ok(m, s, p, side)) return side;
+                if (legal(side)) return side;
             }
             if (answer < pr.sidestep + pr.block) {
                 const bool crouch = hit.level == kLow || hit.level == kSpecialLow || hit.level == kThrow ||
                     (hit.level == kHigh && T8B_ATTACK_ROLL(4ull) < 0.5);
                 const int guard = crouch ? cCrouch : cNeutral;
-                if (candidate_ok(m, s, p, guard)) return guard;
+                if (legal(guard)) return guard;
             }
             break;
         }
     }
     // punish
-    if (other.move >= 0 && can_act(m, s, p)) {
+    if (other.move >= 0 && legal.can) {
         const DMove& mv = move_at(m, 1 - p, other.move);
         int last_active = 0;
         for (int k = 0; k < mv.hit_count; ++k) {
@@ -269,7 +293,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
                 const DFacts& fx = ch.facts[c];
                 if (!(fx.bits & 1u) || (fx.bits & 16u) || fx.startup > window || fx.reach + 0.1 < distance) continue;
                 const double score = fx.damage + ((fx.bits & 4u) ? 25.0 : 0.0);
-                if (score > best_score && candidate_ok(m, s, p, c)) {
+                if (score > best_score && legal(c)) {
                     best = c;
                     best_score = score;
                 }
@@ -278,25 +302,25 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
         }
     }
     // Heat and Rage
-    if (pr.heat_use > 0.0F && can_act(m, s, p)) {
+    if (pr.heat_use > 0.0F && legal.can) {
         const bool want_heat = on(own, fHeatAvailable) && !on(own, fHeat) && T8B_ROLL() < 0.02 * pr.heat_use;
         const bool want_rage = on(own, fRage) && distance < 1.3 && T8B_ROLL() < 0.05 * pr.heat_use;
         if (want_heat || want_rage) {
             for (int c = kUniversalCount; c < ch.candidate_count; ++c) {
                 const DFacts& fx = ch.facts[c];
                 const bool wanted = want_rage ? (fx.flags & kRequiresRage) != 0 : (fx.flags & kEngagesHeat) != 0;
-                if (wanted && candidate_ok(m, s, p, c)) return c;
+                if (wanted && legal(c)) return c;
             }
         }
     }
     // pressure
-    if (pr.pressure > 0.0F && on(other, fInBlockstun) && can_act(m, s, p) && T8B_ROLL() < pr.pressure) {
+    if (pr.pressure > 0.0F && on(other, fInBlockstun) && legal.can && T8B_ROLL() < pr.pressure) {
         for (int k = 0; k < 16; ++k) {
             const int c = kUniversalCount + below(draw(prefix, counter * 64u + 40u + static_cast<uint64_t>(k)), spread);
             if (c >= ch.candidate_count) continue;
             const DFacts& fx = ch.facts[c];
             if ((fx.bits & 1u) && !(fx.bits & 16u) && fx.startup <= 14 && fx.reach + 0.05 >= distance &&
-                candidate_ok(m, s, p, c)) {
+                legal(c)) {
                 return c;
             }
         }
@@ -318,7 +342,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     // offense and spacing
     const double reach = 1.25;
     if (pr.keepaway > 0.0F && distance > reach && distance < pr.distance + 0.6 && T8B_ROLL() < 0.025 * pr.aggression) {
-        if (candidate_ok(m, s, p, cDash)) return cDash;
+        if (legal(cDash)) return cDash;
     }
     const double attack_rate = 0.12 * pr.aggression * (pr.keepaway > 0.0F ? 3.0 : 1.0);
     if (distance <= reach + 0.25 && T8B_ROLL() < attack_rate) {
@@ -328,7 +352,7 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
             const int c = kUniversalCount + below(draw(prefix, counter * 64u + 8u + static_cast<uint64_t>(k)), spread);
             if (c >= ch.candidate_count) continue;
             const DFacts& fx = ch.facts[c];
-            if (!(fx.bits & 1u) || !candidate_ok(m, s, p, c)) continue;
+            if (!(fx.bits & 1u) || !legal(c)) continue;
             if (fx.reach + 0.05 < distance && T8B_ROLL() < 0.3 + 0.7 * pr.smart) continue;
             double score = T8B_ROLL() * 2.0;
             if (T8B_ROLL() < pr.smart) {
@@ -346,15 +370,15 @@ T8B_HD int bot_choice(const Match& m, const Fight& s, int p, const Profile& pr, 
     const double r = T8B_ROLL();
     if (distance > pr.distance + 0.2) {
         const int approach = pr.aggression > 0.7F && distance > 2.0 ? cDash : cWalkForward;
-        if (candidate_ok(m, s, p, approach)) return approach;
+        if (legal(approach)) return approach;
     }
     if (distance < pr.distance - 0.3 && pr.keepaway > 0.0F && r < 0.08 * pr.keepaway) {
         const int retreat = r < 0.03 * pr.keepaway ? cBackdash : cWalkBack;
-        if (candidate_ok(m, s, p, retreat)) return retreat;
+        if (legal(retreat)) return retreat;
     }
     if (r > 1.0 - 0.05 * pr.movement) {
         const int side = r > 1.0 - 0.025 * pr.movement ? cStepLeft : cStepRight;
-        if (candidate_ok(m, s, p, side)) return side;
+        if (legal(side)) return side;
     }
 #undef T8B_ROLL
 #undef T8B_ATTACK_ROLL

@@ -363,9 +363,12 @@ T8B_HD bool can_act(const Match& m, const Fight& s, int p) {
 }
 
 // The move branch of legal (full_combat_core.hpp:380-441) for a move with these flags,
-// required posture and stance, and heat cost; the round is still running.
-T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, uint8_t required_posture,
-                         int32_t required_stance, bool heat_cost) {
+// required posture and stance, and heat cost; the round is still running. `can()` gives
+// can_act(m, s, p) when the move needs it (move_allowed computes it there; a caller checking
+// many candidates of one state passes the value it took once).
+template <class Can>
+T8B_HD bool move_allowed_with(const Match& m, const Fight& s, int p, Can can, uint64_t flags, uint8_t required_posture,
+                              int32_t required_stance, bool heat_cost) {
     const Fighter& f = s.f[p];
     const Cfg& c = *m.cfg;
     const auto need = [flags](uint64_t bit) { return (flags & bit) != 0ull; };
@@ -375,7 +378,7 @@ T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, 
             f.break_frames == 0 && f.pending_throw_hit < 0 &&
             (f.universal == kSidestepLeft || f.universal == kSidestepRight);
         if (!stepping) return false;
-    } else if (!can_act(m, s, p)) {
+    } else if (!can()) {
         return false;
     }
     const Fighter& o = s.f[1 - p];
@@ -397,6 +400,16 @@ T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, 
         (!need(kRequiresHeat) || heat) && (!need(kConsumesHeat) || heat) && (!heat_cost || heat) &&
         (!need(kEngagesHeat) || (on(f, fHeatAvailable) && !heat)) &&
         (!(need(kRequiresRage) || need(kConsumesRage)) || on(f, fRage));
+}
+
+T8B_HD bool move_allowed(const Match& m, const Fight& s, int p, uint64_t flags, uint8_t required_posture,
+                         int32_t required_stance, bool heat_cost) {
+    return move_allowed_with(m, s, p, [&] { return can_act(m, s, p); }, flags, required_posture, required_stance,
+                             heat_cost);
+}
+T8B_HD bool move_allowed_given(const Match& m, const Fight& s, int p, bool can, uint64_t flags, uint8_t required_posture,
+                               int32_t required_stance, bool heat_cost) {
+    return move_allowed_with(m, s, p, [can] { return can; }, flags, required_posture, required_stance, heat_cost);
 }
 
 // What move_allowed derives from the fight rather than from the move, computed once for a

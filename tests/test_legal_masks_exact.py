@@ -1,9 +1,11 @@
-"""The legal-mask shortcut is exact (CPU, no GPU needed): universal_mask, which decides the 22
+"""The legality shortcuts are exact (CPU, no GPU needed): universal_mask, which decides the 22
 universal candidates of a fighter once per fight for the warp-parallel mask kernels (k_masks and
-the engine-parity random play), equals candidate_ok (candidate_legal, full_move_contract.hpp:42-49)
-candidate by candidate, on random fights that reach every branch: postures, stun, throw-break
-windows, heat and Heat Dash contacts, knock-down timers, moves and universals in progress, and
-finished rounds. The check compiles a host program from the library's own headers with nvcc."""
+the engine-parity random play), and Legality, which the scripted opponents use to check many
+candidates of one state (can_act and that word taken once), both equal candidate_ok
+(candidate_legal, full_move_contract.hpp:42-49) candidate by candidate, on random fights that
+reach every branch: postures, stun, throw-break windows, heat and Heat Dash contacts, knock-down
+timers, moves and universals in progress, finished rounds, and move gates with every requirement
+flag. The check compiles a host program from the library's own headers with nvcc."""
 import shutil
 import subprocess
 from pathlib import Path
@@ -32,9 +34,20 @@ int main() {
         moves[i].total_frames = 5 + static_cast<int>(next(40));
         moves[i].flags = (next(2) ? kHasHeatDashBlock : 0ull) | (next(2) ? kHasHeatDashHit : 0ull);
     }
+    std::vector<DGate> gates(40);
+    for (auto& g : gates) {
+        std::memset(&g, 0, sizeof g);
+        g.flags = next(1ull << 20) & next(1ull << 20);  // sparse requirement flags
+        g.required_stance = static_cast<int>(next(3)) - 1;
+        g.required_posture = static_cast<uint8_t>(next(2));
+        g.heat_cost = static_cast<uint8_t>(next(4) == 0);
+        g.move = static_cast<int16_t>(next(8) == 0 ? -1 : static_cast<int>(next(moves.size())));
+    }
+    cfg.back_to_wall_distance = 1.0; cfg.side_exposure_ratio = 0.3;
     DCharacter ch;
     std::memset(&ch, 0, sizeof ch);
     ch.moves = moves.data();
+    ch.gates = gates.data();
     ch.move_count = static_cast<int>(moves.size());
     ch.candidate_count = 40;
     const Match m{{&ch, &ch}, &cfg};
@@ -56,11 +69,20 @@ int main() {
             f.action_frame = static_cast<int>(next(50));
             f.grounded_elapsed = static_cast<int>(next(30));
             f.stance = static_cast<int>(next(3)) - 1;
+            f.x = static_cast<double>(next(1000)) / 100.0 - 5.0;
+            f.axis = static_cast<double>(next(1000)) / 100.0 - 5.0;
         }
+        s.left_wall = -6.0;
+        s.right_wall = 6.0;
         for (int p = 0; p < 2; ++p) {
             const uint32_t mask = universal_mask(m, s, p, can_act(m, s, p));
             for (int c = 0; c < kUniversalCount; ++c) {
                 bad += (((mask >> c) & 1u) != 0u) != candidate_ok(m, s, p, c);
+                ++checked;
+            }
+            const Legality legal(m, s, p);
+            for (int c = -1; c <= ch.candidate_count; ++c) {
+                bad += legal(c) != candidate_ok(m, s, p, c);
                 ++checked;
             }
         }
@@ -82,4 +104,4 @@ def test_universal_mask_equals_candidate_ok(tmp_path):
                    check=True, capture_output=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     checked, bad = (int(v) for v in out.stdout.split())
-    assert checked == 2_000_000 * 2 * 22 and bad == 0 and out.returncode == 0
+    assert checked == 2_000_000 * 2 * (22 + 42) and bad == 0 and out.returncode == 0
