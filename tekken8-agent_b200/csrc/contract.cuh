@@ -102,16 +102,25 @@ T8B_HD uint32_t universal_mask(const Match& m, const Fight& s, int p, bool can) 
 }
 
 // candidate_ok for many candidates of one fighter in one state (a scripted opponent's choice):
-// can_act and the universal candidates' word are taken once.
+// can_act and the universal candidates' word are taken once. `moves_possible` is false when no
+// move candidate can pass (the fighter can neither act nor continue a sidestep, or the round is
+// over), so a caller may skip probing them.
 struct Legality {
     const Match& m;
     const Fight& s;
     int p;
     bool can;
     uint32_t universal;
+    bool moves_possible;
     T8B_HD Legality(const Match& match, const Fight& state, int player)
         : m(match), s(state), p(player), can(can_act(match, state, player)),
-          universal(universal_mask(match, state, player, can)) {}
+          universal(universal_mask(match, state, player, can)), moves_possible(false) {
+        const Fighter& f = state.f[player];
+        const bool stepping = f.move < 0 && f.action_frame >= 1 && f.stun == 0 && !on(f, fCrumpled) &&
+            f.break_frames == 0 && f.pending_throw_hit < 0 &&
+            (f.universal == kSidestepLeft || f.universal == kSidestepRight);
+        moves_possible = state.winner < 0 && (can || stepping);
+    }
     T8B_HD bool operator()(int candidate) const {
         if (candidate == 0) return true;
         const DCharacter& ch = *m.side[p];
@@ -187,9 +196,13 @@ T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggress
     }
     const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
     if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
-        for (int k = 0; k < 24; ++k) {
-            const int c = kUniversalCount + below_with(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount, ch.move_candidate_inverse);
-            if (legal(c)) return c;
+        if (legal.moves_possible) {
+            for (int k = 0; k < 24; ++k) {
+                const int c = kUniversalCount + below_with(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount, ch.move_candidate_inverse);
+                if (legal(c)) return c;
+            }
+        } else {
+            draw_index += 24;  // every probe would fail: their draws are skipped, not their indices
         }
     }
     for (int k = 0; k < 24; ++k) {

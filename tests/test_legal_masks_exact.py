@@ -1,7 +1,8 @@
 """The legality shortcuts are exact (CPU, no GPU needed): universal_mask, which decides the 22
 universal candidates of a fighter once per fight for the warp-parallel mask kernels (k_masks and
 the engine-parity random play), and Legality, which the scripted opponents use to check many
-candidates of one state (can_act and that word taken once), both equal candidate_ok
+candidates of one state (can_act and that word taken once, and no move probed where none can
+pass), both equal candidate_ok
 (candidate_legal, full_move_contract.hpp:42-49) candidate by candidate, on random fights that
 reach every branch: postures, stun, throw-break windows, heat and Heat Dash contacts, knock-down
 timers, moves and universals in progress, finished rounds, and move gates with every requirement
@@ -83,6 +84,8 @@ int main() {
             const Legality legal(m, s, p);
             for (int c = -1; c <= ch.candidate_count; ++c) {
                 bad += legal(c) != candidate_ok(m, s, p, c);
+                // no move candidate passes where moves_possible says none can
+                bad += c >= kUniversalCount && !legal.moves_possible && candidate_ok(m, s, p, c);
                 ++checked;
             }
         }
