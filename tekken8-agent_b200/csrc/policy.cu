@@ -336,10 +336,16 @@ struct t8b_policy {
         check(cudaGetLastError(), "column sums");
     }
 
+    // The flag is set by any tensor-core kernel whose bounded wait ran out (the GEMMs, the
+    // scorer kernels of the forward and of the update) and stays set until a check reports it,
+    // so a forward's stall surfaces at the next update or synchronisation.
     void sync_error(cudaStream_t stream) {
         int flag = 0;
         error.download(&flag, 1, stream);
-        if (flag) raise(T8B_ECUDA, "a tensor-core GEMM stalled and was aborted");
+        if (flag) {
+            error.zero(stream);
+            raise(T8B_ECUDA, "a tensor-core kernel stalled and was aborted");
+        }
     }
 };
 
@@ -796,7 +802,6 @@ int t8b_policy_update_ppo(t8b_policy* p, const t8b_rollout_view_t* view, const t
         s.invalid.download(&invalid, 1, st);
         if (invalid) raise(T8B_ENONFINITE, "PPO rollout contains a non-finite value or invalid action");
         s.metrics.zero(st);
-        s.error.zero(st);
         if (s.sample_entropy.size() < samples) {
             s.sample_entropy.allocate(samples);
             s.sample_decision.allocate(samples);
@@ -1369,7 +1374,10 @@ int t8b_policy_debug_network(t8b_policy* p, const float* observations, size_t n,
 }
 
 int t8b_policy_synchronize(t8b_policy* p, void* stream) {
-    return with_policy(p, [&](t8b_policy&) { check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "synchronize policy"); });
+    return with_policy(p, [&](t8b_policy& s) {
+        check(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), "synchronize policy");
+        s.sync_error(static_cast<cudaStream_t>(stream));
+    });
 }
 
 }  // extern "C"
