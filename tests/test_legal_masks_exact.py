@@ -6,7 +6,10 @@ pass), both equal candidate_ok
 (candidate_legal, full_move_contract.hpp:42-49) candidate by candidate, on random fights that
 reach every branch: postures, stun, throw-break windows, heat and Heat Dash contacts, knock-down
 timers, moves and universals in progress, finished rounds, and move gates with every requirement
-flag. The check compiles a host program from the library's own headers with nvcc."""
+flag. The library's scripted random opponent (checking its probes through Legality and skipping
+the move probes that cannot pass) also picks the same candidate as probing them one by one
+with candidate_ok. The check compiles a host program from the library's own headers with
+nvcc."""
 import shutil
 import subprocess
 from pathlib import Path
@@ -22,6 +25,35 @@ PROGRAM = r"""
 #include <cstring>
 #include <vector>
 using namespace t8b;
+// scripted_candidate (full_move_contract.hpp:90-119) probing one candidate at a time with
+// candidate_ok: the form the library's random_opponent must agree with
+int random_opponent_one_by_one(const Match& m, const Fight& s, int p, double aggression, uint64_t prefix,
+                               uint64_t counter) {
+    const DCharacter& ch = *m.side[p];
+    const bool close = mag(s.f[p].x - s.f[1 - p].x) < 1.6;
+    uint64_t draw_index = 0;
+    const int roll = below(draw(prefix, counter * 64u + draw_index++), 100);
+    if (!close && roll < 55) {
+        const int approach = roll < 30 ? 3 : 1;
+        if (candidate_ok(m, s, p, approach)) return approach;
+    }
+    if (close && roll < 15) {
+        const int guard = roll < 8 ? 0 : 5;
+        if (candidate_ok(m, s, p, guard)) return guard;
+    }
+    const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
+    if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
+        for (int k = 0; k < 24; ++k) {
+            const int c = kUniversalCount + below(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount);
+            if (candidate_ok(m, s, p, c)) return c;
+        }
+    }
+    for (int k = 0; k < 24; ++k) {
+        const int c = below(draw(prefix, counter * 64u + draw_index++), kUniversalCount);
+        if (candidate_ok(m, s, p, c)) return c;
+    }
+    return 0;
+}
 int main() {
     uint64_t state = 0x9a3c5e7f11ull;
     const auto next = [&](uint64_t bound) { state = mix64(state); return state % bound; };
@@ -51,6 +83,7 @@ int main() {
     ch.gates = gates.data();
     ch.move_count = static_cast<int>(moves.size());
     ch.candidate_count = 40;
+    ch.move_candidate_inverse = 1.0 / (ch.candidate_count - kUniversalCount);
     const Match m{{&ch, &ch}, &cfg};
     unsigned long long checked = 0, bad = 0;
     for (int i = 0; i < 2000000; ++i) {
@@ -81,6 +114,11 @@ int main() {
                 bad += (((mask >> c) & 1u) != 0u) != candidate_ok(m, s, p, c);
                 ++checked;
             }
+            const double aggression = static_cast<double>(next(1000)) / 999.0;
+            const uint64_t prefix = mix64(state), counter = next(1u << 20);
+            bad += random_opponent(m, s, p, aggression, prefix, counter) !=
+                random_opponent_one_by_one(m, s, p, aggression, prefix, counter);
+            ++checked;
             const Legality legal(m, s, p);
             for (int c = -1; c <= ch.candidate_count; ++c) {
                 bad += legal(c) != candidate_ok(m, s, p, c);
@@ -107,4 +145,4 @@ def test_universal_mask_equals_candidate_ok(tmp_path):
                    check=True, capture_output=True)
     out = subprocess.run([str(exe)], capture_output=True, text=True)
     checked, bad = (int(v) for v in out.stdout.split())
-    assert checked == 2_000_000 * 2 * (22 + 42) and bad == 0 and out.returncode == 0
+    assert checked == 2_000_000 * 2 * (22 + 1 + 42) and bad == 0 and out.returncode == 0
