@@ -126,7 +126,16 @@ struct Legality {
         const DCharacter& ch = *m.side[p];
         if (candidate < 0 || candidate >= ch.candidate_count) return false;
         if (candidate < kUniversalCount) return ((universal >> candidate) & 1u) != 0u;
-        const DGate g = ch.gates[candidate];
+        return move_ok(candidate);
+    }
+    // The same for a candidate known to be universal (0 <= candidate < kUniversalCount) or a
+    // move (kUniversalCount <= candidate < the candidate count): each call site then carries only
+    // its branch of the check, which keeps the frame loop's code small.
+    T8B_HD bool universal_ok(int candidate) const {
+        return candidate == 0 || (candidate < m.side[p]->candidate_count && ((universal >> candidate) & 1u) != 0u);
+    }
+    T8B_HD bool move_ok(int candidate) const {
+        const DGate g = m.side[p]->gates[candidate];
         if (g.move < 0 || s.winner >= 0) return false;
         return move_allowed_given(m, s, p, can, g.flags, g.required_posture, g.required_stance, g.heat_cost != 0);
     }
@@ -188,18 +197,18 @@ T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggress
     const int roll = below(draw(prefix, counter * 64u + draw_index++), 100);
     if (!close && roll < 55) {
         const int approach = roll < 30 ? 3 : 1;
-        if (legal(approach)) return approach;
+        if (legal.universal_ok(approach)) return approach;
     }
     if (close && roll < 15) {
         const int guard = roll < 8 ? 0 : 5;
-        if (legal(guard)) return guard;
+        if (legal.universal_ok(guard)) return guard;
     }
     const int share = static_cast<int>((close ? 55.0 : 15.0) + 30.0 * aggression);
     if (ch.candidate_count > kUniversalCount && below(draw(prefix, counter * 64u + draw_index++), 100) < share) {
         if (legal.moves_possible) {
             for (int k = 0; k < 24; ++k) {
                 const int c = kUniversalCount + below_with(draw(prefix, counter * 64u + draw_index++), ch.candidate_count - kUniversalCount, ch.move_candidate_inverse);
-                if (legal(c)) return c;
+                if (legal.move_ok(c)) return c;
             }
         } else {
             draw_index += 24;  // every probe would fail: their draws are skipped, not their indices
@@ -207,7 +216,7 @@ T8B_HD int random_opponent(const Match& m, const Fight& s, int p, double aggress
     }
     for (int k = 0; k < 24; ++k) {
         const int c = below(draw(prefix, counter * 64u + draw_index++), kUniversalCount);
-        if (legal(c)) return c;
+        if (legal.universal_ok(c)) return c;
     }
     return 0;
 }
