@@ -185,6 +185,11 @@ GEMM_FLOPS_PER_SAMPLE = {
 #   input gradients: (dO 128 + h2 1,024 + dZ2 1,024 written) + (dZ2 1,024 + h1 1,024 + dZ1 1,024 written) = 5,248
 GEMM_BYTES_PER_SAMPLE = {"gemm_forward_hidden": 3456, "gemm_forward_output": 1280, "gemm_weight_grad": 4608,
                          "gemm_input_grad": 5248}
+# The rollout's fused forward (k_forward_tc: normalise, both hidden layers and the output layer
+# in one kernel, activations in shared memory): the three layers' FLOPs over the observation row
+# read (151 x 4) and the output row written (64 x 4); the weights come from L2.
+GEMM_FLOPS_PER_SAMPLE["k_forward_tc"] = GEMM_FLOPS_PER_SAMPLE["gemm_forward_hidden"] + GEMM_FLOPS_PER_SAMPLE["gemm_forward_output"]
+GEMM_BYTES_PER_SAMPLE["k_forward_tc"] = OBS * 4 + 64 * 4
 # GAE: read reward, value, next value (4 B each), terminated, truncated (1 B each); write
 # advantage and return (4 B each) = 22 B per sample.
 GAE_BYTES_PER_SAMPLE = 22
@@ -209,9 +214,11 @@ def kernel_table(args, profile, steps, peaks):
     n, t = args.envs, args.horizon
     rollout_samples = (t + 1) * n
     update_samples = args.epochs * t * n
-    samples = {"gemm_forward_hidden": rollout_samples + update_samples,
-               "gemm_forward_output": rollout_samples + update_samples,
-               "gemm_weight_grad": update_samples, "gemm_input_grad": update_samples}
+    # with the fused forward the layer GEMMs run in the update only
+    forward_gemm_samples = update_samples + (0 if "k_forward_tc" in profile else rollout_samples)
+    samples = {"gemm_forward_hidden": forward_gemm_samples, "gemm_forward_output": forward_gemm_samples,
+               "gemm_weight_grad": update_samples, "gemm_input_grad": update_samples,
+               "k_forward_tc": rollout_samples}
     total = sum(ms for _, ms in profile.values()) or 1.0
     rows = []
     for label, (launches, ms) in sorted(profile.items(), key=lambda kv: -kv[1][1]):

@@ -7,12 +7,14 @@
 // (w1, b1, ..., w_out, b_out). Every matrix product runs bf16 x bf16 -> fp32 on the tensor
 // cores; the Adam kernel refreshes the bf16 operand copies (row-major and transposed).
 //
-// Forward: k_prep (normalise, bf16) -> GEMM+tanh per hidden layer -> GEMM+bias (output) ->
+// Forward: k_forward_tc (normalise, bf16, both tanh layers and the output layer in one kernel,
+// for two hidden layers of 512; otherwise k_prep -> GEMM+tanh per hidden layer -> GEMM+bias) ->
 // k_sample (scores, masked softmax, sample). Update, per minibatch: k_prep gathers through the
 // shuffled permutation -> the same forward GEMMs -> k_loss (scores, clipped objective, entropy,
 // value loss, d/d(query, value)) -> backward GEMMs with the tanh derivative and bias column sums
 // in the epilogue -> weight-gradient GEMMs reading the row-major activations as MN-major
 // operands (samples as K, split-K) -> fixed-order reductions -> gradient norm -> Adam + casts.
+#include "forward_tc.cuh"
 #include "gemm_host.cuh"
 #include "ppo_kernels.cuh"
 #include "scorer_tc.cuh"
@@ -192,16 +194,40 @@ struct t8b_policy {
                   stream);
     }
 
-    // forward's work on rows [row, row + n) of a batch: the inputs are the batch's base pointers
-    // (observations [batch][width], packed masks [batch][12] or uint8 masks [batch][action_count],
-    // tables [batch]) and the outputs land in rows [row, row + n) of the inference buffers; the
-    // sampler's uniforms are keyed by the row in the batch, so a batch forwarded in row ranges
-    // samples exactly as a whole one.
-    void forward_rows(size_t row, size_t n, const float* obs, const uint8_t* masks, const uint32_t* mask_bits,
-                      const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, bool want_logits,
-                      cudaStream_t st, cudaEvent_t masks_ready = nullptr) {
-        if (!features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
-        if (row + n > capacity) raise(T8B_EINVAL, "forward rows exceed the policy capacity");
+    // The inference forward as one kernel (ppo::k_forward_tc): two hidden layers of 512, at most
+    // 512 padded inputs and 64 outputs; bit-identical to k_prep + network().
+    bool fused_forward() const {
+        return layers == 2 && hidden == ppo::kFwHidden && padded <= ppo::kFwHidden && outputs <= kOutPad;
+    }
+    void forward_fused(size_t row, size_t n, const float* obs, cudaStream_t st) {
+        const CUtensorMap m1 = make_map(w_bf[0].data(), padded, hidden, padded, 64, 256);
+        const CUtensorMap m2 = make_map(w_bf[1].data(), hidden, hidden, hidden, 64, 256);
+        const CUtensorMap mo = make_map(w_bf[2].data(), hidden, kOutPad, hidden, 64, 64);
+        ppo::Forward f{};
+        f.obs = obs + row * static_cast<size_t>(width);
+        f.width = width;
+        f.in_blocks = padded / 64;
+        f.mean = obs_mean.data();
+        f.istd = obs_istd.data();
+        f.clip = config.observation_clip;
+        f.normalize = normalizing() ? 1 : 0;
+        f.b1 = params.data() + b_off[0];
+        f.b2 = params.data() + b_off[1];
+        f.b_out = params.data() + b_off[2];
+        f.outputs = outputs;
+        f.out = out.data() + row * static_cast<size_t>(kOutPad);
+        f.n = static_cast<int>(n);
+        f.error = error.data();
+        check(cudaFuncSetAttribute(ppo::k_forward_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, ppo::kFwSmemBytes),
+              "forward smem");
+        const int tiles = static_cast<int>((n + ppo::kFwRows - 1) / ppo::kFwRows);
+        launch("k_forward_tc", ppo::k_forward_tc, std::min(tiles, sm_count()), ppo::kFwThreads, ppo::kFwSmemBytes, st, m1, m2,
+               mo, f);
+        check(cudaGetLastError(), "fused forward");
+    }
+
+    // k_prep then the layer GEMMs: the forward of the shapes the fused kernel does not serve.
+    void forward_network(size_t row, size_t n, const float* obs, cudaStream_t st) {
         ppo::Prep prep{};
         prep.obs = obs + row * static_cast<size_t>(width);
         prep.width = width;
@@ -215,6 +241,23 @@ struct t8b_policy {
         launch("k_prep", ppo::k_prep, blocks(n, ppo::kWarps), 32 * ppo::kWarps, 0, st, prep);
         check(cudaGetLastError(), "prepare inputs");
         network(n, st, row);
+    }
+
+    // forward's work on rows [row, row + n) of a batch: the inputs are the batch's base pointers
+    // (observations [batch][width], packed masks [batch][12] or uint8 masks [batch][action_count],
+    // tables [batch]) and the outputs land in rows [row, row + n) of the inference buffers; the
+    // sampler's uniforms are keyed by the row in the batch, so a batch forwarded in row ranges
+    // samples exactly as a whole one.
+    void forward_rows(size_t row, size_t n, const float* obs, const uint8_t* masks, const uint32_t* mask_bits,
+                      const int32_t* tables, uint64_t seed, uint64_t step, int deterministic, bool want_logits,
+                      cudaStream_t st, cudaEvent_t masks_ready = nullptr) {
+        if (!features_ready) raise(T8B_ESTATE, "parametric policy action features have not been installed");
+        if (row + n > capacity) raise(T8B_EINVAL, "forward rows exceed the policy capacity");
+        if (fused_forward()) {
+            forward_fused(row, n, obs, st);
+        } else {
+            forward_network(row, n, obs, st);
+        }
         if (masks_ready != nullptr) check(cudaStreamWaitEvent(st, masks_ready, 0), "wait for the masks");
         ppo::Sample smp{};
         smp.out = out.data() + row * static_cast<size_t>(kOutPad);

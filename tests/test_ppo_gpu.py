@@ -473,3 +473,42 @@ def test_tensor_core_scorer_with_fewer_candidates(cuda, features):
     for key, name in (("policy_loss", "policy_loss"), ("value_loss", "value_loss"), ("entropy", "entropy"),
                       ("approximate_kl", "kl"), ("decision_fraction", "decision")):
         assert abs(metrics[key] - m[name].mean()) <= 1e-4 * max(1.0, abs(m[name].mean())), key
+
+
+@pytest.mark.parametrize("n,observation_size,feature_size,normalize",
+                         [(1000, 151, 32, True), (32768, 151, 32, False), (300, 128, 48, True)])
+def test_fused_forward_matches_layer_gemms(cuda, features, n, observation_size, feature_size, normalize):
+    """The inference forward as one kernel (k_forward_tc: the normalised bf16 operand, both tanh
+    layers and the output layer, the activations kept in shared memory) gives network outputs
+    bit-identical to k_prep and the separate layer GEMMs (the path of the update and of
+    t8b_policy_debug_network): full-move and config-3 shapes, ragged batches (a partial last tile,
+    one or several tiles per CTA), with and without the observation normaliser."""
+    import ctypes as C
+    import torch
+    from t8b._lib import call
+    from t8b.policy import GpuActorCritic, actor_config
+    rng = np.random.default_rng(n + observation_size)
+    if feature_size == 32:
+        table, config = features, actor_config(observation_size=observation_size)
+    else:
+        table = rng.normal(size=(8, 256, feature_size)).astype(np.float32)
+        config = actor_config(observation_size=observation_size, action_count=256, action_feature_size=feature_size)
+    policy = GpuActorCritic(n, config, seed=9)
+    policy.set_action_feature_tables(table)
+    shapes, p = oracle_params(policy)
+    p = {key: value + rng.normal(scale=0.05, size=value.shape) for key, value in p.items()}  # non-zero biases
+    policy.set_parameters(R.flatten(p, shapes).astype(np.float32))
+    if normalize:
+        policy.set_observation_statistics(rng.normal(size=observation_size), rng.random(observation_size) + 0.1, 1000)
+    obs = torch.as_tensor(rng.normal(scale=2.0, size=(n, observation_size)).astype(np.float32), device="cuda")
+    tables = torch.as_tensor(rng.integers(0, table.shape[0], n).astype(np.int32), device="cuda")
+    masks = torch.as_tensor((rng.random((n, table.shape[1])) < 0.3).astype(np.uint8), device="cuda")
+    masks[:, 0] = 1
+    policy.forward(obs, masks, n, seed=1, step=0, tables=tables)
+    fused = policy.outputs(n)
+    layered = torch.empty((n, feature_size + 1), device="cuda")
+    call("t8b_policy_debug_network", policy._handle, C.c_void_p(obs.data_ptr()), n, None,
+         C.c_void_p(layered.data_ptr()), None)
+    torch.cuda.synchronize()
+    assert np.isfinite(fused).all() and np.abs(fused).max() > 0
+    assert np.array_equal(fused, layered.cpu().numpy())
