@@ -10,7 +10,8 @@
 //   warps 2-5 or 2-9  epilogue: tcgen05.ld of their 32 TMEM lanes (lane quarter = warp % 4), 32
 //              columns at a time (with 8 warps, the two of a quarter take alternate chunks), handed to the
 //              epilogue functor with a 6.5 KB warp-private shared-memory
-//              scratch (for staging a 32 x 32 chunk so global rows are read and written whole);
+//              scratch (for staging a 32 x 32 chunk so global rows are read whole, and so a bf16
+//              chunk leaves as one TMA store);
 //              the functor's prefetch of chunk c + 1 is issued before chunk c is loaded from
 //              tensor memory; then acc_empty[buffer] frees the buffer.
 // Two accumulator buffers of BN columns let the epilogue of tile i overlap the MMAs of tile i+1.
@@ -73,6 +74,23 @@ __device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, uint
         : "memory");
 }
 
+// Tiled TMA store of a shared-memory tile to the tensor map's box at (x, y) (rows and columns past
+// the tensor are not written), in this thread's bulk async-group.
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+                 "r"(smem_addr(src)), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// this thread's bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// all but the most recent of this thread's bulk stores have finished reading shared memory
+__device__ __forceinline__ void bulk_wait_read_all_but_one() {
+    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+// this thread's bulk stores are complete
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -122,10 +140,13 @@ struct EpiCtx {
     int row0;     // first of the warp's 32 rows
     int col0;     // first of the chunk's 32 columns
     int split, tm, quarter, lane;
-    unsigned char* scratch;  // warp-private, kEpiWarpBytes
+    unsigned char* scratch;  // warp-private, Epi::kScratchBytes
     int buffer;   // prefetch buffer (0 or 1) holding this chunk's inputs
     bool more;    // the next chunk's prefetch has been issued after this one's
+    int chunk;    // chunks this warp has handed to the functor before this one (all tiles)
 };
+// Shared-memory scratch per epilogue warp of the epilogues that stage chunks (a functor's
+// kScratchBytes; multiples of 512 keep every warp's staging tile aligned for the 64B swizzle).
 constexpr int kEpiWarpBytes = 6656;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool valid) {
@@ -154,12 +175,12 @@ struct Shape {
     int* error;         // set to 1 on a stalled wait
 };
 
-template <int BN, int EW>
+template <int BN, int EW, int SCRATCH>
 struct Layout {
     static constexpr int kABytes = BM * BK * 2;
     static constexpr int kBBytes = BN * BK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kEpiBytes = EW * kEpiWarpBytes;
+    static constexpr int kEpiBytes = EW * SCRATCH;
     // stages fill what the 227 KB of a CTA leaves after the epilogue scratch and barriers
     static constexpr int kStageBudget = 232448 - 1024 - 256 - kEpiBytes;
     static constexpr int kStages = kStageBudget / kStageBytes > 8 ? 8 : kStageBudget / kStageBytes;
@@ -169,12 +190,14 @@ struct Layout {
 
 template <int BN, bool A_MN, bool B_MN, class Epi>
 __global__ void __launch_bounds__(threads_for<Epi>(), 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape s, Epi epi) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Shape s,
+                const __grid_constant__ Epi epi) {
     constexpr int EW = Epi::kEpilogueWarps;
     static_assert(EW == 4 || EW == 8, "4 or 8 epilogue warps");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N");
     static_assert(!B_MN || BN % 64 == 0, "MN-major B tiles are whole 64-wide atoms");
-    using L = Layout<BN, EW>;
+    static_assert(Epi::kScratchBytes % 512 == 0, "warp scratch in 512-byte units");
+    using L = Layout<BN, EW, Epi::kScratchBytes>;
     extern __shared__ __align__(1024) unsigned char raw[];
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
     unsigned char* stages = base;
@@ -305,9 +328,10 @@ __global__ void __launch_bounds__(threads_for<Epi>(), 1)
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;  // which alternate 32-column chunks this warp takes (EW = 8)
         constexpr int stride = EW / 4;
-        unsigned char* scratch = epi_scratch + (warp - 2) * kEpiWarpBytes;
+        unsigned char* scratch = epi_scratch + (warp - 2) * Epi::kScratchBytes;
         int acc = 0;
         uint32_t acc_phase = 0;
+        int chunks = 0;
         float v[32];
         for (int work = blockIdx.x; work < total && !*abort; work += gridDim.x) {
             int tm, tn, kb0, kb1, split;
@@ -346,6 +370,7 @@ __global__ void __launch_bounds__(threads_for<Epi>(), 1)
                 }
                 x.col0 = tn * BN + c * 32;
                 x.buffer = n & 1;
+                x.chunk = chunks++;
                 epi(x, v);
             }
             fence_before();
@@ -355,6 +380,7 @@ __global__ void __launch_bounds__(threads_for<Epi>(), 1)
                 acc_phase ^= 1u;
             }
         }
+        bulk_wait();  // an epilogue's TMA stores (issued by lane 0) have landed
     }
     fence_before();
     __syncthreads();

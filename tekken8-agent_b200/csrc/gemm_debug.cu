@@ -8,6 +8,7 @@ namespace t8b {
 // Split-K partials: part[split][row][col] (fp32), rows < m, cols < n.
 struct EpiPartial {
     static constexpr int kEpilogueWarps = 4;
+    static constexpr int kScratchBytes = 0;
     __device__ void prefetch(const tc::EpiCtx&) const {}
     float* part;
     int m, n;

@@ -27,9 +27,10 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }
 
 // Row-major bf16 matrix [outer][inner] with `pitch` elements per row, viewed through boxes of
-// box_inner x box_outer elements with 128B swizzle (box_inner * 2 must be 128).
+// box_inner x box_outer elements with 128B swizzle (box_inner * 2 must be 128), or the 64B swizzle
+// of the epilogues' 32 x 32 store tiles.
 inline CUtensorMap make_map(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch, uint32_t box_inner,
-                            uint32_t box_outer) {
+                            uint32_t box_outer, CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (pitch * 2) % 16 != 0) {
         raise(T8B_EINVAL, "TMA operands need 16-byte aligned rows");
     }
@@ -40,10 +41,16 @@ inline CUtensorMap make_map(const void* base, uint64_t inner, uint64_t outer, ui
     const cuuint32_t element[2] = {1, 1};
     const CUresult r = tensor_map_encoder()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                                             strides, box, element, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) raise(T8B_ECUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(static_cast<int>(r)));
     return map;
+}
+
+// The [rows][ld] bf16 output of a tanh epilogue, written 32 x 32 at a time (ppo::store_rows_bf16).
+inline CUtensorMap make_store_map(void* base, int cols, int rows, int ld) {
+    return make_map(base, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), static_cast<uint64_t>(ld), 32, 32,
+                    CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 inline int sm_count() {
@@ -67,7 +74,7 @@ struct Operand {
 // C[m][n] = A . B^T over k, epilogue `epi`; `splits` partitions the k blocks (split-K).
 template <int BN, bool A_MN, bool B_MN, class Epi>
 void gemm(const char* label, const Operand& a, const Operand& b, int splits, int* error, Epi epi, cudaStream_t stream) {
-    using L = tc::Layout<BN, Epi::kEpilogueWarps>;
+    using L = tc::Layout<BN, Epi::kEpilogueWarps, Epi::kScratchBytes>;
     if (a.k != b.k || a.mn_major != A_MN || b.mn_major != B_MN) raise(T8B_EINVAL, "GEMM operand mismatch");
     tc::Shape s{};
     s.m = a.rows;

@@ -184,7 +184,9 @@ struct t8b_policy {
             bf16* below = l == 0 ? x0 : h[l - 1].data() + row * static_cast<size_t>(hidden);
             const Operand a = l == 0 ? Operand{below, m, padded, padded, false} : Operand{below, m, hidden, hidden, false};
             const Operand b{w_bf[l].data(), hidden, a.k, a.k, false};
-            const ppo::EpiTanh epi{params.data() + b_off[l], h[l].data() + row * static_cast<size_t>(hidden), hidden, m, hidden};
+            const ppo::EpiTanh epi{params.data() + b_off[l],
+                                   make_store_map(h[l].data() + row * static_cast<size_t>(hidden), hidden, m, hidden), hidden,
+                                   m, hidden};
             if (bn_hidden() == 256) dense<256>("gemm_forward_hidden", a, b, epi, stream); else dense<64>("gemm_forward_hidden", a, b, epi, stream);
         }
         const Operand a{h[layers - 1].data() + row * static_cast<size_t>(hidden), m, hidden, hidden, false};
@@ -328,7 +330,8 @@ struct t8b_policy {
         {
             const Operand a{dout.data(), m, kOutPad, kOutPad, false};
             const Operand b{wt_bf[layers].data(), hidden, kOutPad, kOutPad, false};
-            const ppo::EpiTanhGrad epi{h[layers - 1].data(), dz[layers - 1].data(), colsum[layers - 1].data(), hidden, m};
+            const ppo::EpiTanhGrad epi{h[layers - 1].data(), make_store_map(dz[layers - 1].data(), hidden, m, hidden),
+                                       colsum[layers - 1].data(), hidden, m};
             if (bn_hidden() == 256) dense<256>("gemm_input_grad", a, b, epi, stream); else dense<64>("gemm_input_grad", a, b, epi, stream);
         }
         for (int l = layers - 1; l >= 0; --l) {
@@ -361,7 +364,8 @@ struct t8b_policy {
                 // dZ_{l-1} = (dZ_l . W_l) * (1 - H_{l-1}^2)
                 const Operand da{dz[l].data(), m, hidden, hidden, false};
                 const Operand db{wt_bf[l].data(), hidden, hidden, hidden, false};
-                const ppo::EpiTanhGrad epi{h[l - 1].data(), dz[l - 1].data(), colsum[l - 1].data(), hidden, m};
+                const ppo::EpiTanhGrad epi{h[l - 1].data(), make_store_map(dz[l - 1].data(), hidden, m, hidden),
+                                           colsum[l - 1].data(), hidden, m};
                 if (bn_hidden() == 256) dense<256>("gemm_input_grad", da, db, epi, stream); else dense<64>("gemm_input_grad", da, db, epi, stream);
             }
         }

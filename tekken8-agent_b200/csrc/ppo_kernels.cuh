@@ -228,24 +228,35 @@ __global__ void __launch_bounds__(32 * kWarps) k_gather(Prep p) {
 }
 
 // ------------------------------------------------------------------ GEMM epilogues
-// Epilogue stores go through the warp's scratch: each lane writes its own row's 32 values,
-// then the warp writes 8 (bf16) or 4 (fp32) whole 64/128-byte row segments per instruction.
-__device__ __forceinline__ void store_rows_bf16(const tc::EpiCtx& x, const uint32_t* packed, __nv_bfloat16* out, int ld,
+// A bf16 chunk (the warp's 32 rows x 32 columns) is staged in one of two 2 KB tiles of the warp's
+// scratch (at 4096 and 6144, alternating chunk by chunk), each lane writing its row's 64 bytes
+// with the 16-byte pieces rotated as the 64-byte TMA swizzle lays them out (tc::staged_piece), and
+// leaves as one TMA store issued by lane 0 through `map` (a [rows][ld] bf16 tensor, 32 x 32
+// boxes, 64-byte swizzle; rows past the tensor are not written). A tile is restaged once the
+// store that last read it has finished reading. A warp whose rows all lie at or past row m (the
+// padding of the last row tile) stores nothing and lets its earlier stores finish reading first.
+constexpr int kTmaStoreScratch = 8704;  // prefetch 4096 + two staging tiles + 512
+__device__ __forceinline__ void store_rows_bf16(const tc::EpiCtx& x, const uint32_t* packed, const CUtensorMap* map,
                                                 int m) {
-    unsigned char* stage = x.scratch + 4096;
+    unsigned char* stage = x.scratch + 4096 + (x.chunk & 1) * 2048;
+    if (x.row0 >= m) {
+        if (x.lane == 0) tc::bulk_wait_read();
+        __syncwarp();
+        return;
+    }
+    if (x.lane == 0) tc::bulk_wait_read_all_but_one();
+    __syncwarp();
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         *reinterpret_cast<uint4*>(stage + tc::staged_piece(x.lane, q, 4)) =
             make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
     }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int r = i * 8 + (x.lane >> 2), q = x.lane & 3;
-        const uint4 piece = *reinterpret_cast<const uint4*>(stage + tc::staged_piece(r, q, 4));
-        if (x.row0 + r < m) *reinterpret_cast<uint4*>(out + static_cast<size_t>(x.row0 + r) * ld + x.col0 + q * 8) = piece;
+    if (x.lane == 0) {
+        tc::tma_store(map, stage, x.col0, x.row0);
+        tc::bulk_commit();
     }
-    __syncwarp();
 }
 
 // The chunk's 32 bias values, fetched asynchronously into the scratch at `at` (one 128 B
@@ -264,8 +275,9 @@ __device__ __forceinline__ void wait_prefetch(const tc::EpiCtx& x) {
 // Hidden layer forward: h = tanh(acc + b) as bf16 [rows][ld].
 struct EpiTanh {
     static constexpr int kEpilogueWarps = 8;
+    static constexpr int kScratchBytes = kTmaStoreScratch;
     const float* bias;
-    __nv_bfloat16* out;
+    CUtensorMap out;  // the bf16 [rows][ld] output (store_rows_bf16)
     int ld, m, cols;
     __device__ void prefetch(const tc::EpiCtx& x) const { prefetch_bias(x, bias, cols, 0); }
     __device__ void operator()(const tc::EpiCtx& x, const float* v) const {
@@ -280,13 +292,14 @@ struct EpiTanh {
             packed[2 * q] = *reinterpret_cast<uint32_t*>(&lo);
             packed[2 * q + 1] = *reinterpret_cast<uint32_t*>(&hi);
         }
-        store_rows_bf16(x, packed, out, ld, m);
+        store_rows_bf16(x, packed, &out, m);
     }
 };
 
 // Output layer: o = acc + b for the valid columns (zero beyond), fp32 [rows][ld].
 struct EpiBias {
     static constexpr int kEpilogueWarps = 8;
+    static constexpr int kScratchBytes = tc::kEpiWarpBytes;
     const float* bias;
     float* out;
     int ld, m, valid;
@@ -319,8 +332,9 @@ struct EpiBias {
 // with cp.async into one of two 2 KB buffers while the previous chunk is processed.
 struct EpiTanhGrad {
     static constexpr int kEpilogueWarps = 8;
+    static constexpr int kScratchBytes = kTmaStoreScratch;
     const __nv_bfloat16* h;
-    __nv_bfloat16* out;
+    CUtensorMap out;  // the bf16 [rows][ld] gradient (store_rows_bf16)
     float* colsum;
     int ld, m;
     __device__ void prefetch(const tc::EpiCtx& x) const {
@@ -356,7 +370,7 @@ struct EpiTanhGrad {
             __nv_bfloat162 pair = __floats2bfloat162_rn(g[2 * i], g[2 * i + 1]);
             packed[i] = *reinterpret_cast<uint32_t*>(&pair);
         }
-        store_rows_bf16(x, packed, out, ld, m);
+        store_rows_bf16(x, packed, &out, m);
         // Transpose-reduce across the warp: after 5 halving steps lane c holds column c's sum.
 #pragma unroll
         for (int width = 16; width >= 1; width >>= 1) {
@@ -375,6 +389,7 @@ struct EpiTanhGrad {
 // Split-K partial of a weight gradient: part[split][row][col] (fp32).
 struct EpiSplit {
     static constexpr int kEpilogueWarps = 4;
+    static constexpr int kScratchBytes = 0;
     __device__ void prefetch(const tc::EpiCtx&) const {}
     float* part;
     int m, n;
