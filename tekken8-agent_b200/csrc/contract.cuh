@@ -798,13 +798,32 @@ T8B_HD bool is_held(const Input& in) {
         (in.universal == kIdle || in.universal == kWalkForward || in.universal == kWalkBack || in.universal == kCrouch);
 }
 
+// How the frame loop's threads proceed: each on its own (the loop runs while this thread's
+// decision runs), or, in a block whose threads all call the loop, frame by frame together: a
+// block barrier at the top of every frame (until the block's last decision ends) and one between
+// the scripted opponent's choice and the engine step, a thread whose decision has ended only
+// passing the barriers. The warps of an SM then fetch the same code at about the same time,
+// which is what bounds the frame loop (instruction fetch). Barriers inside the engine step
+// measured slower.
+struct FreeFrames {
+    T8B_HD bool any(bool running) const { return running; }
+    T8B_HD void together() const {}
+};
+#ifdef __CUDACC__
+struct LockstepFrames {
+    __device__ __forceinline__ bool any(bool running) const { return __syncthreads_or(running ? 1 : 0) != 0; }
+    __device__ __forceinline__ void together() const { __syncthreads(); }
+};
+#endif
+
 // env_step (full_move_contract.hpp:1071-1154) for a learner on side L. `profiles` is the
 // 331-entry bot table; opponent_candidate < 0 means the scripted opponent plays. The side is a
-// template argument so that every fighter index in the frame loop is a constant.
-template <int L>
+// template argument so that every fighter index in the frame loop is a constant. With `live`
+// false the thread runs no frame (it only keeps the frame barriers of a lockstep block).
+template <int L, class Frames = FreeFrames>
 T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int opponent_candidate, double aggression,
                            const EnvCfg& ec, const Profile* profiles, uint64_t seed, uint64_t stream, uint64_t counter,
-                           const Noise* noise, Memory* memory = nullptr) {
+                           const Noise* noise, Memory* memory = nullptr, bool live = true, Frames frames = Frames{}) {
     constexpr int learner = L;
     StepOut r{0.0F, 0.0F, 0, 0, 0};
     int lag = 0;
@@ -829,12 +848,16 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
     Events e;
     int broken = 0;
     double distance_frames = 0.0;
-    for (int frame = 0; frame < ec.max_frames_per_decision; ++frame) {
+    bool running = live;
+    for (int frame = 0; frames.any(running && frame < ec.max_frames_per_decision); ++frame) {
+        const bool act = running && frame < ec.max_frames_per_decision;
         const bool landing = frame == lag;
         const bool holding = frame > lag && frame < lag + ec.hold_frames;
         const Input own = landing || (learner_held && holding) ? li : Input{-1, kIdle};
         Input other{-1, kIdle};
-        if (policy_opponent) {
+        if (!act) {
+            // past its decision: only the barriers
+        } else if (policy_opponent) {
             if (landing || (opponent_held && holding)) other = oi;
         } else if (decides(m, s, op)) {
             const uint64_t at = counter * 256u + static_cast<uint64_t>(frame);
@@ -842,6 +865,8 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
                                         : random_opponent(m, s, op, aggression, opponent_prefix, at);
             if (!to_input(*m.side[op], choice, other)) other = Input{-1, kIdle};
         }
+        frames.together();
+        if (!act) continue;
         frame_step(m, s, learner == 0 ? own : other, learner == 0 ? other : own, e);
         if (memory != nullptr) memory_update(m, s, e, ec.perception_delay, *memory);
         ++r.frames;
@@ -853,9 +878,12 @@ T8B_HD StepOut decision_as(const Match& m, Fight& s, int learner_candidate, int 
             const double oh = s.f[learner].health, th = s.f[op].health;
             s.winner = oh == th ? 2 : (oh > th ? learner : op);
         }
-        if (s.winner >= 0) break;
+        if (s.winner >= 0) {
+            running = false;
+            continue;
+        }
         const int minimum = ((learner_held || opponent_held) ? ec.hold_frames : 1) + lag;
-        if (frame + 1 >= minimum && (decides(m, s, learner) || (policy_opponent && decides(m, s, op)))) break;
+        if (frame + 1 >= minimum && (decides(m, s, learner) || (policy_opponent && decides(m, s, op)))) running = false;
     }
     const double dealt = opp_before - s.f[op].health;
     const double taken = own_before - s.f[learner].health;

@@ -194,11 +194,13 @@ __device__ __forceinline__ Fight reset_fight(const SimView& v, const Staged& st,
 // frame loop (every fighter index is a constant), then the outcome, tallies and observations.
 // With `reset`, a fight whose round ended is reset at once (reset_fight with the step's seed
 // and counter, as reset_done would do next) and only the new round's observations are written.
+// Every thread of the block calls it (the frame loop runs in lockstep); a thread with `live`
+// false (past its side's last fight) reads fight `env` but runs no frame and writes nothing.
 template <int L>
 __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const Staged& st, size_t env,
                                                          const int64_t* learner_candidates,
                                                          const int64_t* opponent_candidates, uint64_t seed,
-                                                         uint64_t counter, bool reset) {
+                                                         uint64_t counter, bool reset, bool live) {
     const int p1 = v.p1[env], p2 = v.p2[env];
     const Match m = match_of(st, p1, p2);
     Fight s = v.states[env];
@@ -210,9 +212,11 @@ __device__ __forceinline__ unsigned long long step_fight(const SimView& v, const
         memory = v.memories[env];
         remembered = &memory;
     }
-    const StepOut r = decision_as<L>(m, s, static_cast<int>(learner_candidates[env]),
-                                     opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1,
-                                     aggression, *st.ecfg, v.profiles, seed, env, counter, noise, remembered);
+    const StepOut r = decision_as<L, LockstepFrames>(
+        m, s, static_cast<int>(learner_candidates[env]),
+        opponent_candidates != nullptr ? static_cast<int>(opponent_candidates[env]) : -1, aggression, *st.ecfg,
+        v.profiles, seed, env, counter, noise, remembered, live);
+    if (!live) return 0;
     v.rewards[env] = r.reward;
     v.sparse[env] = r.sparse;
     v.terminated[env] = r.terminated ? 1 : 0;
@@ -268,12 +272,11 @@ __global__ void __launch_bounds__(kStepMaxWarps * 32, 1) k_step(SimView v, const
             continue;
         }
         const size_t in_side = first + threadIdx.x;
-        if (in_side < count) {
-            const size_t env = v.side_order[(side == 0 ? 0 : p1_fights) + in_side];
-            frames += side == 0
-                ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0)
-                : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0);
-        }
+        const bool live = in_side < count;
+        const size_t env = v.side_order[(side == 0 ? 0 : p1_fights) + (live ? in_side : first)];
+        frames += side == 0
+            ? step_fight<0>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0, live)
+            : step_fight<1>(v, st, env, learner_candidates, opponent_candidates, seed, counter, reset != 0, live);
     }
     add_frames(v, frames);
 }
