@@ -186,6 +186,34 @@ __global__ void k_record_outcome(float* rewards, uint8_t* terminated, uint8_t* t
     next_values[i] = nv[i];
 }
 
+// A decision's recording (record_policy_device, include/t8_v2/ppo.hpp:241-250) as one launch:
+// up to seven contiguous blocks copied (or zero-filled where the source is null), each moved in
+// 16-byte words when both ends and the size allow it, else in 4-byte words; threads stride over
+// the blocks' words in order.
+constexpr int kRecordBlocks = 7;
+struct RecordCopies {
+    const void* src[kRecordBlocks];
+    void* dst[kRecordBlocks];
+    size_t first[kRecordBlocks + 1];  // prefix of the blocks' word counts
+    int wide[kRecordBlocks];          // 16-byte words (else 4-byte)
+    int count;
+};
+__global__ void k_record(RecordCopies r) {
+    const size_t total = r.first[r.count];
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        int b = 0;
+        while (i >= r.first[b + 1]) ++b;
+        const size_t k = i - r.first[b];
+        if (r.wide[b]) {
+            const uint4 v = r.src[b] ? reinterpret_cast<const uint4*>(r.src[b])[k] : make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(r.dst[b])[k] = v;
+        } else {
+            reinterpret_cast<uint32_t*>(r.dst[b])[k] = r.src[b] ? reinterpret_cast<const uint32_t*>(r.src[b])[k] : 0u;
+        }
+    }
+}
+
 // uint8 masks [n][actions] -> 12 packed words per sample (candidates past `actions` are 0)
 __global__ void k_pack_masks(const uint8_t* bytes, int actions, uint32_t* bits, size_t n) {
     const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -764,29 +792,34 @@ int t8b_rollout_record_policy_device(t8b_rollout* r, size_t step, const float* o
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         const size_t at = step * s.envs;
         const size_t n = s.envs;
-        check(cudaMemcpyAsync(s.observations.data() + at * s.width, observations, sizeof(float) * n * s.width,
-                              cudaMemcpyDeviceToDevice, st), "record observations");
-        if (mask_bits) {
-            check(cudaMemcpyAsync(s.mask_bits.data() + at * 12, mask_bits, sizeof(uint32_t) * n * 12,
-                                  cudaMemcpyDeviceToDevice, st), "record masks");
-        } else {
+        if (!mask_bits) {
             launch("k_pack_masks", k_pack_masks, blocks(n * 12, 256), 256, 0, st, masks, s.action_count, s.mask_bits.data() + at * 12, n);
             check(cudaGetLastError(), "pack masks");
         }
+        RecordCopies r{};
+        size_t words = 0;
+        const auto add = [&](const void* src, void* dst, size_t bytes) {
+            const bool wide = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | bytes) & 15u) == 0;
+            r.src[r.count] = src;
+            r.dst[r.count] = dst;
+            r.wide[r.count] = wide ? 1 : 0;
+            r.first[r.count] = words;
+            words += bytes / (wide ? 16 : 4);
+            r.first[++r.count] = words;
+        };
+        add(observations, s.observations.data() + at * s.width, sizeof(float) * n * s.width);
+        if (mask_bits) add(mask_bits, s.mask_bits.data() + at * 12, sizeof(uint32_t) * n * 12);
+        add(actions, s.actions.data() + at, sizeof(int64_t) * n);
+        add(log_probabilities, s.log_probs.data() + at, sizeof(float) * n);
+        add(values, s.values.data() + at, sizeof(float) * n);
+        add(feature_tables, s.tables.data() + at, sizeof(int32_t) * n);  // null: zeros
+        if (entropies) add(entropies, s.entropies.data() + at, sizeof(float) * n);
+        const unsigned grid = static_cast<unsigned>(std::min<size_t>(blocks(words, 256), static_cast<size_t>(sm_count()) * 8));
+        launch("k_record", k_record, grid, 256, 0, st, r);
+        check(cudaGetLastError(), "record policy");
         s.bytes_current[step] = 0;
         s.mark_recorded(step, st);
-        check(cudaMemcpyAsync(s.actions.data() + at, actions, sizeof(int64_t) * n, cudaMemcpyDeviceToDevice, st), "actions");
-        check(cudaMemcpyAsync(s.log_probs.data() + at, log_probabilities, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "lp");
-        check(cudaMemcpyAsync(s.values.data() + at, values, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "values");
-        if (feature_tables) {
-            check(cudaMemcpyAsync(s.tables.data() + at, feature_tables, sizeof(int32_t) * n, cudaMemcpyDeviceToDevice, st), "tables");
-        } else {
-            check(cudaMemsetAsync(s.tables.data() + at, 0, sizeof(int32_t) * n, st), "tables");
-        }
         s.entropy_recorded[step] = entropies != nullptr;
-        if (entropies) {
-            check(cudaMemcpyAsync(s.entropies.data() + at, entropies, sizeof(float) * n, cudaMemcpyDeviceToDevice, st), "entropies");
-        }
     });
 }
 
