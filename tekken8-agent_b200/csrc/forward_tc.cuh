@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(kFwThreads, 1)
     uint64_t* empty = full + kFwStages;
     uint64_t* act_ready = empty + kFwStages;
     uint64_t* acc_full = act_ready + 1;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+    uint64_t* rows_staged = acc_full + 1;  // the epilogue warps' cp.async copies of a tile's rows have landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rows_staged + 1);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(kFwThreads, 1)
         }
         tc::bar_init(act_ready, 32 * kFwEpiWarps);
         tc::bar_init(acc_full, 1);
+        tc::bar_init(rows_staged, 32 * kFwEpiWarps);
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kFwThreads, 1)
         const int half = e >> 2;          // alternate 32-column chunks
         const int r = quarter * 32 + lane;  // this lane's row of the tile in the epilogues
         const int in_cols = p.in_blocks * 64;
-        uint32_t acc_phase = 0;
+        uint32_t acc_phase = 0, staged_phase = 0;
         const uint32_t t = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
         auto handoff = [&]() {
             tc::fence_before();
@@ -258,7 +260,14 @@ __global__ void __launch_bounds__(kFwThreads, 1)
                 for (int i = e * 32 + lane; i < total; i += 32 * kFwEpiWarps) tc::cp_async4(stage_rows + i, src + i, true);
                 tc::cp_async_commit();
                 tc::cp_async_wait<0>();
-                asm volatile("bar.sync 1, %0;" ::"n"(32 * kFwEpiWarps) : "memory");
+                // every epilogue thread's rows have landed (a bounded wait: a warp that left the
+                // loop after an abort cannot hold the others)
+                tc::bar_arrive(rows_staged);
+                if (!tc::bar_wait(rows_staged, staged_phase, abort)) {
+                    stop();
+                    break;
+                }
+                staged_phase ^= 1u;
 #pragma unroll 1
                 for (int rr = e; rr < kFwRows; rr += kFwEpiWarps) {
                     const float* row = stage_rows + rr * p.width;
