@@ -512,3 +512,38 @@ def test_fused_forward_matches_layer_gemms(cuda, features, n, observation_size, 
     torch.cuda.synchronize()
     assert np.isfinite(fused).all() and np.abs(fused).max() > 0
     assert np.array_equal(fused, layered.cpu().numpy())
+
+
+@pytest.mark.parametrize("n", [1000, 300])
+def test_network_backward_ragged_rows(cuda, features, n):
+    """The layer GEMMs' backward at batch sizes that leave a partial last row tile: the
+    tanh-gradient epilogue's TMA stores are clipped at the last row, and skipped for a warp whose
+    rows all lie past it. Weight and bias gradients of t8b_policy_debug_network (forward, then
+    backward from random output gradients) against float64, within north_star's 2e-2 per tensor
+    for bf16 GEMMs."""
+    import ctypes as C
+    import torch
+    from t8b._lib import call
+    from t8b.policy import GpuActorCritic
+    rng = np.random.default_rng(n)
+    policy = GpuActorCritic(n, seed=5)
+    policy.set_action_feature_tables(features)
+    shapes, p = oracle_params(policy)
+    p = {key: value + rng.normal(scale=0.05, size=value.shape) for key, value in p.items()}
+    flat = R.flatten(p, shapes).astype(np.float32)
+    policy.set_parameters(flat)
+    params = R.unflatten(flat.astype(np.float64), shapes)
+    obs = rng.normal(size=(n, 151)).astype(np.float32)
+    dout = rng.normal(size=(n, 33)).astype(np.float32)
+    tobs = torch.as_tensor(obs, device="cuda")
+    tdout = torch.as_tensor(dout, device="cuda")
+    call("t8b_policy_debug_network", policy._handle, C.c_void_p(tobs.data_ptr()), n, C.c_void_p(tdout.data_ptr()),
+         None, None)
+    torch.cuda.synchronize()
+    got = R.unflatten(policy.gradients().astype(np.float64), shapes)
+    x = obs.astype(np.float64)
+    hs, _ = R.forward(x, params, 2)
+    want = R.backward(x, hs, params, dout.astype(np.float64), 2)
+    errors = {name: relative(got[name], want[name]) for name, _ in shapes}
+    print(f"backward at {n} rows vs float64: {errors}")
+    assert all(e < 2e-2 for e in errors.values()), errors
