@@ -476,13 +476,14 @@ def test_tensor_core_scorer_with_fewer_candidates(cuda, features):
 
 
 @pytest.mark.parametrize("n,observation_size,feature_size,normalize",
-                         [(1000, 151, 32, True), (32768, 151, 32, False), (300, 128, 48, True)])
+                         [(1000, 151, 32, True), (32768, 151, 32, False), (300, 128, 48, True), (700, 300, 32, True)])
 def test_fused_forward_matches_layer_gemms(cuda, features, n, observation_size, feature_size, normalize):
     """The inference forward as one kernel (k_forward_tc: the normalised bf16 operand, both tanh
     layers and the output layer, the activations kept in shared memory) gives network outputs
     bit-identical to k_prep and the separate layer GEMMs (the path of the update and of
     t8b_policy_debug_network): full-move and config-3 shapes, ragged batches (a partial last tile,
-    one or several tiles per CTA), with and without the observation normaliser."""
+    one or several tiles per CTA), with and without the observation normaliser, and a 300-float
+    observation (a 320-column operand: the kernel loads the rows directly instead of staging them)."""
     import ctypes as C
     import torch
     from t8b._lib import call
